@@ -1,0 +1,526 @@
+"""Benchmark of the Qwen3 attention node on B200 (one JSON line on rank 0).
+
+Headline workload ("config 3"): Qwen3-30B-A3B-shape batched paged
+decode, one layer, Hq 32 / Hkv 4 / d 128, 64 sequences per GPU with contexts drawn
+U[1024, 32768], f16 KV in 32-token pages scattered by a seeded global permutation. One step is
+one decode step of the attention node for every sequence: append the new token (QK-RMSNorm,
+NEOX RoPE theta 1e6, f16 K/V write into its page) and paged attention over ctx + 1 keys.
+Metric: algorithmic HBM bytes of the step / step time (GB/s), whole job = sum over GPUs.
+Sequences are independent, so N GPUs run N independent 64-sequence batches (weak scaling, no
+collective on the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, PAGE = 32, 4, 128, 32
+N_SEQS = 64
+CTX_LO, CTX_HI = 1024, 32768
+SCALE = 1.0 / math.sqrt(D)
+SEED = 0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def draw_workload(seed):
+    """Context lengths and page placement of one 64-sequence batch (host side, seeded)."""
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, N_SEQS).astype(np.int64)
+    return rng, ctx
+
+
+def step_bytes(ctx):
+    """Algorithmic HBM bytes of one decode step: K+V of ctx+1 keys per sequence (read), Q (f32)
+    and O (f32), block-table entries, plus the append (q/k/v f32 in, q f32 out, K/V f16 out)."""
+    keys = ctx + 1
+    kv = int(np.sum(keys)) * HKV * D * 2 * 2
+    qo = N_SEQS * HQ * D * 4 * 2
+    tables = int(np.sum((keys + PAGE - 1) // PAGE)) * 4 + N_SEQS * 4
+    append = N_SEQS * ((HQ + 2 * HKV) * D * 4 + HQ * D * 4 + 2 * HKV * D * 2)
+    return kv + qo + tables + append, kv + qo + tables
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                bits = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv is not None:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------
+# B200 arm
+
+
+def build_device_workload(seed, dev):
+    import torch
+
+    import localstack_b200 as L
+    from localstack_b200.kv_cache import KvCache
+
+    rng, ctx = draw_workload(seed)
+    need = (ctx + 1 + PAGE - 1) // PAGE
+    n_pages = int(need.sum())
+    # Pages handed out through the bookkeeping allocator seeded with a permuted free list, as
+    # KvCache::alloc would scatter them (src/kv_cache.cpp:59-83).
+    kv = KvCache(n_pages * PAGE)
+    kv.set_free_blocks(rng.permutation(n_pages).astype(np.uint32))
+    for b in range(N_SEQS):
+        kv.alloc(b, int(ctx[b]))
+    cells = np.empty(N_SEQS, np.int64)
+    pos = np.empty(N_SEQS, np.int32)
+    for b in range(N_SEQS):
+        c, p = kv.alloc(b, 1)  # the decode step's new token
+        cells[b], pos[b] = c[0], p[0]
+    bt, lens = kv.block_tables(np.arange(N_SEQS))
+    g = torch.Generator(device=dev).manual_seed(seed)
+    kc = torch.randn((n_pages * PAGE, HKV, D), generator=g, device=dev, dtype=torch.float32)
+    kc = (kc * torch.rsqrt(kc.square().mean(-1, keepdim=True) + 1e-6)).half()
+    vc = torch.randn((n_pages * PAGE, HKV, D), generator=g, device=dev, dtype=torch.float32).half()
+    w = {
+        "ctx": ctx, "bt_host": bt, "lens_host": lens, "cells_host": cells, "pos_host": pos,
+        "kc": kc, "vc": vc,
+        "q_in": torch.randn((N_SEQS, HQ, D), generator=g, device=dev),
+        "k_in": torch.randn((N_SEQS, HKV, D), generator=g, device=dev),
+        "v_in": torch.randn((N_SEQS, HKV, D), generator=g, device=dev),
+        "gamma": torch.ones(D, device=dev),
+        "rope": L.rope_table(int(ctx.max()) + 2, dev),
+        "bt": torch.from_numpy(bt).to(dev), "lens": torch.from_numpy(lens).to(dev),
+        "cells": torch.from_numpy(cells).to(dev), "pos": torch.from_numpy(pos).to(dev),
+        "max_len": int(lens.max()),
+    }
+    w["q_out"] = torch.empty((N_SEQS, HQ, D), device=dev)
+    w["out"] = torch.empty((N_SEQS, HQ, D), device=dev)
+    w["ws"] = L.DecodeWorkspace(N_SEQS, HQ, HKV, dev)
+    return w
+
+
+def decode_step(L, w, q_in=None, k_in=None, v_in=None, pos=None, cells=None, bt=None, lens=None, out=None):
+    """One attention-node decode step through the C ABI: append, then paged attention."""
+    L.kv_append(w["kc"], w["vc"], q_in if q_in is not None else w["q_in"], k_in if k_in is not None else w["k_in"],
+                v_in if v_in is not None else w["v_in"], pos if pos is not None else w["pos"],
+                cells if cells is not None else w["cells"], w["rope"], w["gamma"], w["gamma"], 1e-6,
+                q_out=w["q_out"])
+    L.attn_decode(w["kc"], w["vc"], w["q_out"], bt if bt is not None else w["bt"],
+                  lens if lens is not None else w["lens"], SCALE, max_seq_len=w["max_len"],
+                  out=out if out is not None else w["out"], workspace=w["ws"])
+
+
+def cpu_baseline_sample(w, budget_s=12.0):
+    """The oracle's page-table decode (ggml CPU precision model, all host threads) on the first
+    sequences of the same batch, sized to roughly `budget_s` of CPU work."""
+    import torch
+
+    from oracle import oracle as O
+
+    threads = O.hardware_threads()
+    bt = w["bt_host"]
+    lens = w["lens_host"]
+    q = w["q_out"].cpu().numpy()
+    # calibrate on one sequence, then take as many as fit the budget
+    sel = [0]
+    kc_all = w["kc"]
+    vc_all = w["vc"]
+
+    def run(idx):
+        pages = np.unique(bt[idx][:, :].ravel())
+        # gather only the sampled sequences' pages to the host, remapping page ids
+        remap = {int(p): i for i, p in enumerate(pages)}
+        pg = torch.from_numpy(pages.astype(np.int64)).to(kc_all.device)
+        kc = kc_all.view(-1, PAGE, HKV, D).index_select(0, pg).reshape(-1, HKV, D).cpu().view(torch.int16).numpy()
+        vc = vc_all.view(-1, PAGE, HKV, D).index_select(0, pg).reshape(-1, HKV, D).cpu().view(torch.int16).numpy()
+        sbt = np.vectorize(lambda p: remap[int(p)])(bt[idx]).astype(np.int32)
+        t0 = time.perf_counter()
+        O.paged_decode_ggml_fast(q[idx], kc.view(np.uint16), vc.view(np.uint16), sbt, lens[idx], SCALE,
+                                 n_threads=threads)
+        return time.perf_counter() - t0
+
+    t1 = run(np.array(sel))
+    per_tok = t1 / float(lens[0])
+    n = 1
+    while n < N_SEQS and per_tok * float(lens[:n + 1].sum()) < budget_s:
+        n += 1
+    idx = np.arange(n)
+    dt = run(idx)
+    kv_bytes = float(np.sum(lens[idx].astype(np.int64))) * HKV * D * 2 * 2
+    return {"value": kv_bytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} of the 64 config-3 sequences ({int(lens[idx].sum())} keys), one decode step, "
+                      f"{dt:.2f} s, K/V bytes only"}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import localstack_b200 as L
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    w = build_device_workload(SEED + rank, dev)
+    total_bytes, read_bytes = step_bytes(w["ctx"])
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        decode_step(L, w)
+    L.check_status()
+
+    # timed region: per-step decode-kernel events ride along on the same stream
+    ev_dec = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for i in range(args.steps):
+            L.kv_append(w["kc"], w["vc"], w["q_in"], w["k_in"], w["v_in"], w["pos"], w["cells"], w["rope"],
+                        w["gamma"], w["gamma"], 1e-6, q_out=w["q_out"])
+            ev_dec[i][0].record(stream)
+            L.attn_decode(w["kc"], w["vc"], w["q_out"], w["bt"], w["lens"], SCALE, max_seq_len=w["max_len"],
+                          out=w["out"], workspace=w["ws"])
+            ev_dec[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    L.check_status()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    dec_ms = sum(a.elapsed_time(b) for a, b in ev_dec) / args.steps
+    t = torch.tensor([ms, dec_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, dec_ms_max = float(t[0]), float(t[1])
+
+    # e2e: the same step through the C ABI with pinned HOST buffers, copies inside the timing
+    pin = lambda x: x.cpu().pin_memory()
+    h_q, h_k, h_v = pin(w["q_in"]), pin(w["k_in"]), pin(w["v_in"])
+    h_pos, h_cells, h_bt, h_lens = pin(w["pos"]), pin(w["cells"]), pin(w["bt"]), pin(w["lens"])
+    h_out = torch.empty_like(w["out"], device="cpu").pin_memory()
+    d_q, d_k, d_v = torch.empty_like(w["q_in"]), torch.empty_like(w["k_in"]), torch.empty_like(w["v_in"])
+    d_pos, d_cells = torch.empty_like(w["pos"]), torch.empty_like(w["cells"])
+    d_bt, d_lens = torch.empty_like(w["bt"]), torch.empty_like(w["lens"])
+    h2d = sum(x.numel() * x.element_size() for x in (h_q, h_k, h_v, h_pos, h_cells, h_bt, h_lens))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        for d, h in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_pos, h_pos), (d_cells, h_cells), (d_bt, h_bt),
+                     (d_lens, h_lens)):
+            d.copy_(h, non_blocking=True)
+        decode_step(L, w, d_q, d_k, d_v, d_pos, d_cells, d_bt, d_lens)
+        h_out.copy_(w["out"], non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 4)):
+        e2e_step()
+    n_e2e = max(10, args.steps // 4)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t[0])
+
+    hbm_peak, tc_peak, peak_src = peaks()
+    achieved = read_bytes / (dec_ms / 1e3) / 1e9  # decode kernel alone, this rank
+    line = None
+    if rank == 0:
+        line = {
+            "metric": "paged decode-attn HBM GB/s (config 3, Qwen3-30B-A3B GQA 32/4, 64 seqs/GPU)",
+            "value": round(total_bytes * world / (ms_max / 1e3) / 1e9, 1),
+            "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
+            "data": "synthetic (seeded; ctx U[1024,32768]; K RMS-normed N(0,1), V N(0,1))",
+            "config": {"workload": "config 3: batched paged decode step (kv_append + split-K decode)",
+                       "n_seqs_per_gpu": N_SEQS, "n_head": HQ, "n_head_kv": HKV, "head_dim": D, "page": PAGE,
+                       "mean_ctx": float(w["ctx"].mean()), "parallelism": f"dp{world} (sequence sharding)",
+                       "l2": "KV inputs 2.2 GB per GPU > 126 MB L2, no flush"},
+            "tokens_per_s": round(N_SEQS * world / (ms_max / 1e3), 1),
+            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel + decode_combine_kernel",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} hbm_gbs",
+                         "algorithmic_bytes_per_launch": read_bytes, "launch_ms": round(dec_ms, 4),
+                         "traffic": None},
+            "e2e": {"value": round(total_bytes * world / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline_sample(w)
+        if not args.no_secondary:
+            line["secondary"] = secondary(L, dev, tc_peak, hbm_peak)
+    barrier()
+    if world > 1:
+        dist.destroy_process_group()
+    return line
+
+
+def secondary(L, dev, tc_peak, hbm_peak):
+    """Config 2 (causal prefill TFLOP/s), config 1 (1.7B decode latency) and config 4 (long
+    context decode GB/s) on this GPU."""
+    import torch
+
+    res = {}
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    # config 2: T=2048, Hq16/Hkv8, pages at seeded random ids, causal; append + prefill
+    rng = np.random.default_rng(2)
+    T, hq, hkv = 2048, 16, 8
+    n_pages = 64
+    perm = rng.permutation(n_pages).astype(np.int32)
+    kc = L.alloc_cache(n_pages * PAGE, hkv, dev)
+    vc = L.alloc_cache(n_pages * PAGE, hkv, dev)
+    g = torch.Generator(device=dev).manual_seed(2)
+    q_in = torch.randn((T, hq, D), generator=g, device=dev).bfloat16()
+    k_in = torch.randn((T, hkv, D), generator=g, device=dev).bfloat16()
+    v_in = torch.randn((T, hkv, D), generator=g, device=dev).bfloat16()
+    pos = torch.arange(T, dtype=torch.int32, device=dev)
+    cells = (torch.from_numpy(perm).to(dev).long()[pos.long() // PAGE] * PAGE + pos.long() % PAGE)
+    rope = L.rope_table(T, dev)
+    gamma = torch.ones(D, device=dev)
+    q16 = torch.empty((T, hq, D), dtype=torch.float16, device=dev)
+    bt = torch.from_numpy(perm[None]).to(dev)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=dev)
+    starts, p0, kvl = i32(0, T), i32(0), i32(T)
+    out = torch.empty((T, hq, D), device=dev)
+    flops = 4.0 * D * hq * T * (T + 1) / 2
+
+    def pre():
+        L.attn_prefill(kc, vc, q16, starts, p0, kvl, bt, T, SCALE, out=out)
+
+    L.kv_append(kc, vc, q_in, k_in, v_in, pos, cells, rope, gamma, gamma, 1e-6, q_out=q16)
+    for _ in range(5):
+        pre()
+    reps = 50
+    a, b = ev(), ev()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(reps):
+        pre()
+    b.record()
+    torch.cuda.synchronize()
+    pms = a.elapsed_time(b) / reps
+    a2, b2 = ev(), ev()
+    a2.record()
+    for _ in range(reps):
+        L.kv_append(kc, vc, q_in, k_in, v_in, pos, cells, rope, gamma, gamma, 1e-6, q_out=q16)
+    b2.record()
+    torch.cuda.synchronize()
+    ams = a2.elapsed_time(b2) / reps
+    res["config2_prefill"] = {"tflops": round(flops / (pms / 1e3) / 1e12, 1), "ms": round(pms, 4),
+                              "frac_of_bf16_peak": round(flops / (pms / 1e3) / 1e12 / tc_peak, 4),
+                              "causal_flops": flops, "append_ms": round(ams, 4),
+                              "note": "L2-resident (8 MiB of KV): back-to-back launches, no flush"}
+    # config 1: B=1, Hq16/Hkv8, 512 cached + 1 appended = 513 keys
+    kc1 = L.alloc_cache(20 * PAGE, 8, dev)
+    vc1 = L.alloc_cache(20 * PAGE, 8, dev)
+    kc1.normal_()
+    vc1.normal_()
+    bt1 = torch.from_numpy(np.random.default_rng(1).permutation(20)[:17].astype(np.int32)[None]).to(dev)
+    q1 = torch.randn((1, 16, D), device=dev)
+    lens1 = i32(513)
+    ws1 = L.DecodeWorkspace(1, 16, 8, dev)
+    o1 = torch.empty((1, 16, D), device=dev)
+    for _ in range(10):
+        L.attn_decode(kc1, vc1, q1, bt1, lens1, SCALE, max_seq_len=513, out=o1, workspace=ws1)
+    a, b = ev(), ev()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(200):
+        L.attn_decode(kc1, vc1, q1, bt1, lens1, SCALE, max_seq_len=513, out=o1, workspace=ws1)
+    b.record()
+    torch.cuda.synchronize()
+    res["config1_decode_us"] = round(a.elapsed_time(b) / 200 * 1e3, 2)
+    # config 4: one 131072-token context, Hq32/Hkv4, whole context on this GPU
+    ctx = 131072
+    n4 = ctx // PAGE
+    kc4 = L.alloc_cache(n4 * PAGE, HKV, dev)
+    vc4 = L.alloc_cache(n4 * PAGE, HKV, dev)
+    kc4.normal_()
+    vc4.normal_()
+    bt4 = torch.from_numpy(np.random.default_rng(4).permutation(n4).astype(np.int32)[None]).to(dev)
+    q4 = torch.randn((1, HQ, D), device=dev)
+    lens4 = i32(ctx)
+    ws4 = L.DecodeWorkspace(1, HQ, HKV, dev)
+    o4 = torch.empty((1, HQ, D), device=dev)
+    for _ in range(5):
+        L.attn_decode(kc4, vc4, q4, bt4, lens4, SCALE, max_seq_len=ctx, out=o4, workspace=ws4)
+    a, b = ev(), ev()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(50):
+        L.attn_decode(kc4, vc4, q4, bt4, lens4, SCALE, max_seq_len=ctx, out=o4, workspace=ws4)
+    b.record()
+    torch.cuda.synchronize()
+    ms4 = a.elapsed_time(b) / 50
+    gbs4 = ctx * HKV * D * 4 / (ms4 / 1e3) / 1e9
+    res["config4_long_decode"] = {"ms": round(ms4, 4), "gbs": round(gbs4, 1), "frac_hbm": round(gbs4 / hbm_peak, 4)}
+    L.check_status()
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# Reference arm: the reference's CPU path for this node, restated (oracle port, ggml precision)
+
+
+def run_reference(args):
+    from oracle import oracle as O
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    threads = O.hardware_threads()
+    rng, ctx = draw_workload(SEED)
+    # A bounded sample of the config-3 batch: the first n sequences, sized so the whole run takes
+    # about a minute of CPU time; K/V generated on the host with the same distributions.
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    keys = (ctx + 1).astype(np.int64)
+    probe_n = 1
+    n_pages = int((keys[:probe_n] + PAGE - 1).sum() // PAGE) + probe_n
+
+    def make(n):
+        need = (keys[:n] + PAGE - 1) // PAGE
+        total = int(need.sum())
+        perm = rng.permutation(total).astype(np.int32)
+        bt = np.zeros((n, int(need.max())), np.int32)
+        at = 0
+        for b in range(n):
+            bt[b, :need[b]] = perm[at:at + need[b]]
+            at += need[b]
+        k = rng.standard_normal((total * PAGE, HKV, D), dtype=np.float32)
+        k /= np.sqrt(np.mean(k * k, -1, keepdims=True) + 1e-6)
+        v = rng.standard_normal((total * PAGE, HKV, D), dtype=np.float32)
+        q = rng.standard_normal((n, HQ, D), dtype=np.float32)
+        return O.f32_to_f16_bits(k), O.f32_to_f16_bits(v), q, bt, keys[:n].astype(np.int32)
+
+    kc, vc, q, bt, lens = make(probe_n)
+    t0 = time.perf_counter()
+    O.paged_decode_ggml_fast(q, kc, vc, bt, lens, SCALE, n_threads=threads)
+    per_key = (time.perf_counter() - t0) / float(lens.sum())
+    # the sample: enough sequences (at least one) or a prefix of one sequence to fill the budget
+    n = 1
+    while n < N_SEQS and per_key * float(keys[:n + 1].sum()) < budget:
+        n += 1
+    kc, vc, q, bt, lens = make(n)
+    if per_key * float(lens.sum()) > budget:
+        lens = np.array([max(PAGE, int(budget / per_key))], np.int32)
+        q, bt = q[:1], bt[:1]
+    for _ in range(args.warmup):
+        O.paged_decode_ggml_fast(q, kc, vc, bt, lens, SCALE, n_threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.paged_decode_ggml_fast(q, kc, vc, bt, lens, SCALE, n_threads=threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    kv_bytes = float(lens.astype(np.int64).sum()) * HKV * D * 2 * 2
+    value = round(kv_bytes / dt / 1e9, 3)
+    sample = (f"{len(lens)} sequence(s) of the config-3 batch, {int(lens.sum())} keys per step "
+              f"(K/V bytes only), {dt * 1e3:.1f} ms per step")
+    return {
+        "impl": "reference",
+        "metric": "paged decode-attn HBM GB/s (config 3, Qwen3-30B-A3B GQA 32/4, 64 seqs/GPU)",
+        "value": value, "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 KV, f16 V accumulator (ggml CPU precision model)",
+        "data": "synthetic (seeded, host-generated, same distributions as the GPU arm)",
+        "config": {"workload": "config 3: batched paged decode attention (CPU, sampled)", "n_head": HQ,
+                   "n_head_kv": HKV, "head_dim": D, "page": PAGE},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-secondary", action="store_true", help="skip configs 1, 2 and 4")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    line = run_reference(args) if args.impl == "reference" else run_b200(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

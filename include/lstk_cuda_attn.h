@@ -1,0 +1,149 @@
+/*
+ * lstk_cuda_attn.h - C ABI of the B200 (sm_100a) backend for the Qwen3 attention node of
+ * ludehsar/localstack (`attn_block`, src/qwen3.cpp:128-171).
+ *
+ * The reference records these ggml ops per layer and lets ggml's scheduler run them
+ * (src/engine.cpp:282-298):
+ *     q/k = ggml_mul(ggml_rms_norm(.., eps), q_norm/k_norm)        src/qwen3.cpp:112-114, 139-140
+ *     q/k = ggml_rope_ext(.., GGML_ROPE_TYPE_NEOX, base, 1, 0, 1) src/qwen3.cpp:143-146
+ *     ggml_set_rows(kv.k[l] / kv.v[l], rows, kv_idxs)            src/qwen3.cpp:150-153
+ *     ggml_flash_attn_ext(Q, K, V, mask, 1/sqrt(hd), 0, 0)       src/qwen3.cpp:155-167
+ * Each entry point below replaces one group of those nodes. Everything is plain C: device
+ * pointers and sizes, no allocation, no host synchronisation, stream-ordered on `stream`
+ * (a cudaStream_t passed as void*; NULL = legacy default stream). Errors come back as a
+ * negative status with a message in lstk_cuda_last_error(), mirroring the reference's
+ * `bool + std::string &err` convention (src/kv_cache.h:47-48, src/engine.h:70-73).
+ *
+ * Cache layout (unchanged from the reference's KvCache, src/kv_cache.h:30-33 and
+ * src/kv_cache.cpp:20-26): one f16 tensor per layer for K and one for V, each
+ * [n_cells][n_head_kv][head_dim] (ggml [n_embd_gqa, size], ne0 innermost). Cell c holds one
+ * token; cells are handed out in blocks (pages) of block_size = 32 consecutive cells, and a
+ * sequence's block table lists its pages in position order (KvCache::seq_blocks,
+ * src/kv_cache.h:41): position p lives in cell table[p / 32] * 32 + p % 32
+ * (KvCache::alloc, src/kv_cache.cpp:59-83).
+ */
+#ifndef LSTK_CUDA_ATTN_H
+#define LSTK_CUDA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define LSTK_OK 0
+#define LSTK_ERR_INVALID_ARG (-1)  /* null pointer, bad size or shape */
+#define LSTK_ERR_CAPACITY (-2)     /* workspace too small, more work than a launch can hold */
+#define LSTK_ERR_TIMEOUT (-3)      /* a kernel's bounded wait ran out (device status) */
+#define LSTK_ERR_CUDA (-4)         /* a CUDA runtime/driver call failed */
+#define LSTK_ERR_UNSUPPORTED (-5)  /* shape outside what the kernels implement */
+#define LSTK_ERR_DEVICE_INDEX (-6) /* a kernel met an out-of-range cell, page or position */
+
+/* Element types. */
+#define LSTK_DTYPE_F32 0
+#define LSTK_DTYPE_F16 1
+#define LSTK_DTYPE_BF16 2
+
+/* Geometry of one layer's K (or V) cache tensor. */
+typedef struct lstk_kv_layout {
+    int64_t n_cells;    /* KvCache::size; a multiple of block_size */
+    int32_t n_head_kv;  /* Qwen3HParams::n_head_kv (src/qwen3.h:30) */
+    int32_t head_dim;   /* Qwen3HParams::head_dim; the kernels implement 128 */
+    int32_t block_size; /* KvCache::block_size (src/kv_cache.h:27); the kernels implement 32 */
+} lstk_kv_layout;
+
+/* Message for the last failed call on this host thread ("" if none). */
+const char *lstk_cuda_last_error(void);
+
+/* Synchronises `stream`, then reads and clears the device status word that kernels set when a
+ * bounded wait times out or an index is out of range. Returns LSTK_OK, LSTK_ERR_TIMEOUT,
+ * LSTK_ERR_DEVICE_INDEX or LSTK_ERR_CUDA. Status is per device and sticky until read. */
+int lstk_cuda_status(void *stream);
+
+/* ---- RoPE table -----------------------------------------------------------------------------
+ * ggml builds the NEOX rotation per step (ggml_rope_cache_init for each position); the backend
+ * reads the same values from a persistent table instead. Entry [p][i] = (cosf(t), sinf(t)) with
+ * t = freq_scale * theta_i, theta_0 = p and theta_{i+1} = theta_i * powf(freq_base, -2/head_dim)
+ * (repeated float multiplication), i < head_dim/2 - what ggml computes for the attn_block call
+ * (freq_factors null, ext_factor 0, attn_factor 1; src/qwen3.cpp:141-146).
+ * Host-side fill into a caller buffer of lstk_rope_table_bytes() bytes (float pairs). */
+size_t lstk_rope_table_bytes(int32_t n_pos, int32_t head_dim);
+int lstk_rope_table_fill(float *host_table, int32_t n_pos, int32_t head_dim, float freq_base, float freq_scale);
+
+/* ---- K/V append: replaces rms_norm+mul (Q,K), rope_ext (Q,K) and the two set_rows -----------
+ * (src/qwen3.cpp:139-153). For each of n_tokens tokens t:
+ *   Q head rows: RMSNorm (sum of squares in double, as ggml's CPU rms_norm) * q_gamma, NEOX RoPE
+ *                at positions[t] -> q_out[t][h][:] (f32 or f16);
+ *   K head rows: the same with k_gamma -> f16 (round-to-nearest-even) into k_cache at cells[t];
+ *   V head rows: -> f16 into v_cache at cells[t].
+ * Inputs are token-major rows [T][H][D] (f32 or bf16) with a per-token stride in elements, so a
+ * fused QKV projection output can be passed as three views. q_gamma / k_gamma may be NULL
+ * (no QK-norm, as for Qwen2, src/qwen3.cpp:139-140). positions must be < rope_n_pos and cells
+ * < n_cells; offending tokens are skipped and set LSTK_ERR_DEVICE_INDEX in the device status.
+ * Every f32 operation is separately rounded, so the written f16 pages are bit-identical to a
+ * CPU evaluation of the ggml op sequence with the same RoPE table. */
+int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
+                        const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
+                        const int32_t *positions, const int64_t *cells, const float *q_gamma, const float *k_gamma,
+                        float eps, const float *rope_table, int32_t rope_n_pos, void *q_out, int32_t q_out_dtype,
+                        void *stream);
+
+/* ---- Paged decode: replaces flash_attn_ext for one new token per sequence --------------------
+ * (src/qwen3.cpp:155-167 with n_tokens = 1 per sequence). Query b attends to positions
+ * [0, seq_lens[b]) of its own sequence through block_tables[b][:] - the cells KvCache::fill_mask
+ * leaves visible to the sequence's last token (src/kv_cache.cpp:140-150) - with
+ * softmax(scale * q k^T) v, f16 K/V, f16-rounded Q for the dot (as ggml's CPU kernel rounds Q to
+ * the K type) and f32 accumulation (GGML_PREC_F32, src/qwen3.cpp:167).
+ *   q            [n_seqs][n_head][head_dim], f32 or f16
+ *   block_tables [n_seqs][max_blocks_per_seq] int32 page ids (< n_cells / block_size)
+ *   seq_lens     [n_seqs] int32, 0 <= len <= max_blocks_per_seq * block_size
+ *   max_seq_len  host upper bound of seq_lens (sizes the launch; 0 = max_blocks * block_size)
+ *   out          [n_seqs][n_head][head_dim] f32; a sequence with no keys gets zeros
+ *   lse_out      optional [n_seqs][n_head] f32: natural-log sum of exp(scale * q k), -inf if empty
+ *   n_ctas       0 = one CTA per SM; otherwise the split-K grid size (results agree within
+ *                rounding for any value; identical for identical values)
+ * Split-K: the page-groups of all sequences are cut into n_ctas equal contiguous ranges, each
+ * CTA streams its range with TMA and emits per-piece (O, lse); a second kernel merges pieces by
+ * log-sum-exp. n_head / n_head_kv must be 1..8. */
+size_t lstk_cuda_attn_decode_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim);
+int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                          int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
+                          int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, float scale,
+                          float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
+                          void *stream);
+
+/* ---- Log-sum-exp merge of partial results over disjoint key ranges --------------------------
+ * Used when one long context is split across GPUs (each GPU runs lstk_cuda_attn_decode over its
+ * contiguous chunk of pages with lse_out). o_parts [n_parts][n_rows][head_dim] f32 (each
+ * normalised by its own softmax sum), lse_parts [n_parts][n_rows] (natural log, -inf = empty).
+ * out [n_rows][head_dim]; lse_out optional [n_rows]. */
+int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
+                         int32_t head_dim, float *out, float *lse_out, void *stream);
+
+/* ---- Paged causal prefill: replaces flash_attn_ext for a chunk of prompt tokens -------------
+ * (src/qwen3.cpp:155-167 with n_tokens > 1). Sequence b's query tokens are rows
+ * [q_seq_start[b], q_seq_start[b+1]) of q, at positions q_pos0[b], q_pos0[b]+1, ...; query
+ * token i attends to positions [0, min(pos_i + 1, kv_lens[b])) of its sequence (causal), read
+ * through block_tables[b][:] - the visibility KvCache::fill_mask grants. K/V must already hold
+ * the chunk (lstk_cuda_kv_append first, as attn_block writes set_rows before flash_attn_ext).
+ *   q            [total_tokens][n_head][head_dim], f16 (the tensor-core operand type) or f32
+ *                (converted into the workspace first)
+ *   q_seq_start  [n_seqs + 1] int32 device; max_q_len = host upper bound of any sequence's rows
+ *   out          [total_tokens][n_head][head_dim] f32
+ * Computed with tcgen05 tensor-core MMAs (f16 x f16 -> f32 in tensor memory) on 128-token tiles
+ * fed by TMA from the scattered pages. n_head / n_head_kv must be 1..8. */
+size_t lstk_cuda_attn_prefill_workspace_size(int64_t total_tokens, int32_t n_head, int32_t head_dim, int32_t q_dtype);
+int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                           int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *q_seq_start,
+                           int32_t max_q_len, int64_t total_tokens, const int32_t *q_pos0, const int32_t *kv_lens,
+                           const int32_t *block_tables, int32_t max_blocks_per_seq, float scale, float *out,
+                           void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSTK_CUDA_ATTN_H */

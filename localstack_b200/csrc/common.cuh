@@ -1,0 +1,169 @@
+// common.cuh - device helpers shared by the attention kernels: the device status word,
+// mbarrier operations with bounded waits, TMA tile loads, and small numeric utilities.
+// sm_100a only.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lstk {
+
+// ---------------------------------------------------------------------------------------------
+// Device status. Kernels never trap: a bounded wait that runs out or an out-of-range index is
+// recorded here (first error wins) and the kernel returns cleanly; lstk_cuda_status() reads it.
+enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadIndex = 2 };
+
+struct DeviceStatus {
+    int code;
+    int where;   // kernel-specific site id
+    int detail;  // offending value (index, stage, ...)
+    int pad;
+};
+
+// Where a status was raised (kept in DeviceStatus::where).
+enum : int {
+    kSiteAppendCell = 1,
+    kSiteAppendPos = 2,
+    kSiteDecodePage = 10,
+    kSiteDecodeLen = 11,
+    kSiteDecodeWaitFull = 12,
+    kSiteDecodeWaitEmpty = 13,
+    kSitePrefillPage = 20,
+    kSitePrefillWait = 21,
+};
+
+__device__ __forceinline__ void report(DeviceStatus *st, int code, int where, int detail) {
+    if (st != nullptr && atomicCAS(&st->code, 0, code) == 0) {
+        st->where = where;
+        st->detail = detail;
+    }
+}
+
+// Upper bound for any single wait inside a kernel. Normal waits last microseconds.
+constexpr uint64_t kWaitLimitNs = 4ull * 1000 * 1000 * 1000;
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared-memory addresses and mbarriers.
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (TMA / tensor-core) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for phase `parity` of the barrier. Gives up (returns false) when *abort becomes
+// non-zero or after kWaitLimitNs; the caller records the timeout and unwinds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const volatile int *abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1; i < (1u << 30); i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 0) {
+            if (abort != nullptr && *abort) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+        }
+    }
+    return false;
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMA: tiled tensor loads global -> shared, completion counted on an mbarrier (no multicast).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                                 int c2, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+        "%4, %5}], [%2], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+        : "memory");
+}
+
+// L2 policy for data read exactly once (streamed KV pages).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Numerics.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float warp_max_xor(float v, int lane_mask_lo) {
+    for (int m = lane_mask_lo; m < 32; m <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum_xor(float v, int lane_mask_lo) {
+    for (int m = lane_mask_lo; m < 32; m <<= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+// Byte offset of the 16-byte chunk `chunk` (0..7) of 128-byte row `row` inside a 1024-byte
+// aligned tile written by TMA with CU_TENSOR_MAP_SWIZZLE_128B: the chunk index is XORed with
+// the row index modulo 8.
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
+    return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
+}  // namespace lstk

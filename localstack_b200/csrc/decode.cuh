@@ -1,0 +1,529 @@
+// decode.cuh - paged split-K flash-decoding (one new token per sequence) and the LSE combine.
+//
+// Replaces flash_attn_ext for the decode step (src/qwen3.cpp:155-167, n_tokens = 1). HBM-bound:
+// per sequence it must stream len * n_head_kv * 128 * 2 bytes of K plus the same of V once.
+//
+// Data layout. K and V caches keep the reference layout [n_cells][n_head_kv][128] f16. A page
+// is 32 consecutive cells; one KV head's share of a page is 32 rows of 256 bytes at a stride of
+// n_head_kv * 256 bytes. A TMA tensor map over (d, head, cell) with box (64, 1, 32) and 128-byte
+// swizzle loads half of one head's page (32 rows x 128 bytes) per instruction.
+//
+// Work decomposition (split-K over "page-groups"). A segment is (sequence b, head group hg) where
+// a head group is up to 4 KV heads; it has ceil(len_b / 32) page-groups, each = one page of those
+// 4 heads' K and V (64 KiB, read contiguously from HBM). All segments are concatenated into one
+// index space of P page-groups and cut into gridDim.x equal contiguous ranges, one per CTA, so
+// every CTA streams the same number of bytes whatever the mix of context lengths. Where a range
+// boundary falls inside a segment, the pieces on either side are merged later by log-sum-exp
+// (decode_combine_kernel); a segment inside one CTA is written out directly.
+//
+// CTA roles. Warp 4 (one lane) issues TMA loads into a 3-stage ring of 64 KiB stages; warps 0..3
+// each own one KV head of the group and run the attention for it with mma.sync m16n8k16
+// (f16 x f16 -> f32): S^T[16 tokens x 8 q-heads] = K[16 x 128] . Q^T, online softmax down the
+// token axis, P^T re-packed in registers with movmatrix, then O^T[128 x 8] += V^T . P^T. The
+// 8-wide N side holds the GQA group (n_head / n_head_kv <= 8 query heads share one K/V head), so
+// every K/V byte brought in is used by all its query heads. The tensor cores only matter here
+// because they take the FLOPs off the issue slots; the kernel is bound by HBM bytes.
+#pragma once
+
+#include "common.cuh"
+
+namespace lstk {
+namespace decode {
+
+constexpr int kD = 128;
+constexpr int kPage = 32;
+constexpr int kHeadsPerGroup = 4;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 3;
+constexpr int kSubTile = kPage * 128;                                // 4 KiB: 32 rows x 128 B
+constexpr int kHeadPage = 2 * kSubTile;                              // 8 KiB: one head's K page
+constexpr int kStageBytes = 2 * kHeadsPerGroup * kHeadPage;          // 64 KiB: K and V, 4 heads
+constexpr int kMaxCtas = 512;
+constexpr int kMaxGroup = 8;
+constexpr int kMaxSeqs = 4096;
+constexpr int kPartRows = kHeadsPerGroup * kMaxGroup;                // partial rows per piece
+
+struct Params {
+    const void *q;
+    int q_f16;
+    const int32_t *block_tables;
+    int max_blocks;
+    const int32_t *seq_lens;
+    int n_seqs, n_head, n_head_kv, group, n_hg;
+    int64_t n_pages;
+    float scale_log2;  // softmax scale * log2(e)
+    float *out;
+    float *lse_out;
+    float *part_o;    // [kMaxCtas][2][kPartRows][128]
+    float *part_lse;  // [kMaxCtas][2][kPartRows], log2 units
+    int32_t *prefix;  // [n_seqs + 1] pages before each sequence
+    DeviceStatus *status;
+};
+
+__host__ __device__ inline int64_t range_lo(int c, int64_t P, int G) { return ((int64_t) c * P) / G; }
+
+// Index of the CTA whose range [lo_c, lo_{c+1}) contains page-group x.
+__device__ inline int cta_of(int64_t x, int64_t P, int G) {
+    int c = (int) ((x * G) / P);
+    while (c + 1 < G && range_lo(c + 1, P, G) <= x) c++;
+    while (c > 0 && range_lo(c, P, G) > x) c--;
+    return c;
+}
+
+// Walks page-groups in index order: sequence b, head group hg, page p.
+struct Cursor {
+    int b, hg, p;
+    __device__ void locate(int64_t x, const int32_t *pfx, int n_seqs, int n_hg) {
+        int lo = 0, hi = n_seqs;  // largest b with n_hg * pfx[b] <= x
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((int64_t) n_hg * pfx[mid] <= x) lo = mid; else hi = mid - 1;
+        }
+        b = lo;
+        const int np = pfx[b + 1] - pfx[b];
+        const int64_t r = x - (int64_t) n_hg * pfx[b];
+        hg = (int) (r / np);
+        p = (int) (r % np);
+    }
+    __device__ void advance(const int32_t *pfx, int n_seqs, int n_hg) {
+        const int np = pfx[b + 1] - pfx[b];
+        if (++p < np) return;
+        p = 0;
+        if (++hg < n_hg) return;
+        hg = 0;
+        do { ++b; } while (b < n_seqs && pfx[b + 1] == pfx[b]);
+    }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t r[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t r[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Address of 16-byte chunk `chunk` (0..15 across the 128 dims) of token row `tok` (0..31) in one
+// head's page buffer: two 4 KiB swizzled sub-tiles, dims 0..63 then 64..127.
+__device__ __forceinline__ uint32_t page_addr(uint32_t base, int tok, int chunk) {
+    return base + (uint32_t) (chunk >> 3) * kSubTile + sw128_offset((uint32_t) tok, (uint32_t) (chunk & 7));
+}
+
+// Per-warp running state for one (segment piece, KV head): 8 query-head columns, 128 dims.
+struct HeadState {
+    float o[8][4];   // O^T fragments: m-tile mt covers dims 16mt..16mt+15
+    float m[2];      // running max (log2 units) for query heads 2t, 2t+1
+    float l[2];      // this lane's partial softmax sums for heads 2t, 2t+1
+    uint32_t qb[8][2];
+    __device__ void reset() {
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+    }
+};
+
+// Loads the B fragments of Q^T (k = dims, n = query heads) for one KV head's query group.
+__device__ __forceinline__ void load_q(HeadState &st, const Params &p, int b, int kvh, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const bool live = g < p.group;
+    const int64_t row = ((int64_t) b * p.n_head + (int64_t) kvh * p.group + (live ? g : 0)) * kD;
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) {
+        const int d0 = kk * 16 + 2 * t;
+        if (!live) {
+            st.qb[kk][0] = st.qb[kk][1] = 0u;
+        } else if (p.q_f16) {
+            const __half *q = reinterpret_cast<const __half *>(p.q) + row;
+            st.qb[kk][0] = *reinterpret_cast<const uint32_t *>(q + d0);
+            st.qb[kk][1] = *reinterpret_cast<const uint32_t *>(q + d0 + 8);
+        } else {
+            const float *q = reinterpret_cast<const float *>(p.q) + row;
+            const float2 a = *reinterpret_cast<const float2 *>(q + d0);
+            const float2 c = *reinterpret_cast<const float2 *>(q + d0 + 8);
+            st.qb[kk][0] = pack_half2(a.x, a.y);
+            st.qb[kk][1] = pack_half2(c.x, c.y);
+        }
+    }
+}
+
+// One page (32 tokens, `valid` of them visible) of one KV head.
+__device__ __forceinline__ void process_page(HeadState &st, uint32_t kbase, uint32_t vbase, int valid,
+                                             float scale_log2, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int li = lane >> 3, lr = lane & 7;
+#pragma unroll
+    for (int slab = 0; slab < 2; slab++) {
+        if (slab * 16 >= valid) break;
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            uint32_t a[4];
+            ldsm_x4(page_addr(kbase, slab * 16 + lr + 8 * (li & 1), 2 * kk + (li >> 1)), a);
+            mma_16816(s, a, st.qb[kk][0], st.qb[kk][1]);
+        }
+        // s[0],s[1]: token slab*16+g, heads 2t,2t+1; s[2],s[3]: token +8.
+        const int tok0 = slab * 16 + g;
+        const bool v0 = tok0 < valid, v1 = tok0 + 8 < valid;
+        float x[4];
+        x[0] = v0 ? s[0] * scale_log2 : -INFINITY;
+        x[1] = v0 ? s[1] * scale_log2 : -INFINITY;
+        x[2] = v1 ? s[2] * scale_log2 : -INFINITY;
+        x[3] = v1 ? s[3] * scale_log2 : -INFINITY;
+        float alpha[2], mu[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float tm = fmaxf(x[h], x[h + 2]);
+            tm = warp_max_xor(tm, 4);
+            const float mn = fmaxf(st.m[h], tm);
+            mu[h] = mn == -INFINITY ? 0.f : mn;
+            alpha[h] = fast_exp2(st.m[h] - mu[h]);
+            st.m[h] = mn;
+        }
+        const float p0 = fast_exp2(x[0] - mu[0]);
+        const float p1 = fast_exp2(x[1] - mu[1]);
+        const float p2 = fast_exp2(x[2] - mu[0]);
+        const float p3 = fast_exp2(x[3] - mu[1]);
+        st.l[0] = st.l[0] * alpha[0] + (p0 + p2);
+        st.l[1] = st.l[1] * alpha[1] + (p1 + p3);
+#pragma unroll
+        for (int mt = 0; mt < 8; mt++) {
+            st.o[mt][0] *= alpha[0];
+            st.o[mt][1] *= alpha[1];
+            st.o[mt][2] *= alpha[0];
+            st.o[mt][3] *= alpha[1];
+        }
+        const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
+        const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
+        const bool tail = (slab + 1) * 16 > valid;
+#pragma unroll
+        for (int mt = 0; mt < 8; mt++) {
+            uint32_t a[4];
+            ldsm_x4_trans(page_addr(vbase, slab * 16 + lr + 8 * (li >> 1), 2 * mt + (li & 1)), a);
+            if (tail) {
+                // Zero V where the token is not visible, so stale non-finite cells cannot leak
+                // through a zero probability. a0,a1: tokens 2t,2t+1; a2,a3: tokens 2t+8,2t+9.
+                const int tb = slab * 16 + 2 * t;
+                const uint32_t lo_keep = (tb < valid ? 0x0000ffffu : 0u) | (tb + 1 < valid ? 0xffff0000u : 0u);
+                const uint32_t hi_keep = (tb + 8 < valid ? 0x0000ffffu : 0u) | (tb + 9 < valid ? 0xffff0000u : 0u);
+                a[0] &= lo_keep;
+                a[1] &= lo_keep;
+                a[2] &= hi_keep;
+                a[3] &= hi_keep;
+            }
+            mma_16816(st.o[mt], a, pb0, pb1);
+        }
+    }
+}
+
+extern __shared__ __align__(1024) uint8_t dyn_smem[];
+
+__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                    const __grid_constant__ CUtensorMap vmap,
+                                                                    const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t *stages = base;
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + kStages * kStageBytes);
+    uint64_t *empty = full + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
+    int32_t *pfx = reinterpret_cast<int32_t *>(empty + kStages) + 4;
+
+    // Prefix over sequences of page counts (every CTA computes it; CTA 0 publishes it).
+    __shared__ int32_t chunk_sum[kThreads];
+    {
+        const int per = (p.n_seqs + kThreads - 1) / kThreads;
+        const int b0 = threadIdx.x * per;
+        int32_t local = 0;
+        for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
+            int32_t len = p.seq_lens[b];
+            if (len < 0 || len > p.max_blocks * kPage) {
+                report(p.status, kStatusBadIndex, kSiteDecodeLen, b);
+                len = len < 0 ? 0 : p.max_blocks * kPage;
+            }
+            local += (len + kPage - 1) / kPage;
+        }
+        chunk_sum[threadIdx.x] = local;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int32_t acc = 0;
+            for (int i = 0; i < kThreads; i++) {
+                const int32_t v = chunk_sum[i];
+                chunk_sum[i] = acc;
+                acc += v;
+            }
+        }
+        __syncthreads();
+        int32_t acc = chunk_sum[threadIdx.x];
+        for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
+            pfx[b] = acc;
+            int32_t len = p.seq_lens[b];
+            len = len < 0 ? 0 : min(len, p.max_blocks * kPage);
+            acc += (len + kPage - 1) / kPage;
+        }
+        if (threadIdx.x == kThreads - 1) pfx[p.n_seqs] = acc;
+        if (threadIdx.x == 0) {
+            *abort_flag = 0;
+            for (int s = 0; s < kStages; s++) {
+                mbar_init(smem_u32(&full[s]), 1);
+                mbar_init(smem_u32(&empty[s]), kConsumerWarps);
+            }
+            fence_barrier_init();
+        }
+        __syncthreads();
+        if (blockIdx.x == 0)
+            for (int b = threadIdx.x; b <= p.n_seqs; b += kThreads) p.prefix[b] = pfx[b];
+    }
+
+    const int64_t P = (int64_t) p.n_hg * pfx[p.n_seqs];
+    const int64_t lo = range_lo(blockIdx.x, P, gridDim.x);
+    const int64_t hi = range_lo(blockIdx.x + 1, P, gridDim.x);
+
+    if (lo < hi && warp == kConsumerWarps) {
+        // Producer: one lane streams the CTA's page-groups through the stage ring.
+        if (lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            const uint64_t policy = l2_policy_evict_first();
+            Cursor cur;
+            cur.locate(lo, pfx, p.n_seqs, p.n_hg);
+            int64_t i = 0;
+            bool ok = true;
+            for (int64_t x = lo; x < hi; x++, i++) {
+                const int s = (int) (i % kStages);
+                const uint32_t k_use = (uint32_t) (i / kStages);
+                if (k_use > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag)) {
+                    report(p.status, kStatusTimeout, kSiteDecodeWaitEmpty, s);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + cur.p];
+                const int nh = min(kHeadsPerGroup, p.n_head_kv - cur.hg * kHeadsPerGroup);
+                const uint32_t fb = smem_u32(&full[s]);
+                if (pid < 0 || pid >= p.n_pages) {
+                    report(p.status, kStatusBadIndex, kSiteDecodePage, pid);
+                    mbar_arrive(fb);
+                } else {
+                    mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kHeadPage));
+                    const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                    for (int h = 0; h < nh; h++) {
+                        const int kvh = cur.hg * kHeadsPerGroup + h;
+                        for (int half = 0; half < 2; half++) {
+                            const uint32_t off = (uint32_t) (h * kHeadPage + half * kSubTile);
+                            tma_load_3d_hint(sb + off, &kmap, fb, half * 64, kvh, pid * kPage, policy);
+                            tma_load_3d_hint(sb + kHeadsPerGroup * kHeadPage + off, &vmap, fb, half * 64, kvh,
+                                             pid * kPage, policy);
+                        }
+                    }
+                }
+                cur.advance(pfx, p.n_seqs, p.n_hg);
+            }
+            if (!ok || *abort_flag) {
+                // Let every copy already issued land before the CTA's shared memory goes away.
+                const int64_t n_issued = i;
+                for (int64_t j = n_issued > kStages ? n_issued - kStages : 0; j < n_issued; j++)
+                    mbar_wait_bounded(smem_u32(&full[j % kStages]), (uint32_t) (j / kStages) & 1, nullptr);
+            }
+        }
+    } else if (lo < hi) {
+        // Consumers: warp w owns KV head hg*4 + w of every page-group.
+        HeadState st;
+        Cursor cur;
+        cur.locate(lo, pfx, p.n_seqs, p.n_hg);
+        int64_t piece_start = lo;
+        int64_t i = 0;
+        for (int64_t x = lo; x < hi; x++, i++) {
+            const int np = pfx[cur.b + 1] - pfx[cur.b];
+            const int kvh = cur.hg * kHeadsPerGroup + warp;
+            const bool active = kvh < p.n_head_kv;
+            if (x == lo || cur.p == 0) {
+                piece_start = x;
+                st.reset();
+                if (active) load_q(st, p, cur.b, kvh, lane);
+            }
+            const int s = (int) (i % kStages);
+            // Warp-uniform outcome: ldmatrix / mma.sync below are warp-collective.
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full[s]), (uint32_t) (i / kStages) & 1,
+                                                             abort_flag))) {
+                if (lane == 0) {
+                    report(p.status, kStatusTimeout, kSiteDecodeWaitFull, s);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + cur.p];
+            if (active && pid >= 0 && pid < p.n_pages) {
+                int len = p.seq_lens[cur.b];
+                len = len < 0 ? 0 : min(len, p.max_blocks * kPage);
+                const int valid = min(kPage, len - cur.p * kPage);
+                const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage, valid,
+                             p.scale_log2, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
+
+            if (cur.p == np - 1 || x == hi - 1) {
+                // Piece ends: finish the softmax sums and write the (partial) result.
+                const int g = lane >> 2, t = lane & 3;
+                float l[2];
+                l[0] = warp_sum_xor(st.l[0], 4);
+                l[1] = warp_sum_xor(st.l[1], 4);
+                const bool whole = piece_start == x - cur.p && cur.p == np - 1;
+                if (active) {
+                    const int slot = piece_start == lo ? 0 : 1;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int n = 2 * t + h;
+                        if (n >= p.group) continue;
+                        const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
+                        const float lse2 = l[h] > 0.f ? st.m[h] + __log2f(l[h]) : -INFINITY;
+                        float *dst;
+                        if (whole) {
+                            dst = p.out + ((int64_t) cur.b * p.n_head + (int64_t) kvh * p.group + n) * kD;
+                            if (g == 0 && p.lse_out != nullptr)
+                                p.lse_out[(int64_t) cur.b * p.n_head + (int64_t) kvh * p.group + n] =
+                                    lse2 * 0.69314718055994531f;
+                        } else {
+                            const int64_t prow = ((int64_t) blockIdx.x * 2 + slot) * kPartRows +
+                                                 (int64_t) warp * kMaxGroup + n;
+                            dst = p.part_o + prow * kD;
+                            if (g == 0) p.part_lse[prow] = lse2;
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < 8; mt++) {
+                            dst[mt * 16 + g] = st.o[mt][h] * inv;
+                            dst[mt * 16 + g + 8] = st.o[mt][h + 2] * inv;
+                        }
+                    }
+                }
+            }
+            cur.advance(pfx, p.n_seqs, p.n_hg);
+        }
+    }
+    __syncthreads();
+}
+
+struct CombineParams {
+    int n_seqs, n_head, n_head_kv, group, n_hg, grid;
+    const int32_t *prefix;
+    const float *part_o;
+    const float *part_lse;
+    float *out;
+    float *lse_out;
+};
+
+// One CTA per segment (b, hg); thread = (row of the 4x8 partial block, 16-dim slice).
+__global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams p) {
+    const int b = blockIdx.x, hg = blockIdx.y;
+    const int row = threadIdx.x >> 3;
+    const int d0 = (threadIdx.x & 7) * 16;
+    const int w = row / kMaxGroup, n = row % kMaxGroup;
+    const int kvh = hg * kHeadsPerGroup + w;
+    if (kvh >= p.n_head_kv || n >= p.group) return;
+    const int64_t out_row = (int64_t) b * p.n_head + (int64_t) kvh * p.group + n;
+    const int32_t pb = p.prefix[b];
+    const int np = p.prefix[b + 1] - pb;
+    if (np == 0) {
+        for (int d = 0; d < 16; d++) p.out[out_row * kD + d0 + d] = 0.f;
+        if (d0 == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
+        return;
+    }
+    const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
+    const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
+    const int c0 = cta_of(x0, P, p.grid);
+    const int c1 = cta_of(x0 + np - 1, P, p.grid);
+    if (c0 == c1) return;
+    // CTAs between c0 and c1 whose range is empty (more CTAs than page-groups) wrote nothing.
+    float M = -INFINITY;
+    for (int c = c0; c <= c1; c++) {
+        if (range_lo(c + 1, P, p.grid) <= range_lo(c, P, p.grid)) continue;
+        const int slot = range_lo(c, P, p.grid) < x0 ? 1 : 0;
+        M = fmaxf(M, p.part_lse[((int64_t) c * 2 + slot) * kPartRows + w * kMaxGroup + n]);
+    }
+    float acc[16];
+#pragma unroll
+    for (int d = 0; d < 16; d++) acc[d] = 0.f;
+    float den = 0.f;
+    if (M != -INFINITY) {
+        for (int c = c0; c <= c1; c++) {
+            if (range_lo(c + 1, P, p.grid) <= range_lo(c, P, p.grid)) continue;
+            const int slot = range_lo(c, P, p.grid) < x0 ? 1 : 0;
+            const int64_t prow = ((int64_t) c * 2 + slot) * kPartRows + w * kMaxGroup + n;
+            const float wt = exp2f(p.part_lse[prow] - M);
+            den += wt;
+            const float4 *src = reinterpret_cast<const float4 *>(p.part_o + prow * kD + d0);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; q4++) {
+                const float4 v = src[q4];
+                acc[4 * q4 + 0] += wt * v.x;
+                acc[4 * q4 + 1] += wt * v.y;
+                acc[4 * q4 + 2] += wt * v.z;
+                acc[4 * q4 + 3] += wt * v.w;
+            }
+        }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    float4 *dst = reinterpret_cast<float4 *>(p.out + out_row * kD + d0);
+#pragma unroll
+    for (int q4 = 0; q4 < 4; q4++)
+        dst[q4] = make_float4(acc[4 * q4] * inv, acc[4 * q4 + 1] * inv, acc[4 * q4 + 2] * inv, acc[4 * q4 + 3] * inv);
+    if (d0 == 0 && p.lse_out != nullptr)
+        p.lse_out[out_row] = den > 0.f ? (M + __log2f(den)) * 0.69314718055994531f : -INFINITY;
+}
+
+// LSE merge of n_parts partial results (natural-log lse), one warp per output row.
+__global__ void __launch_bounds__(256) lse_merge_kernel(const float *o_parts, const float *lse_parts, int n_parts,
+                                                        int64_t n_rows, int head_dim, float *out, float *lse_out) {
+    const int64_t row = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= n_rows) return;
+    float M = -INFINITY;
+    for (int r = 0; r < n_parts; r++) M = fmaxf(M, lse_parts[(int64_t) r * n_rows + row]);
+    float den = 0.f;
+    for (int d = lane; d < head_dim; d += 32) out[row * head_dim + d] = 0.f;
+    if (M == -INFINITY) {
+        if (lane == 0 && lse_out) lse_out[row] = -INFINITY;
+        return;
+    }
+    for (int d = lane; d < head_dim; d += 32) {
+        float acc = 0.f;
+        float dn = 0.f;
+        for (int r = 0; r < n_parts; r++) {
+            const float wt = __expf(lse_parts[(int64_t) r * n_rows + row] - M);
+            dn += wt;
+            acc += wt * o_parts[((int64_t) r * n_rows + row) * head_dim + d];
+        }
+        out[row * head_dim + d] = acc / dn;
+        den = dn;
+    }
+    den = __shfl_sync(0xffffffffu, den, 0);
+    if (lane == 0 && lse_out) lse_out[row] = M + __logf(den);
+}
+
+}  // namespace decode
+}  // namespace lstk

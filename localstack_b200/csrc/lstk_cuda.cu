@@ -1,0 +1,403 @@
+// lstk_cuda.cu - the extern "C" entry points of include/lstk_cuda_attn.h: argument validation,
+// device binding, TMA tensor-map construction and kernel launches. No allocation, no host sync
+// (except lstk_cuda_status, whose job is to synchronise and read the device status word).
+#include "common.cuh"
+#include "decode.cuh"
+#include "host_util.h"
+#include "kv_append.cuh"
+#include "prefill.cuh"
+
+#include "lstk_cuda_attn.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+namespace lstk {
+
+// One status word per device that has loaded this library.
+__device__ DeviceStatus g_device_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    bool ready = false;
+    int n_sms = 0;
+    DeviceStatus *status = nullptr;
+    size_t decode_smem = 0;
+    bool prefill_attr = false;
+};
+
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_devices_mu;
+thread_local int t_last_device = -1;
+
+std::string cuda_msg(const char *what, cudaError_t e) {
+    return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+}
+
+// Makes the device that owns `ptr` current for this runtime and returns its info.
+int bind_device(const void *ptr, DeviceInfo **info) {
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+    if (e != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return set_error(LSTK_ERR_INVALID_ARG, "pointer is not device memory" +
+                                                   (e != cudaSuccess ? std::string(": ") + cudaGetErrorName(e) : ""));
+    }
+    const int dev = attr.device;
+    if (dev < 0 || dev >= kMaxDevices) return set_error(LSTK_ERR_UNSUPPORTED, "device ordinal out of range");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaSetDevice", e));
+    std::lock_guard<std::mutex> lock(g_devices_mu);
+    DeviceInfo &d = g_devices[dev];
+    if (!d.ready) {
+        if ((e = cudaDeviceGetAttribute(&d.n_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return set_error(LSTK_ERR_CUDA, cuda_msg("cudaDeviceGetAttribute", e));
+        void *addr = nullptr;
+        if ((e = cudaGetSymbolAddress(&addr, g_device_status)) != cudaSuccess)
+            return set_error(LSTK_ERR_CUDA, cuda_msg("cudaGetSymbolAddress", e));
+        d.status = static_cast<DeviceStatus *>(addr);
+        d.ready = true;
+    }
+    t_last_device = dev;
+    *info = &d;
+    return LSTK_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// 3-D f16 map over [dim2][dim1][dim0] (dim0 contiguous) with a (box0, box1, box2) box and
+// 128-byte swizzle; out-of-range boxes fill zeros.
+int encode_f16_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
+                  uint32_t box1, uint32_t box2) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[3] = {dim0, dim1, dim2};
+    const cuuint64_t strides[2] = {dim0 * 2, dim0 * dim1 * 2};
+    const cuuint32_t box[3] = {box0, box1, box2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
+    return LSTK_OK;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int check_layout(const lstk_kv_layout *L, const char *fn) {
+    if (L == nullptr) return set_error(LSTK_ERR_INVALID_ARG, std::string(fn) + ": layout is NULL");
+    if (L->head_dim != 128 || L->block_size != 32)
+        return set_error(LSTK_ERR_UNSUPPORTED, std::string(fn) + ": kernels implement head_dim 128, block_size 32");
+    if (L->n_head_kv <= 0 || L->n_cells <= 0 || L->n_cells % L->block_size != 0 || L->n_cells > (int64_t) INT32_MAX)
+        return set_error(LSTK_ERR_INVALID_ARG, std::string(fn) + ": bad layout (n_head_kv, n_cells)");
+    return LSTK_OK;
+}
+
+int launch_check(const char *what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg(what, e));
+    return clear_error();
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Decode workspace: [prefix (n_seqs+1) int32][part_lse][part_o], each 256-byte aligned.
+size_t decode_ws_prefix_bytes(int32_t n_seqs) { return align_up(sizeof(int32_t) * ((size_t) n_seqs + 1), 256); }
+constexpr size_t kDecodePartLseBytes = sizeof(float) * decode::kMaxCtas * 2 * decode::kPartRows;
+constexpr size_t kDecodePartOBytes = sizeof(float) * decode::kMaxCtas * 2 * decode::kPartRows * decode::kD;
+
+}  // namespace
+}  // namespace lstk
+
+using namespace lstk;
+
+extern "C" {
+
+int lstk_cuda_status(void *stream) {
+    if (t_last_device < 0) return clear_error();
+    DeviceInfo &d = g_devices[t_last_device];
+    cudaError_t e = cudaSetDevice(t_last_device);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("lstk_cuda_status", e));
+    DeviceStatus st;
+    if ((e = cudaMemcpy(&st, d.status, sizeof(st), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return set_error(LSTK_ERR_CUDA, cuda_msg("lstk_cuda_status read", e));
+    if (st.code == kStatusOk) return clear_error();
+    const DeviceStatus zero = {0, 0, 0, 0};
+    cudaMemcpy(d.status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    char buf[160];
+    snprintf(buf, sizeof(buf), "device status: %s at site %d (detail %d)",
+             st.code == kStatusTimeout ? "bounded wait timed out" : "index out of range", st.where, st.detail);
+    return set_error(st.code == kStatusTimeout ? LSTK_ERR_TIMEOUT : LSTK_ERR_DEVICE_INDEX, buf);
+}
+
+int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
+                        const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
+                        const int32_t *positions, const int64_t *cells, const float *q_gamma, const float *k_gamma,
+                        float eps, const float *rope_table, int32_t rope_n_pos, void *q_out, int32_t q_out_dtype,
+                        void *stream) {
+    int rc = check_layout(layout, "lstk_cuda_kv_append");
+    if (rc) return rc;
+    if (n_tokens < 0 || n_head <= 0 || n_head % layout->n_head_kv != 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: bad n_tokens / n_head");
+    if (in_dtype != LSTK_DTYPE_F32 && in_dtype != LSTK_DTYPE_BF16)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_kv_append: in_dtype must be f32 or bf16");
+    if (q_out_dtype != LSTK_DTYPE_F32 && q_out_dtype != LSTK_DTYPE_F16)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_kv_append: q_out_dtype must be f32 or f16");
+    if (!k_cache || !v_cache || !q_in || !k_in || !v_in || !positions || !cells || !rope_table || !q_out ||
+        rope_n_pos <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: NULL pointer or empty rope table");
+    const int hd = layout->head_dim;
+    if (q_row_stride < (int64_t) n_head * hd || k_row_stride < (int64_t) layout->n_head_kv * hd ||
+        v_row_stride < (int64_t) layout->n_head_kv * hd || q_row_stride % 4 || k_row_stride % 4 || v_row_stride % 4)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: row strides too small or not multiples of 4");
+    if (!aligned(q_in, 16) || !aligned(k_in, 16) || !aligned(v_in, 16) || !aligned(q_out, 16) ||
+        !aligned(k_cache, 16) || !aligned(v_cache, 16))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: pointers must be 16-byte aligned");
+    if (n_tokens == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(k_cache, &dev))) return rc;
+    append::Params p;
+    p.q_in = q_in;
+    p.k_in = k_in;
+    p.v_in = v_in;
+    p.q_stride = q_row_stride;
+    p.k_stride = k_row_stride;
+    p.v_stride = v_row_stride;
+    p.in_bf16 = in_dtype == LSTK_DTYPE_BF16;
+    p.n_tokens = n_tokens;
+    p.n_head = n_head;
+    p.n_head_kv = layout->n_head_kv;
+    p.positions = positions;
+    p.cells = cells;
+    p.q_gamma = q_gamma;
+    p.k_gamma = k_gamma;
+    p.eps = eps;
+    p.rope = reinterpret_cast<const float2 *>(rope_table);
+    p.rope_n_pos = rope_n_pos;
+    p.k_cache = static_cast<__half *>(k_cache);
+    p.v_cache = static_cast<__half *>(v_cache);
+    p.n_cells = layout->n_cells;
+    p.q_out = q_out;
+    p.q_out_f16 = q_out_dtype == LSTK_DTYPE_F16;
+    p.status = dev->status;
+    const int64_t rows = (int64_t) n_tokens * (n_head + 2 * layout->n_head_kv);
+    const int64_t groups = (rows + append::kRowsPerWarp - 1) / append::kRowsPerWarp;
+    const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * 16);
+    append::kv_append_kernel<<<(unsigned) blocks, append::kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return launch_check("kv_append_kernel");
+}
+
+size_t lstk_cuda_attn_decode_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim) {
+    (void) n_head;
+    (void) n_head_kv;
+    (void) head_dim;
+    if (n_seqs < 0) return 0;
+    return decode_ws_prefix_bytes(n_seqs) + kDecodePartLseBytes + kDecodePartOBytes;
+}
+
+int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                          int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
+                          int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, float scale,
+                          float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
+                          void *stream) {
+    int rc = check_layout(layout, "lstk_cuda_attn_decode");
+    if (rc) return rc;
+    const int hkv = layout->n_head_kv;
+    if (n_seqs < 0 || n_head <= 0 || n_head % hkv != 0 || max_blocks_per_seq <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode: bad n_seqs / n_head / max_blocks_per_seq");
+    const int group = n_head / hkv;
+    if (group > decode::kMaxGroup)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode: n_head / n_head_kv must be at most 8");
+    if (n_seqs > decode::kMaxSeqs)
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode: more than 4096 sequences in one call");
+    if (q_dtype != LSTK_DTYPE_F32 && q_dtype != LSTK_DTYPE_F16)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode: q_dtype must be f32 or f16");
+    if (!k_cache || !v_cache || !q || !block_tables || !seq_lens || !out || !workspace)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode: NULL pointer");
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16) || !aligned(out, 16) ||
+        !aligned(workspace, 256))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode: misaligned pointer");
+    if (workspace_bytes < lstk_cuda_attn_decode_workspace_size(n_seqs, n_head, hkv, layout->head_dim))
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode: workspace too small");
+    if (max_seq_len <= 0 || max_seq_len > max_blocks_per_seq * layout->block_size)
+        max_seq_len = max_blocks_per_seq * layout->block_size;
+    if (n_seqs == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(k_cache, &dev))) return rc;
+
+    CUtensorMap kmap, vmap;
+    if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+    if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+
+    const int n_hg = (hkv + decode::kHeadsPerGroup - 1) / decode::kHeadsPerGroup;
+    const int64_t max_groups = (int64_t) n_seqs * n_hg * ((max_seq_len + decode::kPage - 1) / decode::kPage);
+    int64_t grid = n_ctas > 0 ? n_ctas : dev->n_sms;
+    grid = std::max<int64_t>(1, std::min<int64_t>({grid, max_groups, (int64_t) decode::kMaxCtas}));
+
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    decode::Params p;
+    p.q = q;
+    p.q_f16 = q_dtype == LSTK_DTYPE_F16;
+    p.block_tables = block_tables;
+    p.max_blocks = max_blocks_per_seq;
+    p.seq_lens = seq_lens;
+    p.n_seqs = n_seqs;
+    p.n_head = n_head;
+    p.n_head_kv = hkv;
+    p.group = group;
+    p.n_hg = n_hg;
+    p.n_pages = layout->n_cells / layout->block_size;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.lse_out = lse_out;
+    p.prefix = reinterpret_cast<int32_t *>(ws);
+    p.part_lse = reinterpret_cast<float *>(ws + decode_ws_prefix_bytes(n_seqs));
+    p.part_o = reinterpret_cast<float *>(ws + decode_ws_prefix_bytes(n_seqs) + kDecodePartLseBytes);
+    p.status = dev->status;
+
+    const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
+                        16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
+    if (dev->decode_smem < smem) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(decode::decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
+        dev->decode_smem = smem;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    decode::decode_split_kernel<<<(unsigned) grid, decode::kThreads, smem, s>>>(kmap, vmap, p);
+    if ((rc = launch_check("decode_split_kernel"))) return rc;
+
+    decode::CombineParams c;
+    c.n_seqs = n_seqs;
+    c.n_head = n_head;
+    c.n_head_kv = hkv;
+    c.group = group;
+    c.n_hg = n_hg;
+    c.grid = (int) grid;
+    c.prefix = p.prefix;
+    c.part_o = p.part_o;
+    c.part_lse = p.part_lse;
+    c.out = out;
+    c.lse_out = lse_out;
+    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg), 256, 0, s>>>(c);
+    return launch_check("decode_combine_kernel");
+}
+
+int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
+                         int32_t head_dim, float *out, float *lse_out, void *stream) {
+    if (!o_parts || !lse_parts || !out || n_parts <= 0 || n_rows < 0 || head_dim <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_merge: bad arguments");
+    if (n_rows == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(o_parts, &dev);
+    if (rc) return rc;
+    const int64_t blocks = (n_rows + 7) / 8;
+    decode::lse_merge_kernel<<<(unsigned) blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        o_parts, lse_parts, n_parts, n_rows, head_dim, out, lse_out);
+    return launch_check("lse_merge_kernel");
+}
+
+size_t lstk_cuda_attn_prefill_workspace_size(int64_t total_tokens, int32_t n_head, int32_t head_dim,
+                                             int32_t q_dtype) {
+    if (total_tokens < 0 || n_head <= 0 || head_dim <= 0) return 0;
+    if (q_dtype == LSTK_DTYPE_F16) return 0;
+    return align_up((size_t) total_tokens * n_head * head_dim * 2, 256);
+}
+
+int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                           int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *q_seq_start,
+                           int32_t max_q_len, int64_t total_tokens, const int32_t *q_pos0, const int32_t *kv_lens,
+                           const int32_t *block_tables, int32_t max_blocks_per_seq, float scale, float *out,
+                           void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_layout(layout, "lstk_cuda_attn_prefill");
+    if (rc) return rc;
+    const int hkv = layout->n_head_kv;
+    if (n_seqs < 0 || n_head <= 0 || n_head % hkv != 0 || max_blocks_per_seq <= 0 || max_q_len < 0 ||
+        total_tokens < 0 || total_tokens > (int64_t) INT32_MAX)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill: bad sizes");
+    const int group = n_head / hkv;
+    if (group > 8 || prefill::kBM % group != 0)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_prefill: n_head / n_head_kv must be 1, 2, 4 or 8");
+    if (q_dtype != LSTK_DTYPE_F16 && q_dtype != LSTK_DTYPE_F32)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_prefill: q_dtype must be f16 or f32");
+    if (!k_cache || !v_cache || !q || !q_seq_start || !q_pos0 || !kv_lens || !block_tables || !out)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill: NULL pointer");
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16) || !aligned(out, 16))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill: misaligned pointer");
+    if (workspace_bytes < lstk_cuda_attn_prefill_workspace_size(total_tokens, n_head, layout->head_dim, q_dtype) ||
+        (q_dtype == LSTK_DTYPE_F32 && (!workspace || !aligned(workspace, 256))))
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: workspace too small or misaligned");
+    if (n_seqs == 0 || total_tokens == 0 || max_q_len == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(k_cache, &dev))) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    const void *q16 = q;
+    if (q_dtype == LSTK_DTYPE_F32) {
+        const int64_t n = total_tokens * n_head * layout->head_dim;
+        const int64_t blocks = std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t) dev->n_sms * 8);
+        prefill::q_to_f16_kernel<<<(unsigned) blocks, 256, 0, s>>>(static_cast<const float *>(q),
+                                                                    static_cast<__half *>(workspace), n);
+        if ((rc = launch_check("q_to_f16_kernel"))) return rc;
+        q16 = workspace;
+    }
+
+    CUtensorMap qmap, kmap, vmap;
+    const int tpt = prefill::kBM / group;
+    if ((rc = encode_f16_3d(&qmap, q16, 128, n_head, total_tokens, 64, group, tpt))) return rc;
+    if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+    if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+
+    prefill::Params p;
+    p.n_seqs = n_seqs;
+    p.n_head = n_head;
+    p.n_head_kv = hkv;
+    p.group = group;
+    p.n_qt = (max_q_len + tpt - 1) / tpt;
+    p.q_seq_start = q_seq_start;
+    p.q_pos0 = q_pos0;
+    p.kv_lens = kv_lens;
+    p.block_tables = block_tables;
+    p.max_blocks = max_blocks_per_seq;
+    p.n_pages = layout->n_cells / layout->block_size;
+    p.n_cells = layout->n_cells;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.status = dev->status;
+    const int64_t grid = (int64_t) n_seqs * p.n_qt * hkv;
+    if (grid > (int64_t) INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: grid too large");
+    if (!dev->prefill_attr) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   prefill::kSmemBytes);
+        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(prefill)", e));
+        dev->prefill_attr = true;
+    }
+    prefill::prefill_kernel<<<(unsigned) grid, prefill::kThreads, prefill::kSmemBytes, s>>>(qmap, kmap, vmap, p);
+    return launch_check("prefill_kernel");
+}
+
+}  // extern "C"

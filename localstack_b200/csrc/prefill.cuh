@@ -1,0 +1,469 @@
+// prefill.cuh - paged causal flash-attention for prompt chunks on the tcgen05 tensor cores.
+//
+// Replaces flash_attn_ext for n_tokens > 1 (src/qwen3.cpp:155-167), where QK^T and PV are real
+// dense contractions: per 128x128 tile pair, 2 x 128x128x128 MACs on f16 operands.
+//
+// Tiling. A work item is (sequence b, query tile qt, KV head kvh). Its 128 query rows are
+// 128/G consecutive tokens x the G = n_head/n_head_kv query heads that share KV head kvh,
+// row r = token (r / G), head kvh*G + r % G. Packing the GQA group into the M dimension lets
+// one K/V tile feed all G heads in the same MMA. A TMA map over q [T][n_head][128] with box
+// (64, G, 128/G) loads exactly that row order. K/V tiles are 128 keys = 4 pages, each page
+// fetched by TMA through the block table (box (64, 1, 32), 128-byte swizzle).
+//
+// Pipeline (one CTA per SM: 192 KiB of shared memory, 512 TMEM columns):
+//   warp 4  TMA producer: Q once, then K_j / V_j into double buffers.
+//   warp 5  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
+//           waiting for softmax j, so the tensor core computes the next scores while the
+//           softmax warps work; then O += P_j V_j with P_j from shared memory.
+//   warps 0-3  softmax: thread r owns row r (TMEM lane r): loads S_j, applies the causal mask,
+//           online max / exp2 / sum, rescales its O row in TMEM when the max moved, writes P_j
+//           (f16) into shared memory in the MMA operand layout. Epilogue: O / l -> f32 out.
+// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (f32, 128 lanes = 128 rows).
+//
+// Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
+//   Q, K, P: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
+//   V: the B operand of PV with N = head dim contiguous ("MN-major"): sub-tile h holds dims
+//      64h..64h+63 of all 128 keys; LBO = 16 KiB between the two dim halves, SBO = 1 KiB
+//      between groups of 8 keys.
+#pragma once
+
+#include "common.cuh"
+
+namespace lstk {
+namespace prefill {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kD = 128;
+constexpr int kPage = 32;
+constexpr int kTile = kBM * kD * 2;  // 32 KiB
+constexpr int kSub = kTile / 2;      // 16 KiB: 128 rows x 128 B
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+
+// Shared memory carve-up (offsets from a 1024-aligned base).
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTile;       // 2 buffers
+constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
+constexpr int kOffP = kOffV + 2 * kTile;
+constexpr int kOffBar = kOffP + kTile;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
+
+struct Params {
+    int n_seqs, n_head, n_head_kv, group, n_qt;
+    const int32_t *q_seq_start;
+    const int32_t *q_pos0;
+    const int32_t *kv_lens;
+    const int32_t *block_tables;
+    int max_blocks;
+    int64_t n_pages;
+    int64_t n_cells;
+    float scale_log2;
+    float *out;
+    DeviceStatus *status;
+};
+
+struct Barriers {
+    uint64_t q_full;
+    uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
+    uint64_t s_full[2];
+    uint64_t p_full;
+    uint64_t o_done;
+    uint64_t mma_drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+// ---- tcgen05 wrappers ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float v[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory descriptor: start address, leading/stride byte offsets, sm100 version bit,
+// 128-byte swizzle layout.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t) ((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t) ((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t) ((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t) 1 << 46;
+    d |= (uint64_t) 2 << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::f16: f32 accumulator, f16 A and B, M = 128, N = 128.
+constexpr uint32_t idesc_f16(bool b_mn_major) {
+    return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t) (kBN >> 3) << 17) | ((uint32_t) (kBM >> 4) << 24);
+}
+
+extern __shared__ __align__(1024) uint8_t dyn_smem[];
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap vmap,
+                                                              const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+
+    // Heaviest tiles (latest query positions) are launched first.
+    const int x = blockIdx.x;
+    const int kvh = x % p.n_head_kv;
+    const int rest = x / p.n_head_kv;
+    const int b = rest % p.n_seqs;
+    const int qt = p.n_qt - 1 - rest / p.n_seqs;
+    const int G = p.group;
+    const int tpt = kBM / G;  // tokens per query tile
+    const int q_begin = p.q_seq_start[b];
+    const int n_q = p.q_seq_start[b + 1] - q_begin;
+    const int tok0 = qt * tpt;
+    if (tok0 >= n_q) return;  // uniform across the CTA, before any barrier or TMEM use
+    const int kv_len = max(0, min(p.kv_lens[b], p.max_blocks * kPage));
+    const int pos0 = p.q_pos0[b];
+    const int last_tok = min(tok0 + tpt, n_q) - 1;
+    const int n_keys = max(0, min(kv_len, pos0 + last_tok + 1));
+    const int n_tiles = (n_keys + kBN - 1) / kBN;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+    Barriers *bars = reinterpret_cast<Barriers *>(base + kOffBar);
+    const uint32_t sQ = smem_u32(base + kOffQ);
+    const uint32_t sK = smem_u32(base + kOffK);
+    const uint32_t sV = smem_u32(base + kOffV);
+    const uint32_t sP = smem_u32(base + kOffP);
+    volatile int *abort_flag = &bars->abort;
+
+    if (threadIdx.x == 0) {
+        bars->abort = 0;
+        mbar_init(smem_u32(&bars->q_full), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&bars->k_full[i]), 1);
+            mbar_init(smem_u32(&bars->v_full[i]), 1);
+            mbar_init(smem_u32(&bars->k_empty[i]), 1);
+            mbar_init(smem_u32(&bars->v_empty[i]), 1);
+            mbar_init(smem_u32(&bars->s_full[i]), 1);
+        }
+        mbar_init(smem_u32(&bars->p_full), 4);  // one arrival per softmax warp
+        mbar_init(smem_u32(&bars->o_done), 1);
+        mbar_init(smem_u32(&bars->mma_drain), 1);
+        fence_barrier_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 4) {
+        // ---- TMA producer ----
+        if (lane == 0 && n_tiles > 0) {
+            prefetch_tensormap(&qmap);
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            const int32_t *bt = p.block_tables + (int64_t) b * p.max_blocks;
+            mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
+            for (int h = 0; h < 2; h++)
+                tma_load_3d(sQ + h * kSub, &qmap, smem_u32(&bars->q_full), h * 64, kvh * G, q_begin + tok0);
+            int n_k = 0, n_v = 0;  // K and V tiles issued
+            bool ok = true;
+            for (int j = 0; j < n_tiles && ok; j++) {
+                const int buf = j & 1;
+                const uint32_t use = (uint32_t) (j >> 1);
+                int cell0[4];
+                for (int q = 0; q < 4; q++) {
+                    const int pi = j * 4 + q;
+                    cell0[q] = (int) p.n_cells;  // out of bounds: TMA fills zeros
+                    if (pi * kPage < n_keys) {
+                        const int32_t pid = bt[pi];
+                        if (pid >= 0 && pid < p.n_pages) cell0[q] = pid * kPage;
+                        else report(p.status, kStatusBadIndex, kSitePrefillPage, pid);
+                    }
+                }
+                if (use > 0) ok = mbar_wait_bounded(smem_u32(&bars->k_empty[buf]), (use - 1) & 1, abort_flag);
+                if (!ok) break;
+                mbar_arrive_expect_tx(smem_u32(&bars->k_full[buf]), kTile);
+                for (int q = 0; q < 4; q++)
+                    for (int h = 0; h < 2; h++)
+                        tma_load_3d(sK + buf * kTile + h * kSub + q * (kPage * 128), &kmap,
+                                    smem_u32(&bars->k_full[buf]), h * 64, kvh, cell0[q]);
+                n_k++;
+                if (use > 0) ok = mbar_wait_bounded(smem_u32(&bars->v_empty[buf]), (use - 1) & 1, abort_flag);
+                if (!ok) break;
+                mbar_arrive_expect_tx(smem_u32(&bars->v_full[buf]), kTile);
+                for (int q = 0; q < 4; q++)
+                    for (int h = 0; h < 2; h++)
+                        tma_load_3d(sV + buf * kTile + h * kSub + q * (kPage * 128), &vmap,
+                                    smem_u32(&bars->v_full[buf]), h * 64, kvh, cell0[q]);
+                n_v++;
+            }
+            if (!ok) {
+                report(p.status, kStatusTimeout, kSitePrefillWait, 4);
+                *abort_flag = 1;
+            }
+            if (*abort_flag) {
+                // Drain: every load still in flight lands before shared memory is released.
+                mbar_wait_bounded(smem_u32(&bars->q_full), 0, nullptr);
+                for (int j = max(0, n_k - 2); j < n_k; j++)
+                    mbar_wait_bounded(smem_u32(&bars->k_full[j & 1]), (uint32_t) (j >> 1) & 1, nullptr);
+                for (int j = max(0, n_v - 2); j < n_v; j++)
+                    mbar_wait_bounded(smem_u32(&bars->v_full[j & 1]), (uint32_t) (j >> 1) & 1, nullptr);
+            }
+        }
+    } else if (warp == 5) {
+        // ---- MMA issuer ----
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_qk = idesc_f16(false);
+            constexpr uint32_t idesc_pv = idesc_f16(true);
+            bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag);
+            auto issue_qk = [&](int j) -> bool {
+                const int buf = j & 1;
+                if (!mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag))
+                    return false;
+                tc_fence_after();
+                const uint32_t d = tmem + (buf ? kColS1 : kColS0);
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t off = (uint32_t) ((kk >> 2) * kSub + (kk & 3) * 32);
+                    mma_f16_ss(d, sdesc_sw128(sQ + off, 16, 1024), sdesc_sw128(sK + buf * kTile + off, 16, 1024),
+                               idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(smem_u32(&bars->s_full[buf]));
+                mma_commit(smem_u32(&bars->k_empty[buf]));
+                return true;
+            };
+            if (ok) ok = issue_qk(0);
+            for (int j = 0; ok && j < n_tiles; j++) {
+                if (j + 1 < n_tiles && !issue_qk(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                const int buf = j & 1;
+                if (!mbar_wait_bounded(smem_u32(&bars->p_full), (uint32_t) j & 1, abort_flag) ||
+                    !mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t aoff = (uint32_t) ((kk >> 2) * kSub + (kk & 3) * 32);
+                    const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
+                    mma_f16_ss(tmem + kColO, sdesc_sw128(sP + aoff, 16, 1024),
+                               sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(smem_u32(&bars->o_done));
+                mma_commit(smem_u32(&bars->v_empty[buf]));
+            }
+            if (!ok) {
+                report(p.status, kStatusTimeout, kSitePrefillWait, 5);
+                *abort_flag = 1;
+            }
+            // Every MMA issued so far completes before TMEM can be released.
+            mma_commit(smem_u32(&bars->mma_drain));
+            mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
+        }
+    } else {
+        // ---- softmax warps 0..3: thread r owns query row r ----
+        const int r = threadIdx.x;
+        const uint32_t lane_base = tmem + ((uint32_t) (warp * 32) << 16);
+        const int tq = tok0 + r / G;  // query token index within the sequence
+        const int head = kvh * G + r % G;
+        const int qpos = pos0 + tq;
+        const int row_keys = min(kv_len, qpos + 1);  // keys [0, row_keys) are visible
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; j++) {
+            const int buf = j & 1;
+            // Warp-uniform outcomes: tcgen05.ld / st below are warp-collective.
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait_bounded(smem_u32(&bars->s_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[128];
+#pragma unroll
+            for (int c = 0; c < 4; c++) tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + c * 32, s + c * 32);
+            tmem_wait_ld();
+            const int kbase = j * kBN;
+            float tmax = -INFINITY;
+            if (kbase + kBN <= row_keys) {
+#pragma unroll
+                for (int c = 0; c < 128; c++) {
+                    s[c] *= p.scale_log2;
+                    tmax = fmaxf(tmax, s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 128; c++) {
+                    s[c] = (kbase + c < row_keys) ? s[c] * p.scale_log2 : -INFINITY;
+                    tmax = fmaxf(tmax, s[c]);
+                }
+            }
+            const float m_new = fmaxf(m, tmax);
+            const float mu = m_new == -INFINITY ? 0.f : m_new;
+            const float alpha = fast_exp2(m - mu);
+            float rs = 0.f;
+            uint32_t pk[64];
+#pragma unroll
+            for (int c = 0; c < 64; c++) {
+                const float a = fast_exp2(s[2 * c] - mu);
+                const float bb = fast_exp2(s[2 * c + 1] - mu);
+                rs += a + bb;
+                pk[c] = pack_half2(a, bb);
+            }
+            // P_{j-1} consumed and O updated by PV_{j-1} before P_j / the rescale are written.
+            if (j > 0) {
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (j - 1) & 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        float o[32];
+                        tmem_ld32(lane_base + kColO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] *= alpha;
+                        tmem_st32(lane_base + kColO + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // P row r into the K-major swizzled operand tile (two 64-key sub-tiles).
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const uint32_t addr = sP + h * kSub + sw128_offset((uint32_t) r, (uint32_t) c);
+                    const int w0 = h * 32 + c * 4;
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[w0]),
+                                 "r"(pk[w0 + 1]), "r"(pk[w0 + 2]), "r"(pk[w0 + 3])
+                                 : "memory");
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
+            l = l * alpha + rs;
+            m = m_new;
+        }
+        // Epilogue: O / l for this row.
+        if (ok && n_tiles > 0)
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (n_tiles - 1) & 1, abort_flag));
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) {
+            report(p.status, kStatusTimeout, kSitePrefillWait, warp);
+            *abort_flag = 1;
+        }
+        tc_fence_after();
+        const bool live = tq < n_q;
+        float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            float o[32];
+            if (n_tiles > 0 && ok) {
+                tmem_ld32(lane_base + kColO + c * 32, o);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) o[i] = 0.f;
+            }
+            if (live) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4 *>(dst + c * 32 + i) =
+                        make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 5) tmem_dealloc(tmem, kTmemCols);
+}
+
+// f32 -> f16 copy of q for the tensor-core path (when the caller passes f32 queries).
+__global__ void q_to_f16_kernel(const float *src, __half *dst, int64_t n) {
+    for (int64_t i = ((int64_t) blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n;
+         i += (int64_t) gridDim.x * blockDim.x * 4) {
+        if (i + 3 < n) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + i);
+            *reinterpret_cast<__half2 *>(dst + i) = __floats2half2_rn(v.x, v.y);
+            *reinterpret_cast<__half2 *>(dst + i + 2) = __floats2half2_rn(v.z, v.w);
+        } else {
+            for (int64_t k = i; k < n; k++) dst[k] = __float2half_rn(src[k]);
+        }
+    }
+}
+
+}  // namespace prefill
+}  // namespace lstk

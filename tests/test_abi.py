@@ -1,0 +1,105 @@
+"""The C-ABI library loads, exports every function its headers declare, and rejects bad
+arguments with the documented status codes before touching a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import localstack_b200 as L
+from localstack_b200 import _lib
+
+INCLUDE = os.path.join(_lib.ROOT, "include")
+
+
+def _declared(header):
+    with open(os.path.join(INCLUDE, header)) as f:
+        return sorted(set(re.findall(r"\b(lstk_[a-z0-9_]+)\s*\(", f.read())))
+
+
+def test_every_declared_symbol_is_exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r" T (lstk_\w+)", out.stdout))
+    for header in sorted(os.listdir(INCLUDE)):
+        if header.endswith(".h"):
+            missing = [s for s in _declared(header) if s not in exported]
+            assert not missing, f"{header}: not exported: {missing}"
+    lib = L.lib()
+    for s in _declared("lstk_cuda_attn.h"):
+        assert hasattr(lib, s)
+
+
+def test_library_is_built_for_sm100a_only():
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", _lib.LIB_PATH], capture_output=True,
+                         text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    assert "sm_100a" in out.stdout
+
+
+def _layout(n_cells=64, hkv=8, hd=128, bs=32):
+    return _lib.KvLayout(n_cells, hkv, hd, bs)
+
+
+NULL = None
+
+
+def test_validation_errors_without_gpu():
+    lib = L.lib()
+    fake = ctypes.c_void_p(0x10000)  # never dereferenced: validation fails first
+    lay = _layout()
+    # head_dim other than 128 is unsupported
+    rc = lib.lstk_cuda_attn_decode(ctypes.byref(_layout(hd=64)), fake, fake, fake, 0, 1, 16, fake, 1, fake, 0, 0.1,
+                                   fake, NULL, fake, 1 << 30, 0, NULL)
+    assert rc == _lib.LSTK_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
+    # GQA group above 8
+    rc = lib.lstk_cuda_attn_decode(ctypes.byref(_layout(hkv=1)), fake, fake, fake, 0, 1, 16, fake, 1, fake, 0, 0.1,
+                                   fake, NULL, fake, 1 << 30, 0, NULL)
+    assert rc == _lib.LSTK_ERR_UNSUPPORTED
+    # workspace too small
+    rc = lib.lstk_cuda_attn_decode(ctypes.byref(lay), fake, fake, fake, 0, 4, 16, fake, 1, fake, 0, 0.1, fake, NULL,
+                                   fake, 16, 0, NULL)
+    assert rc == _lib.LSTK_ERR_CAPACITY
+    # null layout, null pointers, n_head not a multiple of n_head_kv
+    assert lib.lstk_cuda_attn_decode(None, fake, fake, fake, 0, 1, 16, fake, 1, fake, 0, 0.1, fake, NULL, fake,
+                                     1 << 30, 0, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_attn_decode(ctypes.byref(lay), NULL, fake, fake, 0, 1, 16, fake, 1, fake, 0, 0.1, fake, NULL,
+                                     fake, 1 << 30, 0, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_attn_decode(ctypes.byref(lay), fake, fake, fake, 0, 1, 12, fake, 1, fake, 0, 0.1, fake, NULL,
+                                     fake, 1 << 30, 0, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    # kv_append: bad dtype, short stride, unaligned pointer
+    args = lambda dt=0, qs=16 * 128, ptr=fake: (ctypes.byref(lay), ptr, fake, fake, fake, fake, dt, qs, 8 * 128,
+                                                8 * 128, 1, 16, fake, fake, NULL, NULL, 1e-6, fake, 10, fake, 0, NULL)
+    assert lib.lstk_cuda_kv_append(*args(dt=1)) == _lib.LSTK_ERR_UNSUPPORTED
+    assert lib.lstk_cuda_kv_append(*args(qs=100)) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_kv_append(*args(ptr=ctypes.c_void_p(0x10002))) == _lib.LSTK_ERR_INVALID_ARG
+    # prefill: GQA group 3 cannot tile 128 rows
+    rc = lib.lstk_cuda_attn_prefill(ctypes.byref(_layout(hkv=4)), fake, fake, fake, 1, 1, 12, fake, 1, 1, fake, fake,
+                                    fake, 1, 0.1, fake, NULL, 0, NULL)
+    assert rc == _lib.LSTK_ERR_UNSUPPORTED
+    # merge: no parts
+    assert lib.lstk_cuda_attn_merge(fake, fake, 0, 1, 128, fake, NULL, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    # a zero-sized call is a no-op that succeeds without a device
+    rc = lib.lstk_cuda_kv_append(ctypes.byref(lay), fake, fake, fake, fake, fake, 0, 16 * 128, 8 * 128, 8 * 128, 0, 16,
+                                 fake, fake, NULL, NULL, 1e-6, fake, 10, fake, 0, NULL)
+    assert rc == _lib.LSTK_OK
+
+
+def test_workspace_sizes():
+    lib = L.lib()
+    a = lib.lstk_cuda_attn_decode_workspace_size(64, 32, 4, 128)
+    b = lib.lstk_cuda_attn_decode_workspace_size(4096, 32, 4, 128)
+    assert 0 < a < b
+    assert lib.lstk_cuda_attn_prefill_workspace_size(2048, 16, 128, _lib.DTYPE_F16) == 0
+    assert lib.lstk_cuda_attn_prefill_workspace_size(2048, 16, 128, _lib.DTYPE_F32) == 2048 * 16 * 128 * 2
+
+
+def test_rope_table_host_fill():
+    t = L.rope_table_host(4).numpy()
+    assert t.shape == (4, 64, 2)
+    assert np.all(t[0, :, 0] == 1.0) and np.all(t[0, :, 1] == 0.0)
+    lib = L.lib()
+    assert lib.lstk_rope_table_fill(None, 4, 128, 1e6, 1.0) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_rope_table_bytes(4, 128) == 4 * 64 * 2 * 4

@@ -1,0 +1,116 @@
+"""K/V append (QK-RMSNorm + NEOX RoPE + f16 set_rows) on the GPU vs the CPU oracle: bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import localstack_b200 as L
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(T, Hq, Hkv, n_cells, positions, cells, dtype="f32", gamma=True, seed=0, q_out_dtype=torch.float32,
+         fused_rows=False):
+    rng = np.random.default_rng(seed)
+    D = 128
+    if fused_rows:
+        # One [T][(Hq + 2 Hkv) * D] projection output, passed as three strided views.
+        qkv = rng.standard_normal((T, (Hq + 2 * Hkv) * D), dtype=np.float32) * 3
+        q_in, k_in, v_in = (qkv[:, :Hq * D].reshape(T, Hq, D), qkv[:, Hq * D:(Hq + Hkv) * D].reshape(T, Hkv, D),
+                            qkv[:, (Hq + Hkv) * D:].reshape(T, Hkv, D))
+    else:
+        q_in = rng.standard_normal((T, Hq, D), dtype=np.float32) * 3
+        k_in = rng.standard_normal((T, Hkv, D), dtype=np.float32) * 3
+        v_in = rng.standard_normal((T, Hkv, D), dtype=np.float32) * 3
+    qg = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32) if gamma else None
+    kg = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32) if gamma else None
+    if dtype == "bf16":
+        to_bits = lambda a: (torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).view(torch.int16).numpy()
+                             .view(np.uint16))
+        q_h, k_h, v_h = to_bits(q_in), to_bits(k_in), to_bits(v_in)
+    else:
+        q_h, k_h, v_h = q_in, k_in, v_in
+    kc_ref = np.zeros((n_cells, Hkv, D), np.uint16)
+    vc_ref = np.zeros((n_cells, Hkv, D), np.uint16)
+    q_ref = O.kv_append(q_h, k_h, v_h, positions, cells, kc_ref, vc_ref, qg, kg, 1e-6, 1e6, 1.0, in_dtype=dtype)
+
+    dev = "cuda"
+    if fused_rows:
+        qkv_t = torch.from_numpy(qkv).to(dev)
+        if dtype == "bf16":
+            qkv_t = qkv_t.to(torch.bfloat16)
+        q_t, k_t, v_t = qkv_t[:, :Hq * D], qkv_t[:, Hq * D:(Hq + Hkv) * D], qkv_t[:, (Hq + Hkv) * D:]
+    else:
+        tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+        q_t, k_t, v_t = (torch.from_numpy(a).to(dev).to(tdt) for a in (q_in, k_in, v_in))
+    kc = L.alloc_cache(n_cells, Hkv, dev)
+    vc = L.alloc_cache(n_cells, Hkv, dev)
+    rope = L.rope_table(int(max(positions)) + 1, dev)
+    pos_t = torch.from_numpy(np.asarray(positions, np.int32)).to(dev)
+    cells_t = torch.from_numpy(np.asarray(cells, np.int64)).to(dev)
+    qg_t = torch.from_numpy(qg).to(dev) if gamma else None
+    kg_t = torch.from_numpy(kg).to(dev) if gamma else None
+    q_out = L.kv_append(kc, vc, q_t, k_t, v_t, pos_t, cells_t, rope, qg_t, kg_t, 1e-6, q_out_dtype=q_out_dtype)
+    L.check_status()
+    kc_gpu = kc.cpu().view(torch.int16).numpy().view(np.uint16)
+    vc_gpu = vc.cpu().view(torch.int16).numpy().view(np.uint16)
+    return q_out.float().cpu().numpy(), kc_gpu, vc_gpu, q_ref, kc_ref, vc_ref
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_append_prefill_chunk_bit_exact(dtype):
+    # Config-2 shape: 2048 tokens, Hq 16 / Hkv 8, scattered into 64 seeded pages.
+    rng = np.random.default_rng(1)
+    T, n_pages = 2048, 64 + 3
+    perm = rng.permutation(n_pages)[:64]
+    pos = np.arange(T, dtype=np.int32)
+    cells = (perm[pos // 32] * 32 + pos % 32).astype(np.int64)
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 16, 8, n_pages * 32, pos, cells, dtype=dtype)
+    assert np.array_equal(kc, kc_ref), "K pages differ"
+    assert np.array_equal(vc, vc_ref), "V pages differ"
+    assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32)), "Q out differs"
+
+
+def test_append_long_positions_and_fused_rows():
+    # Positions up to 131071 (config 4), 30B-A3B heads, QKV as strided views of one projection.
+    rng = np.random.default_rng(2)
+    T = 97
+    pos = np.sort(rng.choice(131072, T, replace=False)).astype(np.int32)
+    cells = rng.permutation(4096 * 32)[:T].astype(np.int64)
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 32, 4, 4096 * 32, pos, cells, fused_rows=True, seed=3)
+    assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
+    assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32))
+
+
+def test_append_no_gamma_and_f16_q_out():
+    rng = np.random.default_rng(4)
+    T = 33
+    pos = np.arange(500, 500 + T, dtype=np.int32)
+    cells = rng.permutation(64)[:T].astype(np.int64)
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 16, 8, 64, pos, cells, gamma=False, q_out_dtype=torch.float16)
+    assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
+    assert np.array_equal(q.astype(np.float16), q_ref.astype(np.float16))
+
+
+def test_append_single_token_decode_step():
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(1, 32, 4, 1024, np.array([512], np.int32), np.array([777], np.int64))
+    assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
+    assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32))
+
+
+def test_append_bad_cell_reports_device_index():
+    dev = "cuda"
+    kc = L.alloc_cache(64, 8, dev)
+    vc = L.alloc_cache(64, 8, dev)
+    q = torch.randn(2, 16, 128, device=dev)
+    k = torch.randn(2, 8, 128, device=dev)
+    v = torch.randn(2, 8, 128, device=dev)
+    rope = L.rope_table(16, dev)
+    pos = torch.tensor([0, 1], dtype=torch.int32, device=dev)
+    cells = torch.tensor([3, 64], dtype=torch.int64, device=dev)  # 64 is out of range
+    L.kv_append(kc, vc, q, k, v, pos, cells, rope)
+    with pytest.raises(L.LstkError) as e:
+        L.check_status()
+    assert e.value.code == -6
+    L.check_status()  # status is cleared once read
+    assert torch.count_nonzero(kc[3]) > 0  # the valid token was still written

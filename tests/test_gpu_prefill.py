@@ -1,0 +1,106 @@
+"""Paged causal prefill (tcgen05 tensor cores) on the GPU vs the CPU oracle.
+
+Tolerance (north star): |gpu - oracle_exact| <= 2e-3 + 1e-2 * |oracle_exact| on f32 outputs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import localstack_b200 as L
+from oracle import oracle as O
+from tests.helpers import max_err, random_cache, random_q, scattered_block_tables, within
+
+pytestmark = pytest.mark.gpu
+SCALE = 1.0 / math.sqrt(128)
+DEV = "cuda"
+
+
+def _f16(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(DEV).view(torch.float16)
+
+
+def _prefill_case(q_lens, ctx_before, Hq, Hkv, seed, q_dtype=torch.float16, ggml_check=False):
+    """Sequence b has ctx_before[b] cached tokens and q_lens[b] new query tokens (already in the
+    cache, as kv_append runs before attention). Returns (gpu, oracle_exact[, oracle_ggml])."""
+    rng = np.random.default_rng(seed)
+    kv_lens = [c + t for c, t in zip(ctx_before, q_lens)]
+    bt, n_pages = scattered_block_tables(rng, kv_lens)
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    total = int(sum(q_lens))
+    q = random_q(rng, total, Hq)
+    q16 = q.astype(np.float16)
+    starts = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    q_t = torch.from_numpy(q16).to(DEV) if q_dtype == torch.float16 else torch.from_numpy(q).to(DEV)
+    out = L.attn_prefill(_f16(kc), _f16(vc), q_t, torch.from_numpy(starts).to(DEV),
+                         torch.tensor(ctx_before, dtype=torch.int32, device=DEV),
+                         torch.tensor(kv_lens, dtype=torch.int32, device=DEV), torch.from_numpy(bt).to(DEV),
+                         max(q_lens), SCALE)
+    L.check_status()
+    q_seq = np.concatenate([np.full(n, b, np.int32) for b, n in enumerate(q_lens)])
+    q_pos = np.concatenate([np.arange(c, c + n, dtype=np.int32) for c, n in zip(ctx_before, q_lens)])
+    qr = q16.astype(np.float32)
+    ex = O.paged_attn(qr, q_seq, q_pos, kc, vc, bt, kv_lens, SCALE, causal=True, mode=O.MODE_EXACT)
+    res = [out.cpu().numpy(), ex]
+    if ggml_check:
+        res.append(O.paged_attn(qr, q_seq, q_pos, kc, vc, bt, kv_lens, SCALE, causal=True, mode=O.MODE_GGML))
+    return res
+
+
+def test_config2_prefill_2048():
+    # Config 2: one 2048-token prompt, Hq 16 / Hkv 8, pages scattered, causal.
+    out, ex = _prefill_case([2048], [0], 16, 8, seed=2)
+    assert within(out, ex), max_err(out, ex)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(32, 4), (16, 8), (8, 8), (32, 8), (16, 2)])
+def test_group_sizes_and_ragged_tiles(Hq, Hkv):
+    out, ex = _prefill_case([1, 77, 300], [0, 0, 0], Hq, Hkv, seed=Hq + Hkv)
+    assert within(out, ex), max_err(out, ex)
+
+
+def test_chunked_prefill_with_prior_context_30b_shape():
+    # Config-5 style: prefill chunks of 512 tokens behind existing context, batched.
+    out, ex, gg = _prefill_case([512, 512, 200, 512], [0, 512, 1000, 33], 32, 4, seed=5, ggml_check=True)
+    assert within(out, ex), max_err(out, ex)
+    gap = np.abs(ex.astype(np.float64) - gg)
+    assert np.all(np.abs(out.astype(np.float64) - gg) <= gap + 2e-3 + 1e-2 * np.abs(gg))
+
+
+def test_f32_query_input():
+    out, ex = _prefill_case([129, 64], [5, 0], 16, 8, seed=8, q_dtype=torch.float32)
+    assert within(out, ex), max_err(out, ex)
+
+
+def test_chunked_equals_single_prefill():
+    # The reference splits long prompts into n_batch chunks (src/engine.cpp:254-264); attention of
+    # the chunks over the growing cache must equal one pass over the whole prompt.
+    rng = np.random.default_rng(13)
+    T, Hq, Hkv = 1100, 16, 8
+    bt, n_pages = scattered_block_tables(rng, [T])
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    q16 = random_q(rng, T, Hq).astype(np.float16)
+    k_t, v_t, bt_t = _f16(kc), _f16(vc), torch.from_numpy(bt).to(DEV)
+    q_t = torch.from_numpy(q16).to(DEV)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=DEV)
+    whole = L.attn_prefill(k_t, v_t, q_t, i32(0, T), i32(0), i32(T), bt_t, T, SCALE)
+    parts = []
+    for a, b in [(0, 512), (512, 1024), (1024, T)]:
+        parts.append(L.attn_prefill(k_t, v_t, q_t[a:b].contiguous(), i32(0, b - a), i32(a), i32(b), bt_t, b - a,
+                                    SCALE))
+    chunked = torch.cat(parts)
+    L.check_status()
+    assert within(chunked.cpu().numpy(), whole.cpu().numpy(), atol=1e-5, rtol=1e-5)
+
+
+def test_bad_page_reports_device_index():
+    kc = L.alloc_cache(128, 8, DEV)
+    vc = L.alloc_cache(128, 8, DEV)
+    q = torch.randn(40, 16, 128, device=DEV).half()
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=DEV)
+    bt = torch.tensor([[1, 9]], dtype=torch.int32, device=DEV)  # page 9 >= 4 pages
+    L.attn_prefill(kc, vc, q, i32(0, 40), i32(0), i32(40), bt, 40, SCALE)
+    with pytest.raises(L.LstkError) as e:
+        L.check_status()
+    assert e.value.code == -6
