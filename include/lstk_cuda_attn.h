@@ -115,6 +115,25 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
                           float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
                           void *stream);
 
+/* ---- Paged decode with no caller workspace (no counterpart in the reference) ----------------
+ * Same computation, arguments and results as lstk_cuda_attn_decode, minus the workspace: the
+ * split-K scratch is a fixed array compiled into this library (about 5.3 MiB, held on every
+ * device that loads the library until the process exits). It is for callers that cannot
+ * allocate device memory at the point where they decode - an engine whose memory is all handed
+ * to its own pool up front, code running where cudaMalloc is not allowed or would stall the
+ * pipeline, or a plain C/FFI host that only owns the tensors it passes in. This call allocates
+ * nothing. Limits: n_seqs <= 1024 and n_ctas <= 160 (0 = one CTA per SM); larger requests fail
+ * with LSTK_ERR_CAPACITY. The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. All calls on a device
+ * share the one array and it keeps the previous call's contents (nothing in it needs to start at
+ * zero), so calls whose kernels overlap on the GPU - different streams without ordering between
+ * them - race and give wrong results; order them on one stream. */
+int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                 const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                 const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                 int32_t max_seq_len, float scale, float *out, float *lse_out, int32_t n_ctas,
+                                 void *stream);
+
 /* ---- Log-sum-exp merge of partial results over disjoint key ranges --------------------------
  * Used when one long context is split across GPUs (each GPU runs lstk_cuda_attn_decode over its
  * contiguous chunk of pages with lse_out). o_parts [n_parts][n_rows][head_dim] f32 (each

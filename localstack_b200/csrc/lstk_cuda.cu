@@ -401,3 +401,139 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode without caller-provided workspace.
+//
+// Some hosts of this backend cannot call cudaMalloc when they want to run a decode step: an
+// inference engine that hands all device memory to its own pool at start-up, a caller running
+// inside a context where allocation is forbidden or would synchronise, or an embedding through a
+// plain C FFI that only owns the tensors it passes in. For them the split-K scratch of the decode
+// kernel lives in a fixed array inside this library instead of a caller buffer.
+//
+// Scratch layout (the same as lstk_cuda_attn_decode's workspace, for at most
+// kStaticMaxSeqs sequences and kStaticMaxCtas CTAs): a page prefix of (n_seqs + 1) int32, then
+// per-CTA partial log-sum-exp values and partial outputs. Nothing in it has to start at zero:
+// every entry the combine kernel reads is written earlier in the same call.
+namespace lstk {
+namespace {
+
+constexpr int kStaticMaxSeqs = 1024;
+constexpr int kStaticMaxCtas = 160;
+constexpr size_t kStaticPrefixBytes = sizeof(int32_t) * (kStaticMaxSeqs + 1 + 63);  // 256-byte multiple
+constexpr size_t kStaticLseBytes = sizeof(float) * kStaticMaxCtas * 2 * decode::kPartRows;
+constexpr size_t kStaticOBytes = sizeof(float) * kStaticMaxCtas * 2 * decode::kPartRows * decode::kD;
+constexpr size_t kStaticScratchBytes = kStaticPrefixBytes + kStaticLseBytes + kStaticOBytes;  // ~5.3 MiB
+static_assert(kStaticPrefixBytes % 256 == 0, "prefix region must keep the next regions aligned");
+
+// Loaded onto every device that uses this library and kept until the process exits. In host
+// code this name is only a stand-in: its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
+
+uint8_t *g_decode_scratch_ptr[kMaxDevices] = {};
+
+}  // namespace
+}  // namespace lstk
+
+extern "C" {
+
+int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                 const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                 const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                 int32_t max_seq_len, float scale, float *out, float *lse_out, int32_t n_ctas,
+                                 void *stream) {
+    int rc = check_layout(layout, "lstk_cuda_attn_decode_static");
+    if (rc) return rc;
+    const int hkv = layout->n_head_kv;
+    if (n_seqs < 0 || n_head <= 0 || n_head % hkv != 0 || max_blocks_per_seq <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_static: bad n_seqs / n_head / max_blocks");
+    if (n_seqs > kStaticMaxSeqs)
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode_static: at most 1024 sequences per call "
+                                            "(the built-in scratch is sized for that); use lstk_cuda_attn_decode "
+                                            "with a workspace for larger batches");
+    if (n_ctas > kStaticMaxCtas)
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode_static: at most 160 CTAs");
+    const int group = n_head / hkv;
+    if (group > decode::kMaxGroup)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode_static: n_head / n_head_kv must be at most 8");
+    if (q_dtype != LSTK_DTYPE_F32 && q_dtype != LSTK_DTYPE_F16)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode_static: q_dtype must be f32 or f16");
+    if (!k_cache || !v_cache || !q || !block_tables || !seq_lens || !out)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_static: NULL pointer");
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16) || !aligned(out, 16))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_static: misaligned pointer");
+    if (max_seq_len <= 0 || max_seq_len > max_blocks_per_seq * layout->block_size)
+        max_seq_len = max_blocks_per_seq * layout->block_size;
+    if (n_seqs == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(k_cache, &dev))) return rc;
+
+    // First call on this device (which bind_device made current): resolve the array's device
+    // address once.
+    const int dev_id = t_last_device;
+    if (g_decode_scratch_ptr[dev_id] == nullptr) {
+        void *addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaGetSymbolAddress(decode scratch)", e));
+        g_decode_scratch_ptr[dev_id] = static_cast<uint8_t *>(addr);
+    }
+    uint8_t *ws = g_decode_scratch_ptr[dev_id];
+
+    CUtensorMap kmap, vmap;
+    if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+    if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+
+    const int n_hg = (hkv + decode::kHeadsPerGroup - 1) / decode::kHeadsPerGroup;
+    const int64_t max_groups = (int64_t) n_seqs * n_hg * ((max_seq_len + decode::kPage - 1) / decode::kPage);
+    int64_t grid = n_ctas > 0 ? n_ctas : dev->n_sms;
+    grid = std::max<int64_t>(1, std::min<int64_t>({grid, max_groups, (int64_t) kStaticMaxCtas}));
+
+    decode::Params p;
+    p.q = q;
+    p.q_f16 = q_dtype == LSTK_DTYPE_F16;
+    p.block_tables = block_tables;
+    p.max_blocks = max_blocks_per_seq;
+    p.seq_lens = seq_lens;
+    p.n_seqs = n_seqs;
+    p.n_head = n_head;
+    p.n_head_kv = hkv;
+    p.group = group;
+    p.n_hg = n_hg;
+    p.n_pages = layout->n_cells / layout->block_size;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.lse_out = lse_out;
+    p.prefix = reinterpret_cast<int32_t *>(ws);
+    p.part_lse = reinterpret_cast<float *>(ws + kStaticPrefixBytes);
+    p.part_o = reinterpret_cast<float *>(ws + kStaticPrefixBytes + kStaticLseBytes);
+    p.status = dev->status;
+
+    const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
+                        16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
+    if (dev->decode_smem < smem) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(decode::decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
+        dev->decode_smem = smem;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    decode::decode_split_kernel<<<(unsigned) grid, decode::kThreads, smem, s>>>(kmap, vmap, p);
+    if ((rc = launch_check("decode_split_kernel"))) return rc;
+
+    decode::CombineParams c;
+    c.n_seqs = n_seqs;
+    c.n_head = n_head;
+    c.n_head_kv = hkv;
+    c.group = group;
+    c.n_hg = n_hg;
+    c.grid = (int) grid;
+    c.prefix = p.prefix;
+    c.part_o = p.part_o;
+    c.part_lse = p.part_lse;
+    c.out = out;
+    c.lse_out = lse_out;
+    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg), 256, 0, s>>>(c);
+    return launch_check("decode_combine_kernel");
+}
+
+}  // extern "C"
