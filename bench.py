@@ -43,10 +43,10 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def draw_workload(seed):
-    """Context lengths and page placement of one 64-sequence batch (host side, seeded)."""
+def draw_workload(seed, n_seqs=None):
+    """Context lengths of one batch (host side, seeded); 64 sequences = config 3."""
     rng = np.random.default_rng(seed)
-    ctx = rng.integers(CTX_LO, CTX_HI + 1, N_SEQS).astype(np.int64)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, n_seqs or N_SEQS).astype(np.int64)
     return rng, ctx
 
 
@@ -54,10 +54,11 @@ def step_bytes(ctx):
     """Algorithmic HBM bytes of one decode step: K+V of ctx+1 keys per sequence (read), Q (f32)
     and O (f32), block-table entries, plus the append (q/k/v f32 in, q f32 out, K/V f16 out)."""
     keys = ctx + 1
+    B = len(ctx)
     kv = int(np.sum(keys)) * HKV * D * 2 * 2
-    qo = N_SEQS * HQ * D * 4 * 2
-    tables = int(np.sum((keys + PAGE - 1) // PAGE)) * 4 + N_SEQS * 4
-    append = N_SEQS * ((HQ + 2 * HKV) * D * 4 + HQ * D * 4 + 2 * HKV * D * 2)
+    qo = B * HQ * D * 4 * 2
+    tables = int(np.sum((keys + PAGE - 1) // PAGE)) * 4 + B * 4
+    append = B * ((HQ + 2 * HKV) * D * 4 + HQ * D * 4 + 2 * HKV * D * 2)
     return kv + qo + tables + append, kv + qo + tables
 
 
@@ -112,27 +113,27 @@ class ClockSampler:
 # B200 arm
 
 
-def build_device_workload(seed, dev):
+def build_device_workload(seed, dev, n_seqs=N_SEQS):
     import torch
 
     import localstack_b200 as L
     from localstack_b200.kv_cache import KvCache
 
-    rng, ctx = draw_workload(seed)
+    rng, ctx = draw_workload(seed, n_seqs)
     need = (ctx + 1 + PAGE - 1) // PAGE
     n_pages = int(need.sum())
     # Pages handed out through the bookkeeping allocator seeded with a permuted free list, as
     # KvCache::alloc would scatter them (src/kv_cache.cpp:59-83).
     kv = KvCache(n_pages * PAGE)
     kv.set_free_blocks(rng.permutation(n_pages).astype(np.uint32))
-    for b in range(N_SEQS):
+    for b in range(n_seqs):
         kv.alloc(b, int(ctx[b]))
-    cells = np.empty(N_SEQS, np.int64)
-    pos = np.empty(N_SEQS, np.int32)
-    for b in range(N_SEQS):
+    cells = np.empty(n_seqs, np.int64)
+    pos = np.empty(n_seqs, np.int32)
+    for b in range(n_seqs):
         c, p = kv.alloc(b, 1)  # the decode step's new token
         cells[b], pos[b] = c[0], p[0]
-    bt, lens = kv.block_tables(np.arange(N_SEQS))
+    bt, lens = kv.block_tables(np.arange(n_seqs))
     g = torch.Generator(device=dev).manual_seed(seed)
     kc = torch.randn((n_pages * PAGE, HKV, D), generator=g, device=dev, dtype=torch.float32)
     kc = (kc * torch.rsqrt(kc.square().mean(-1, keepdim=True) + 1e-6)).half()
@@ -140,18 +141,18 @@ def build_device_workload(seed, dev):
     w = {
         "ctx": ctx, "bt_host": bt, "lens_host": lens, "cells_host": cells, "pos_host": pos,
         "kc": kc, "vc": vc,
-        "q_in": torch.randn((N_SEQS, HQ, D), generator=g, device=dev),
-        "k_in": torch.randn((N_SEQS, HKV, D), generator=g, device=dev),
-        "v_in": torch.randn((N_SEQS, HKV, D), generator=g, device=dev),
+        "q_in": torch.randn((n_seqs, HQ, D), generator=g, device=dev),
+        "k_in": torch.randn((n_seqs, HKV, D), generator=g, device=dev),
+        "v_in": torch.randn((n_seqs, HKV, D), generator=g, device=dev),
         "gamma": torch.ones(D, device=dev),
         "rope": L.rope_table(int(ctx.max()) + 2, dev),
         "bt": torch.from_numpy(bt).to(dev), "lens": torch.from_numpy(lens).to(dev),
         "cells": torch.from_numpy(cells).to(dev), "pos": torch.from_numpy(pos).to(dev),
         "max_len": int(lens.max()),
     }
-    w["q_out"] = torch.empty((N_SEQS, HQ, D), device=dev)
-    w["out"] = torch.empty((N_SEQS, HQ, D), device=dev)
-    w["ws"] = L.DecodeWorkspace(N_SEQS, HQ, HKV, dev)
+    w["q_out"] = torch.empty((n_seqs, HQ, D), device=dev)
+    w["out"] = torch.empty((n_seqs, HQ, D), device=dev)
+    w["ws"] = L.DecodeWorkspace(n_seqs, HQ, HKV, dev)
     return w
 
 
@@ -198,13 +199,13 @@ def cpu_baseline_sample(w, budget_s=12.0):
     t1 = run(np.array(sel))
     per_tok = t1 / float(lens[0])
     n = 1
-    while n < N_SEQS and per_tok * float(lens[:n + 1].sum()) < budget_s:
+    while n < len(lens) and per_tok * float(lens[:n + 1].sum()) < budget_s:
         n += 1
     idx = np.arange(n)
     dt = run(idx)
     kv_bytes = float(np.sum(lens[idx].astype(np.int64))) * HKV * D * 2 * 2
     return {"value": kv_bytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} of the 64 config-3 sequences ({int(lens[idx].sum())} keys), one decode step, "
+            "sample": f"{n} of the {len(lens)} config-3 sequences ({int(lens[idx].sum())} keys), one decode step, "
                       f"{dt:.2f} s, K/V bytes only"}
 
 
@@ -228,7 +229,7 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
 
-    w = build_device_workload(SEED + rank, dev)
+    w = build_device_workload(SEED + rank, dev, args.seqs)
     total_bytes, read_bytes = step_bytes(w["ctx"])
     stream = torch.cuda.current_stream()
 
@@ -309,10 +310,10 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
             "data": "synthetic (seeded; ctx U[1024,32768]; K RMS-normed N(0,1), V N(0,1))",
             "config": {"workload": "config 3: batched paged decode step (kv_append + split-K decode)",
-                       "n_seqs_per_gpu": N_SEQS, "n_head": HQ, "n_head_kv": HKV, "head_dim": D, "page": PAGE,
+                       "n_seqs_per_gpu": args.seqs, "n_head": HQ, "n_head_kv": HKV, "head_dim": D, "page": PAGE,
                        "mean_ctx": float(w["ctx"].mean()), "parallelism": f"dp{world} (sequence sharding)",
                        "l2": "KV inputs 2.2 GB per GPU > 126 MB L2, no flush"},
-            "tokens_per_s": round(N_SEQS * world / (ms_max / 1e3), 1),
+            "tokens_per_s": round(args.seqs * world / (ms_max / 1e3), 1),
             "roofline": {"bound": "hbm", "kernel": "decode_split_kernel + decode_combine_kernel",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} hbm_gbs",
@@ -514,6 +515,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true", help="skip configs 1, 2 and 4")
+    ap.add_argument("--seqs", type=int, default=N_SEQS, help="sequences per GPU (64 = config 3)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

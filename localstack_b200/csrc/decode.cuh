@@ -437,63 +437,81 @@ struct CombineParams {
     float *lse_out;
 };
 
-// One CTA per segment (b, hg); thread = (row of the 4x8 partial block, 16-dim slice).
-__global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams p) {
+// One CTA per (sequence b, head group hg, KV head w of the group, query head n of its group):
+// the 128 dims of one output row. The row's partial pieces (one per CTA whose range touched the
+// segment; up to gridDim of the split kernel for a single long sequence) are spread over the 4
+// warps, lanes own 4 dims each, and block reductions give the log-sum-exp weights.
+constexpr int kCombineThreads = 128;
+
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const CombineParams p) {
     const int b = blockIdx.x, hg = blockIdx.y;
-    const int row = threadIdx.x >> 3;
-    const int d0 = (threadIdx.x & 7) * 16;
-    const int w = row / kMaxGroup, n = row % kMaxGroup;
+    const int w = blockIdx.z / kMaxGroup, n = blockIdx.z % kMaxGroup;
     const int kvh = hg * kHeadsPerGroup + w;
     if (kvh >= p.n_head_kv || n >= p.group) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t out_row = (int64_t) b * p.n_head + (int64_t) kvh * p.group + n;
     const int32_t pb = p.prefix[b];
     const int np = p.prefix[b + 1] - pb;
     if (np == 0) {
-        for (int d = 0; d < 16; d++) p.out[out_row * kD + d0 + d] = 0.f;
-        if (d0 == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
+        p.out[out_row * kD + tid] = 0.f;
+        if (tid == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
         return;
     }
     const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
     const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
     const int c0 = cta_of(x0, P, p.grid);
     const int c1 = cta_of(x0 + np - 1, P, p.grid);
-    if (c0 == c1) return;
-    // CTAs between c0 and c1 whose range is empty (more CTAs than page-groups) wrote nothing.
-    float M = -INFINITY;
-    for (int c = c0; c <= c1; c++) {
-        if (range_lo(c + 1, P, p.grid) <= range_lo(c, P, p.grid)) continue;
-        const int slot = range_lo(c, P, p.grid) < x0 ? 1 : 0;
-        M = fmaxf(M, p.part_lse[((int64_t) c * 2 + slot) * kPartRows + w * kMaxGroup + n]);
+    if (c0 == c1) return;  // the split kernel wrote this row directly
+    const int part_row = w * kMaxGroup + n;
+    // Piece of CTA c for this segment: its slot (1 if the CTA's range began in an earlier
+    // segment), or -1 when the CTA's range is empty (more CTAs than page-groups).
+    auto slot_of = [&](int c) -> int {
+        const int64_t lo = range_lo(c, P, p.grid);
+        if (range_lo(c + 1, P, p.grid) <= lo) return -1;
+        return lo < x0 ? 1 : 0;
+    };
+    __shared__ float red[kCombineThreads / 32];
+    __shared__ float acc_s[kCombineThreads / 32][kD];
+    float mx = -INFINITY;
+    for (int c = c0 + tid; c <= c1; c += kCombineThreads) {
+        const int slot = slot_of(c);
+        if (slot >= 0) mx = fmaxf(mx, p.part_lse[((int64_t) c * 2 + slot) * kPartRows + part_row]);
     }
-    float acc[16];
-#pragma unroll
-    for (int d = 0; d < 16; d++) acc[d] = 0.f;
+    mx = warp_max_xor(mx, 1);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+    for (int i = 1; i < kCombineThreads / 32; i++) M = fmaxf(M, red[i]);
+    __syncthreads();
+    // Weighted sum: warp k takes pieces k, k+4, ...; lane owns dims 4*lane .. 4*lane+3.
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float den = 0.f;
     if (M != -INFINITY) {
-        for (int c = c0; c <= c1; c++) {
-            if (range_lo(c + 1, P, p.grid) <= range_lo(c, P, p.grid)) continue;
-            const int slot = range_lo(c, P, p.grid) < x0 ? 1 : 0;
-            const int64_t prow = ((int64_t) c * 2 + slot) * kPartRows + w * kMaxGroup + n;
+#pragma unroll 4
+        for (int c = c0 + warp; c <= c1; c += kCombineThreads / 32) {
+            const int slot = slot_of(c);
+            if (slot < 0) continue;
+            const int64_t prow = ((int64_t) c * 2 + slot) * kPartRows + part_row;
             const float wt = exp2f(p.part_lse[prow] - M);
+            const float4 v = reinterpret_cast<const float4 *>(p.part_o + prow * kD)[lane];
             den += wt;
-            const float4 *src = reinterpret_cast<const float4 *>(p.part_o + prow * kD + d0);
-#pragma unroll
-            for (int q4 = 0; q4 < 4; q4++) {
-                const float4 v = src[q4];
-                acc[4 * q4 + 0] += wt * v.x;
-                acc[4 * q4 + 1] += wt * v.y;
-                acc[4 * q4 + 2] += wt * v.z;
-                acc[4 * q4 + 3] += wt * v.w;
-            }
+            acc.x += wt * v.x;
+            acc.y += wt * v.y;
+            acc.z += wt * v.z;
+            acc.w += wt * v.w;
         }
     }
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    float4 *dst = reinterpret_cast<float4 *>(p.out + out_row * kD + d0);
-#pragma unroll
-    for (int q4 = 0; q4 < 4; q4++)
-        dst[q4] = make_float4(acc[4 * q4] * inv, acc[4 * q4 + 1] * inv, acc[4 * q4 + 2] * inv, acc[4 * q4 + 3] * inv);
-    if (d0 == 0 && p.lse_out != nullptr)
-        p.lse_out[out_row] = den > 0.f ? (M + __log2f(den)) * 0.69314718055994531f : -INFINITY;
+    reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    float total = 0.f, o = 0.f;
+    for (int i = 0; i < kCombineThreads / 32; i++) {
+        total += red[i];
+        o += acc_s[i][tid];
+    }
+    p.out[out_row * kD + tid] = total > 0.f ? o / total : 0.f;
+    if (tid == 0 && p.lse_out != nullptr)
+        p.lse_out[out_row] = total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY;
 }
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.

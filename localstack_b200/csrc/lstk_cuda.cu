@@ -303,7 +303,8 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
     c.part_lse = p.part_lse;
     c.out = out;
     c.lse_out = lse_out;
-    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg), 256, 0, s>>>(c);
+    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg, decode::kPartRows),
+                                    decode::kCombineThreads, 0, s>>>(c);
     return launch_check("decode_combine_kernel");
 }
 
@@ -532,7 +533,8 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     c.part_lse = p.part_lse;
     c.out = out;
     c.lse_out = lse_out;
-    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg), 256, 0, s>>>(c);
+    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg, decode::kPartRows),
+                                    decode::kCombineThreads, 0, s>>>(c);
     return launch_check("decode_combine_kernel");
 }
 
