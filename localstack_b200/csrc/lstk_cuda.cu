@@ -175,7 +175,7 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
         v_row_stride < (int64_t) layout->n_head_kv * hd || q_row_stride % 4 || k_row_stride % 4 || v_row_stride % 4)
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: row strides too small or not multiples of 4");
     if (!aligned(q_in, 16) || !aligned(k_in, 16) || !aligned(v_in, 16) || !aligned(q_out, 16) ||
-        !aligned(k_cache, 16) || !aligned(v_cache, 16))
+        !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(rope_table, 16))
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: pointers must be 16-byte aligned");
     if (n_tokens == 0) return clear_error();
     DeviceInfo *dev = nullptr;
