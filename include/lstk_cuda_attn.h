@@ -152,9 +152,13 @@ int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n
  *                (converted into the workspace first)
  *   q_seq_start  [n_seqs + 1] int32 device; max_q_len = host upper bound of any sequence's rows
  *   out          [total_tokens][n_head][head_dim] f32
- * Computed with tcgen05 tensor-core MMAs (f16 x f16 -> f32 in tensor memory) on 128-token tiles
- * fed by TMA from the scattered pages. n_head / n_head_kv must be 1..8. */
-size_t lstk_cuda_attn_prefill_workspace_size(int64_t total_tokens, int32_t n_head, int32_t head_dim, int32_t q_dtype);
+ * Computed with tcgen05 tensor-core MMAs (f16 x f16 -> f32 in tensor memory) on 128-row query
+ * tiles and 128-key tiles fed by TMA from the scattered pages. The workspace is sized by
+ * lstk_cuda_attn_prefill_workspace_size from the same shape arguments (today: the f16 copy of
+ * f32 queries; 0 bytes for f16 queries). n_head / n_head_kv must be 1, 2, 4 or 8. */
+size_t lstk_cuda_attn_prefill_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim,
+                                             int32_t max_q_len, int32_t max_blocks_per_seq, int64_t total_tokens,
+                                             int32_t q_dtype);
 int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
                            int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *q_seq_start,
                            int32_t max_q_len, int64_t total_tokens, const int32_t *q_pos0, const int32_t *kv_lens,

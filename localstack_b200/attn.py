@@ -140,7 +140,8 @@ def attn_prefill(k_cache, v_cache, q, q_seq_start, q_pos0, kv_lens, block_tables
         scale = 1.0 / math.sqrt(HEAD_DIM)
     if out is None:
         out = torch.empty((total, Hq, HEAD_DIM), dtype=torch.float32, device=q.device)
-    need = lib().lstk_cuda_attn_prefill_workspace_size(total, Hq, HEAD_DIM, _DT[q.dtype])
+    need = lib().lstk_cuda_attn_prefill_workspace_size(B, Hq, L.n_head_kv, HEAD_DIM, int(max_q_len),
+                                                       block_tables.shape[1], total, _DT[q.dtype])
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
     check(lib().lstk_cuda_attn_prefill(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B, Hq,

@@ -322,9 +322,15 @@ int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n
     return launch_check("lse_merge_kernel");
 }
 
-size_t lstk_cuda_attn_prefill_workspace_size(int64_t total_tokens, int32_t n_head, int32_t head_dim,
+size_t lstk_cuda_attn_prefill_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim,
+                                             int32_t max_q_len, int32_t max_blocks_per_seq, int64_t total_tokens,
                                              int32_t q_dtype) {
-    if (total_tokens < 0 || n_head <= 0 || head_dim <= 0) return 0;
+    // The launch shape is part of the signature so that a schedule which needs per-launch scratch
+    // (partial results of split KV ranges) can size it; the current kernel needs only the f16
+    // copy of f32 queries.
+    if (n_seqs < 0 || n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || max_q_len < 0 || max_blocks_per_seq < 0 ||
+        total_tokens < 0)
+        return 0;
     if (q_dtype == LSTK_DTYPE_F16) return 0;
     return align_up((size_t) total_tokens * n_head * head_dim * 2, 256);
 }
@@ -349,7 +355,8 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill: NULL pointer");
     if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16) || !aligned(out, 16))
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill: misaligned pointer");
-    if (workspace_bytes < lstk_cuda_attn_prefill_workspace_size(total_tokens, n_head, layout->head_dim, q_dtype) ||
+    if (workspace_bytes < lstk_cuda_attn_prefill_workspace_size(n_seqs, n_head, hkv, layout->head_dim, max_q_len,
+                                                                max_blocks_per_seq, total_tokens, q_dtype) ||
         (q_dtype == LSTK_DTYPE_F32 && (!workspace || !aligned(workspace, 256))))
         return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: workspace too small or misaligned");
     if (n_seqs == 0 || total_tokens == 0 || max_q_len == 0) return clear_error();

@@ -92,8 +92,10 @@ def test_workspace_sizes():
     a = lib.lstk_cuda_attn_decode_workspace_size(64, 32, 4, 128)
     b = lib.lstk_cuda_attn_decode_workspace_size(4096, 32, 4, 128)
     assert 0 < a < b
-    assert lib.lstk_cuda_attn_prefill_workspace_size(2048, 16, 128, _lib.DTYPE_F16) == 0
-    assert lib.lstk_cuda_attn_prefill_workspace_size(2048, 16, 128, _lib.DTYPE_F32) == 2048 * 16 * 128 * 2
+    # f16 queries need no scratch; f32 queries need their f16 copy
+    assert lib.lstk_cuda_attn_prefill_workspace_size(1, 16, 8, 128, 2048, 64, 2048, _lib.DTYPE_F16) == 0
+    assert lib.lstk_cuda_attn_prefill_workspace_size(1, 16, 8, 128, 2048, 64, 2048, _lib.DTYPE_F32) == \
+        2048 * 16 * 128 * 2
 
 
 def test_rope_table_host_fill():
