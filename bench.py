@@ -113,13 +113,16 @@ class ClockSampler:
 # B200 arm
 
 
-def build_device_workload(seed, dev, n_seqs=N_SEQS):
+def build_device_workload(seed, dev, ctx):
+    """Device-resident decode batch for the context lengths `ctx` (this rank's sequences)."""
     import torch
 
     import localstack_b200 as L
     from localstack_b200.kv_cache import KvCache
 
-    rng, ctx = draw_workload(seed, n_seqs)
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, np.int64)
+    n_seqs = len(ctx)
     need = (ctx + 1 + PAGE - 1) // PAGE
     n_pages = int(need.sum())
     # Pages handed out through the bookkeeping allocator seeded with a permuted free list, as
@@ -229,8 +232,19 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
 
-    w = build_device_workload(SEED + rank, dev, args.seqs)
+    # Sequence sharding: one seeded batch of seqs x world sequences, split over the ranks by LPT
+    # on context length; each rank owns its sequences' pages, tables and queries.
+    from localstack_b200.shard import lpt_partition
+
+    _, ctx_all = draw_workload(SEED, args.seqs * world)
+    parts, loads = lpt_partition(ctx_all, world)
+    w = build_device_workload(SEED + 1 + rank, dev, ctx_all[parts[rank]])
     total_bytes, read_bytes = step_bytes(w["ctx"])
+    all_bytes = float(total_bytes)
+    if world > 1:
+        tb = torch.tensor([all_bytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(tb)
+        all_bytes = float(tb[0])
     stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
@@ -298,28 +312,32 @@ def run_b200(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t[0])
 
+    c4_split = config4_split(L, dev, world) if world > 1 and not args.no_secondary else None
+
     hbm_peak, tc_peak, peak_src = peaks()
     achieved = read_bytes / (dec_ms / 1e3) / 1e9  # decode kernel alone, this rank
     line = None
     if rank == 0:
         line = {
             "metric": "paged decode-attn HBM GB/s (config 3, Qwen3-30B-A3B GQA 32/4, 64 seqs/GPU)",
-            "value": round(total_bytes * world / (ms_max / 1e3) / 1e9, 1),
+            "value": round(all_bytes / (ms_max / 1e3) / 1e9, 1),
             "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
             "data": "synthetic (seeded; ctx U[1024,32768]; K RMS-normed N(0,1), V N(0,1))",
             "config": {"workload": "config 3: batched paged decode step (kv_append + split-K decode)",
                        "n_seqs_per_gpu": args.seqs, "n_head": HQ, "n_head_kv": HKV, "head_dim": D, "page": PAGE,
-                       "mean_ctx": float(w["ctx"].mean()), "parallelism": f"dp{world} (sequence sharding)",
+                       "mean_ctx": float(ctx_all.mean()), "parallelism": f"dp{world} (sequence sharding)",
+                       "partition": "LPT by context length", "max_over_mean_tokens": round(
+                           float(loads.max() / loads.mean()), 4),
                        "l2": "KV inputs 2.2 GB per GPU > 126 MB L2, no flush"},
-            "tokens_per_s": round(args.seqs * world / (ms_max / 1e3), 1),
+            "tokens_per_s": round(len(ctx_all) / (ms_max / 1e3), 1),
             "roofline": {"bound": "hbm", "kernel": "decode_split_kernel + decode_combine_kernel",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": read_bytes, "launch_ms": round(dec_ms, 4),
                          "traffic": None},
-            "e2e": {"value": round(total_bytes * world / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "e2e": {"value": round(all_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),
@@ -328,10 +346,39 @@ def run_b200(args):
             line["cpu_baseline"] = cpu_baseline_sample(w)
         if not args.no_secondary:
             line["secondary"] = secondary(L, dev, tc_peak, hbm_peak)
+            if c4_split is not None:
+                line["secondary"]["config4_kv_split"] = c4_split
     barrier()
     if world > 1:
         dist.destroy_process_group()
     return line
+
+
+def graph_time_ms(fn, per_graph=20, replays=10):
+    """Device time of one fn() call, from a CUDA graph holding `per_graph` back-to-back calls
+    (removes the host's launch overhead from latency-bound launches)."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()  # warm on the capture stream
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        for _ in range(per_graph):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(replays):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / (per_graph * replays)
 
 
 def secondary(L, dev, tc_peak, hbm_peak):
@@ -408,7 +455,9 @@ def secondary(L, dev, tc_peak, hbm_peak):
         L.attn_decode(kc1, vc1, q1, bt1, lens1, SCALE, max_seq_len=513, out=o1, workspace=ws1)
     b.record()
     torch.cuda.synchronize()
-    res["config1_decode_us"] = round(a.elapsed_time(b) / 200 * 1e3, 2)
+    res["config1_decode_us_eager"] = round(a.elapsed_time(b) / 200 * 1e3, 2)
+    res["config1_decode_us"] = round(graph_time_ms(
+        lambda: L.attn_decode(kc1, vc1, q1, bt1, lens1, SCALE, max_seq_len=513, out=o1, workspace=ws1)) * 1e3, 2)
     # config 4: one 131072-token context, Hq32/Hkv4, whole context on this GPU
     ctx = 131072
     n4 = ctx // PAGE
@@ -430,11 +479,68 @@ def secondary(L, dev, tc_peak, hbm_peak):
         L.attn_decode(kc4, vc4, q4, bt4, lens4, SCALE, max_seq_len=ctx, out=o4, workspace=ws4)
     b.record()
     torch.cuda.synchronize()
-    ms4 = a.elapsed_time(b) / 50
+    ms4e = a.elapsed_time(b) / 50
+    ms4 = graph_time_ms(lambda: L.attn_decode(kc4, vc4, q4, bt4, lens4, SCALE, max_seq_len=ctx, out=o4, workspace=ws4),
+                        per_graph=10, replays=5)
     gbs4 = ctx * HKV * D * 4 / (ms4 / 1e3) / 1e9
-    res["config4_long_decode"] = {"ms": round(ms4, 4), "gbs": round(gbs4, 1), "frac_hbm": round(gbs4 / hbm_peak, 4)}
+    res["config4_long_decode"] = {"ms": round(ms4, 4), "gbs": round(gbs4, 1), "frac_hbm": round(gbs4 / hbm_peak, 4),
+                                  "ms_eager": round(ms4e, 4), "timing": "CUDA graph of 10 back-to-back decodes"}
     L.check_status()
     return res
+
+
+def config4_split(L, dev, world):
+    """Config 4 over all ranks: one 131072-token context whose pages are split into `world`
+    contiguous chunks (chunk r on rank r); per step every rank decodes its chunk, the [O | lse]
+    records are all-gathered over NCCL and merged on every rank. L2 is flushed before each timed
+    step (a chunk of 268 MB / world can fit in L2); time = max over ranks of the per-step sum."""
+    import torch
+    import torch.distributed as dist
+
+    from localstack_b200.shard import KvSplitDecode, chunk_keys, page_chunks
+
+    rank = dist.get_rank()
+    ctx = 131072
+    s, e = page_chunks(ctx // PAGE, world)[rank]
+    n_local = e - s
+    kc = L.alloc_cache(n_local * PAGE, HKV, dev)
+    vc = L.alloc_cache(n_local * PAGE, HKV, dev)
+    kc.normal_()
+    vc.normal_()
+    bt = torch.from_numpy(np.random.default_rng(4 + rank).permutation(n_local).astype(np.int32)[None]).to(dev)
+    q = torch.randn((1, HQ, D), generator=torch.Generator(device=dev).manual_seed(4), device=dev)
+    keys = torch.tensor([chunk_keys(ctx, s, e)], dtype=torch.int32, device=dev)
+    dec = KvSplitDecode(1, HQ, HKV, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    step = lambda: dec(kc, vc, q, bt, keys, SCALE, max_seq_len=n_local * PAGE)
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    # one step (decode, all_gather, merge) as a CUDA graph, so host launch latency stays out
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    reps = 30
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        g.replay()
+        b.record()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+    del g
+    torch.cuda.synchronize()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    L.check_status()
+    del dec
+    return {"n_gpus": world, "ms": round(ms, 4), "gbs": round(ctx * HKV * D * 4 / (ms / 1e3) / 1e9, 1),
+            "pages_per_rank": n_local, "exchange": "NCCL all_gather of [O | lse] records, LSE merge on every rank",
+            "l2": "flushed before each step", "timing": "CUDA graph of one step, max over ranks"}
 
 
 # ---------------------------------------------------------------------------------------------

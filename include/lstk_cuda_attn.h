@@ -138,9 +138,12 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
  * Used when one long context is split across GPUs (each GPU runs lstk_cuda_attn_decode over its
  * contiguous chunk of pages with lse_out). o_parts [n_parts][n_rows][head_dim] f32 (each
  * normalised by its own softmax sum), lse_parts [n_parts][n_rows] (natural log, -inf = empty).
- * out [n_rows][head_dim]; lse_out optional [n_rows]. */
+ * Part r starts at o_parts + r * o_part_stride and lse_parts + r * lse_part_stride (elements;
+ * 0 = densely packed, n_rows * head_dim and n_rows), so the parts can sit in one gathered buffer
+ * of per-rank records [O | lse]. out [n_rows][head_dim]; lse_out optional [n_rows]. */
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
-                         int32_t head_dim, float *out, float *lse_out, void *stream);
+                         int32_t head_dim, int64_t o_part_stride, int64_t lse_part_stride, float *out,
+                         float *lse_out, void *stream);
 
 /* ---- Paged causal prefill: replaces flash_attn_ext for a chunk of prompt tokens -------------
  * (src/qwen3.cpp:155-167 with n_tokens > 1). Sequence b's query tokens are rows

@@ -89,7 +89,7 @@ def lib():
     L.lstk_cuda_attn_decode_workspace_size.restype = _SZ
     L.lstk_cuda_attn_decode.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _P, _I32, _F, _P, _P, _P, _SZ,
                                         _I32, _P]
-    L.lstk_cuda_attn_merge.argtypes = [_P, _P, _I32, _I64, _I32, _P, _P, _P]
+    L.lstk_cuda_attn_merge.argtypes = [_P, _P, _I32, _I64, _I32, _I64, _I64, _P, _P, _P]
     L.lstk_cuda_attn_prefill_workspace_size.argtypes = [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32]
     L.lstk_cuda_attn_prefill_workspace_size.restype = _SZ
     L.lstk_cuda_attn_prefill.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _F, _P,

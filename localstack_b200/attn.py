@@ -117,13 +117,18 @@ def attn_decode(k_cache, v_cache, q, block_tables, seq_lens, scale=None, max_seq
 def attn_merge(o_parts, lse_parts, out=None, lse_out=None, stream=None):
     """Log-sum-exp merge of partial results over disjoint key ranges.
 
-    o_parts [R][rows][D] f32, lse_parts [R][rows] f32 (natural log). Returns (out, lse)."""
+    o_parts [R][rows][D] f32, lse_parts [R][rows] f32 (natural log); each part's rows are dense,
+    parts may be strided (e.g. views into one gathered buffer of [O | lse] records).
+    Returns (out, lse)."""
     R, rows, D = o_parts.shape
+    if o_parts.stride(2) != 1 or o_parts.stride(1) != D or lse_parts.shape != (R, rows) or lse_parts.stride(1) != 1:
+        raise ValueError("attn_merge: each part must be a dense [rows][D] / [rows] block")
     if out is None:
         out = torch.empty((rows, D), dtype=torch.float32, device=o_parts.device)
     if lse_out is None:
         lse_out = torch.empty((rows,), dtype=torch.float32, device=o_parts.device)
-    check(lib().lstk_cuda_attn_merge(_p(o_parts), _p(lse_parts), R, rows, D, _p(out), _p(lse_out), _stream(stream)))
+    check(lib().lstk_cuda_attn_merge(_p(o_parts), _p(lse_parts), R, rows, D, o_parts.stride(0), lse_parts.stride(0),
+                                     _p(out), _p(lse_out), _stream(stream)))
     return out, lse_out
 
 

@@ -106,7 +106,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA: tiled tensor loads global -> shared, completion counted on an mbarrier (no multicast).
+// TMA: tiled tensor loads global -> shared, completion counted on an mbarrier (single CTA).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
                                             int c2) {
     asm volatile(

@@ -516,12 +516,13 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.
 __global__ void __launch_bounds__(256) lse_merge_kernel(const float *o_parts, const float *lse_parts, int n_parts,
-                                                        int64_t n_rows, int head_dim, float *out, float *lse_out) {
+                                                        int64_t n_rows, int head_dim, int64_t o_stride,
+                                                        int64_t lse_stride, float *out, float *lse_out) {
     const int64_t row = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= n_rows) return;
     float M = -INFINITY;
-    for (int r = 0; r < n_parts; r++) M = fmaxf(M, lse_parts[(int64_t) r * n_rows + row]);
+    for (int r = 0; r < n_parts; r++) M = fmaxf(M, lse_parts[(int64_t) r * lse_stride + row]);
     float den = 0.f;
     for (int d = lane; d < head_dim; d += 32) out[row * head_dim + d] = 0.f;
     if (M == -INFINITY) {
@@ -532,9 +533,9 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const float *o_parts, co
         float acc = 0.f;
         float dn = 0.f;
         for (int r = 0; r < n_parts; r++) {
-            const float wt = __expf(lse_parts[(int64_t) r * n_rows + row] - M);
+            const float wt = __expf(lse_parts[(int64_t) r * lse_stride + row] - M);
             dn += wt;
-            acc += wt * o_parts[((int64_t) r * n_rows + row) * head_dim + d];
+            acc += wt * o_parts[(int64_t) r * o_stride + row * head_dim + d];
         }
         out[row * head_dim + d] = acc / dn;
         den = dn;

@@ -309,16 +309,22 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
-                         int32_t head_dim, float *out, float *lse_out, void *stream) {
-    if (!o_parts || !lse_parts || !out || n_parts <= 0 || n_rows < 0 || head_dim <= 0)
+                         int32_t head_dim, int64_t o_part_stride, int64_t lse_part_stride, float *out,
+                         float *lse_out, void *stream) {
+    if (!o_parts || !lse_parts || !out || n_parts <= 0 || n_rows < 0 || head_dim <= 0 || o_part_stride < 0 ||
+        lse_part_stride < 0)
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_merge: bad arguments");
+    if (o_part_stride == 0) o_part_stride = n_rows * head_dim;
+    if (lse_part_stride == 0) lse_part_stride = n_rows;
+    if (o_part_stride < n_rows * head_dim || lse_part_stride < n_rows)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_merge: part stride smaller than a part");
     if (n_rows == 0) return clear_error();
     DeviceInfo *dev = nullptr;
     int rc = bind_device(o_parts, &dev);
     if (rc) return rc;
     const int64_t blocks = (n_rows + 7) / 8;
     decode::lse_merge_kernel<<<(unsigned) blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        o_parts, lse_parts, n_parts, n_rows, head_dim, out, lse_out);
+        o_parts, lse_parts, n_parts, n_rows, head_dim, o_part_stride, lse_part_stride, out, lse_out);
     return launch_check("lse_merge_kernel");
 }
 

@@ -1,0 +1,99 @@
+"""Multi-GPU sharding of the attention node's decode, one process per GPU (torch.distributed).
+
+The reference runs every layer in one process on one ggml backend (src/engine.cpp:282-298). Its
+attention node shards in two ways, both built here on the single-GPU C ABI:
+
+* Independent sequences (batched decode): sequences go to ranks by LPT - longest context first,
+  each to the least-loaded rank. A rank holds its own sequences' pages, block tables and queries
+  and runs the ordinary decode; nothing crosses GPUs on the data path.
+* One long sequence: its page list is cut into R contiguous chunks, chunk r's pages resident on
+  rank r. Each rank decodes its chunk with lse_out into one record [O (rows x D) | lse (rows)];
+  the records are all-gathered (NCCL on GPUs) and every rank merges them by log-sum-exp with
+  lstk_cuda_attn_merge, reading the parts straight out of the gathered buffer through the
+  merge's part strides. The merged output is therefore replicated on every rank.
+"""
+import heapq
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .attn import HEAD_DIM, DecodeWorkspace, attn_decode, attn_merge
+
+
+def lpt_partition(lengths, world):
+    """Sequences per rank by LPT greedy: longest first (ties: lower index), each to the rank with
+    the least total length so far (ties: lower rank). Returns (list of index arrays, ascending
+    within a rank; int64 array of per-rank total lengths)."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    lengths = np.asarray(lengths, np.int64)
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    heap = [(0, r) for r in range(world)]
+    parts = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        parts[r].append(i)
+        heapq.heappush(heap, (load + int(lengths[i]), r))
+    loads = np.zeros(world, np.int64)
+    for load, r in heap:
+        loads[r] = load
+    return [np.array(sorted(p), np.int64) for p in parts], loads
+
+
+def page_chunks(n_pages, world):
+    """Contiguous [start, end) ranges of a page list, one per rank, sizes differing by at most one."""
+    if world <= 0 or n_pages < 0:
+        raise ValueError("bad page chunking")
+    return [(r * n_pages // world, (r + 1) * n_pages // world) for r in range(world)]
+
+
+def chunk_keys(seq_len, start, end, block_size=32):
+    """Number of the sequence's keys that live in pages [start, end) of its block table."""
+    return max(0, min(seq_len, end * block_size) - start * block_size)
+
+
+def record_views(buf, rows, head_dim=HEAD_DIM):
+    """(O [R][rows][D], lse [R][rows]) views of a buffer of R records [O | lse]."""
+    rec = rows * head_dim + rows
+    g = buf.view(-1, rec)
+    return g[:, :rows * head_dim].view(g.shape[0], rows, head_dim), g[:, rows * head_dim:]
+
+
+def all_gather_records(gathered, local, group=None):
+    """Gather every rank's record into `gathered` ([world * rec], rank order)."""
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(gathered, local, group=group)
+    else:
+        dist.all_gather(list(gathered.view(dist.get_world_size(group), -1).unbind(0)), local, group=group)
+    return gathered
+
+
+class KvSplitDecode:
+    """Decode of sequences whose pages are split over the ranks of `group` in contiguous chunks.
+
+    Every rank calls it with the same n_seqs / n_head; rank r passes its own chunk's block tables
+    and per-sequence key counts (chunk_keys). Returns the merged output [n_seqs][n_head][D] f32,
+    identical on every rank, and keeps the merged natural-log lse in `self.lse`."""
+
+    def __init__(self, n_seqs, n_head, n_head_kv, device, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.n_seqs, self.n_head = n_seqs, n_head
+        self.rows = n_seqs * n_head
+        rec = self.rows * HEAD_DIM + self.rows
+        self.local = torch.empty(rec, dtype=torch.float32, device=device)
+        self.gathered = torch.empty(self.world * rec, dtype=torch.float32, device=device)
+        self.ws = DecodeWorkspace(n_seqs, n_head, n_head_kv, device)
+        self.out = torch.empty((n_seqs, n_head, HEAD_DIM), dtype=torch.float32, device=device)
+        self.lse = torch.empty((n_seqs, n_head), dtype=torch.float32, device=device)
+
+    def __call__(self, k_cache, v_cache, q, block_tables, chunk_lens, scale=None, max_seq_len=0):
+        o_loc, lse_loc = record_views(self.local, self.rows)
+        attn_decode(k_cache, v_cache, q, block_tables, chunk_lens, scale, max_seq_len,
+                    out=o_loc[0].view(self.n_seqs, self.n_head, HEAD_DIM),
+                    lse_out=lse_loc[0].view(self.n_seqs, self.n_head), workspace=self.ws)
+        all_gather_records(self.gathered, self.local, self.group)
+        o_parts, lse_parts = record_views(self.gathered, self.rows)
+        attn_merge(o_parts, lse_parts, out=self.out.view(self.rows, HEAD_DIM), lse_out=self.lse.view(self.rows))
+        return self.out

@@ -80,7 +80,8 @@ def test_validation_errors_without_gpu():
                                     fake, 1, 0.1, fake, NULL, 0, NULL)
     assert rc == _lib.LSTK_ERR_UNSUPPORTED
     # merge: no parts
-    assert lib.lstk_cuda_attn_merge(fake, fake, 0, 1, 128, fake, NULL, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_attn_merge(fake, fake, 0, 1, 128, 0, 0, fake, NULL, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_attn_merge(fake, fake, 2, 4, 128, 100, 0, fake, NULL, NULL) == _lib.LSTK_ERR_INVALID_ARG
     # a zero-sized call is a no-op that succeeds without a device
     rc = lib.lstk_cuda_kv_append(ctypes.byref(lay), fake, fake, fake, fake, fake, 0, 16 * 128, 8 * 128, 8 * 128, 0, 16,
                                  fake, fake, NULL, NULL, 1e-6, fake, 10, fake, 0, NULL)

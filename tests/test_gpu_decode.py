@@ -153,3 +153,52 @@ def test_bad_page_reports_device_index():
     with pytest.raises(L.LstkError) as e:
         L.check_status()
     assert e.value.code == -6
+
+
+def test_append_and_decode_replay_in_cuda_graph():
+    """A decode step (append + split-K decode + combine) captured once in a CUDA graph and
+    replayed gives the eager results bit for bit (no host work inside the entry points)."""
+    rng = np.random.default_rng(17)
+    lens = [700, 33, 1500]
+    Hq, Hkv = 32, 4
+    bt, n_pages = scattered_block_tables(rng, [n + 1 for n in lens])
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    dev = "cuda"
+    f16 = lambda a: torch.from_numpy(a.view(np.int16)).to(dev).view(torch.float16)
+    kc_e, vc_e = f16(kc), f16(vc)
+    kc_g, vc_g = kc_e.clone(), vc_e.clone()
+    B = len(lens)
+    q_in = torch.from_numpy(random_q(rng, B, Hq, normed=False)).to(dev)
+    k_in = torch.from_numpy(random_q(rng, B, Hkv, normed=False)).to(dev)
+    v_in = torch.from_numpy(random_q(rng, B, Hkv, normed=False)).to(dev)
+    pos = torch.tensor(lens, dtype=torch.int32, device=dev)
+    cells = torch.tensor([int(bt[b, lens[b] // 32]) * 32 + lens[b] % 32 for b in range(B)], dtype=torch.int64,
+                         device=dev)
+    rope = L.rope_table(2048, dev)
+    gamma = torch.linspace(0.5, 1.5, 128, device=dev)
+    bt_t = torch.from_numpy(bt).to(dev)
+    kl = torch.tensor([n + 1 for n in lens], dtype=torch.int32, device=dev)
+    ws = L.DecodeWorkspace(B, Hq, Hkv, dev)
+
+    def step(kc_t, vc_t, q_out, out):
+        L.kv_append(kc_t, vc_t, q_in, k_in, v_in, pos, cells, rope, gamma, gamma, 1e-6, q_out=q_out)
+        L.attn_decode(kc_t, vc_t, q_out, bt_t, kl, SCALE, max_seq_len=max(lens) + 1, out=out, workspace=ws)
+
+    q_e, o_e = torch.empty(B, Hq, 128, device=dev), torch.empty(B, Hq, 128, device=dev)
+    step(kc_e, vc_e, q_e, o_e)
+    q_g, o_g = torch.zeros_like(q_e), torch.zeros_like(o_e)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(kc_g, vc_g, q_g, o_g)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(side)
+    o_g.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step(kc_g, vc_g, q_g, o_g)
+    g.replay()
+    torch.cuda.synchronize()
+    L.check_status()
+    assert torch.equal(o_g, o_e) and torch.equal(q_g, q_e)
+    assert torch.equal(kc_g.view(torch.int16), kc_e.view(torch.int16))
+    del g
