@@ -136,6 +136,14 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Programmatic dependent launch. A grid launched with programmatic stream serialization may be
+// scheduled before its predecessor in the stream has finished; pdl_wait() blocks until every
+// grid it depends on has completed and its memory is visible (a no-op for an ordinary launch),
+// so everything a kernel reads from earlier work comes after it. pdl_launch_dependents() lets
+// the next such grid be scheduled now (otherwise that happens when this grid completes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------------------------------------
 // Numerics.
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -252,6 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
     int32_t *pfx = reinterpret_cast<int32_t *>(empty + kStages) + 4;
 
+    // Inputs (q, seq_lens, tables, pages) may come from the previous kernel in the stream; the
+    // combine grid may be scheduled right away (it waits for this grid to complete).
+    pdl_wait();
+    pdl_launch_dependents();
     // Prefix over sequences of page counts (every CTA computes it; CTA 0 publishes it).
     __shared__ int32_t chunk_sum[kThreads];
     {
@@ -439,11 +443,15 @@ struct CombineParams {
 
 // One CTA per (sequence b, head group hg, KV head w of the group, query head n of its group):
 // the 128 dims of one output row. The row's partial pieces (one per CTA whose range touched the
-// segment; up to gridDim of the split kernel for a single long sequence) are spread over the 4
-// warps, lanes own 4 dims each, and block reductions give the log-sum-exp weights.
-constexpr int kCombineThreads = 128;
+// segment; up to gridDim of the split kernel for a single long sequence) are handled in three
+// passes: one thread per piece finds its partial row and lse (the only place the range
+// arithmetic runs), then the weights exp2(lse - M), then the 8 warps sum weighted rows with the
+// loads of several pieces in flight per warp (lanes own 4 dims each).
+constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = kCombineThreads / 32;
 
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const CombineParams p) {
+    pdl_wait();  // the split grid's partials and prefix are complete and visible
     const int b = blockIdx.x, hg = blockIdx.y;
     const int w = blockIdx.z / kMaxGroup, n = blockIdx.z % kMaxGroup;
     const int kvh = hg * kHeadsPerGroup + w;
@@ -453,7 +461,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     const int32_t pb = p.prefix[b];
     const int np = p.prefix[b + 1] - pb;
     if (np == 0) {
-        p.out[out_row * kD + tid] = 0.f;
+        if (tid < kD) p.out[out_row * kD + tid] = 0.f;
         if (tid == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
         return;
     }
@@ -463,55 +471,67 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     const int c1 = cta_of(x0 + np - 1, P, p.grid);
     if (c0 == c1) return;  // the split kernel wrote this row directly
     const int part_row = w * kMaxGroup + n;
-    // Piece of CTA c for this segment: its slot (1 if the CTA's range began in an earlier
-    // segment), or -1 when the CTA's range is empty (more CTAs than page-groups).
-    auto slot_of = [&](int c) -> int {
-        const int64_t lo = range_lo(c, P, p.grid);
-        if (range_lo(c + 1, P, p.grid) <= lo) return -1;
-        return lo < x0 ? 1 : 0;
-    };
-    __shared__ float red[kCombineThreads / 32];
-    __shared__ float acc_s[kCombineThreads / 32][kD];
+    const int n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
+    __shared__ float wt_s[kMaxCtas];
+    __shared__ int row_s[kMaxCtas];
+    __shared__ float red_max[kCombineWarps], red_sum[kCombineWarps];
+    __shared__ float acc_s[kCombineWarps][kD];
+    // Pass 1: piece i = CTA c0 + i. Its slot is 1 if the CTA's range began in an earlier
+    // segment; an empty range (more CTAs than page-groups) contributes nothing.
     float mx = -INFINITY;
-    for (int c = c0 + tid; c <= c1; c += kCombineThreads) {
-        const int slot = slot_of(c);
-        if (slot >= 0) mx = fmaxf(mx, p.part_lse[((int64_t) c * 2 + slot) * kPartRows + part_row]);
+    for (int i = tid; i < n_pc; i += kCombineThreads) {
+        const int c = c0 + i;
+        const int64_t lo = range_lo(c, P, p.grid);
+        int prow = -1;
+        float l = -INFINITY;
+        if (range_lo(c + 1, P, p.grid) > lo) {
+            prow = (c * 2 + (lo < x0 ? 1 : 0)) * kPartRows + part_row;
+            l = p.part_lse[prow];
+        }
+        row_s[i] = prow;
+        wt_s[i] = l;
+        mx = fmaxf(mx, l);
     }
     mx = warp_max_xor(mx, 1);
-    if (lane == 0) red[warp] = mx;
+    if (lane == 0) red_max[warp] = mx;
     __syncthreads();
-    float M = red[0];
-    for (int i = 1; i < kCombineThreads / 32; i++) M = fmaxf(M, red[i]);
-    __syncthreads();
-    // Weighted sum: warp k takes pieces k, k+4, ...; lane owns dims 4*lane .. 4*lane+3.
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = red_max[0];
+    for (int i = 1; i < kCombineWarps; i++) M = fmaxf(M, red_max[i]);
+    // Pass 2: weights (0 for empty pieces or when every piece is empty).
     float den = 0.f;
-    if (M != -INFINITY) {
+    for (int i = tid; i < n_pc; i += kCombineThreads) {
+        const float wv = (row_s[i] >= 0 && M != -INFINITY) ? exp2f(wt_s[i] - M) : 0.f;
+        wt_s[i] = wv;
+        den += wv;
+    }
+    den = warp_sum_xor(den, 1);
+    if (lane == 0) red_sum[warp] = den;
+    __syncthreads();
+    // Pass 3: warp k sums pieces k, k + 8, ...
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-        for (int c = c0 + warp; c <= c1; c += kCombineThreads / 32) {
-            const int slot = slot_of(c);
-            if (slot < 0) continue;
-            const int64_t prow = ((int64_t) c * 2 + slot) * kPartRows + part_row;
-            const float wt = exp2f(p.part_lse[prow] - M);
-            const float4 v = reinterpret_cast<const float4 *>(p.part_o + prow * kD)[lane];
-            den += wt;
-            acc.x += wt * v.x;
-            acc.y += wt * v.y;
-            acc.z += wt * v.z;
-            acc.w += wt * v.w;
+    for (int i = warp; i < n_pc; i += kCombineWarps) {
+        const float wv = wt_s[i];
+        if (wv > 0.f) {
+            const float4 v = reinterpret_cast<const float4 *>(p.part_o + (int64_t) row_s[i] * kD)[lane];
+            acc.x += wv * v.x;
+            acc.y += wv * v.y;
+            acc.z += wv * v.z;
+            acc.w += wv * v.w;
         }
     }
     reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
-    if (lane == 0) red[warp] = den;
     __syncthreads();
-    float total = 0.f, o = 0.f;
-    for (int i = 0; i < kCombineThreads / 32; i++) {
-        total += red[i];
-        o += acc_s[i][tid];
+    if (tid < kD) {
+        float total = 0.f, o = 0.f;
+        for (int i = 0; i < kCombineWarps; i++) {
+            total += red_sum[i];
+            o += acc_s[i][tid];
+        }
+        p.out[out_row * kD + tid] = total > 0.f ? o / total : 0.f;
+        if (tid == 0 && p.lse_out != nullptr)
+            p.lse_out[out_row] = total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY;
     }
-    p.out[out_row * kD + tid] = total > 0.f ? o / total : 0.f;
-    if (tid == 0 && p.lse_out != nullptr)
-        p.lse_out[out_row] = total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY;
 }
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.

@@ -211,6 +211,47 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     return launch_check("kv_append_kernel");
 }
 
+// Launches the split kernel and the combine kernel with programmatic stream serialization:
+// each grid can be scheduled while its predecessor in the stream finishes, and waits for it
+// (pdl_wait) before reading anything it produced.
+static int launch_pdl_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg(what, e));
+    return launch_check(what);
+}
+
+static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const decode::Params &p, int grid,
+                         size_t smem, cudaStream_t s) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3(decode::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int rc = launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_split_kernel, kmap, vmap, p),
+                              "decode_split_kernel");
+    if (rc) return rc;
+    decode::CombineParams c;
+    c.n_seqs = p.n_seqs;
+    c.n_head = p.n_head;
+    c.n_head_kv = p.n_head_kv;
+    c.group = p.group;
+    c.n_hg = p.n_hg;
+    c.grid = grid;
+    c.prefix = p.prefix;
+    c.part_o = p.part_o;
+    c.part_lse = p.part_lse;
+    c.out = p.out;
+    c.lse_out = p.lse_out;
+    cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, decode::kPartRows);
+    cfg.blockDim = dim3(decode::kCombineThreads);
+    cfg.dynamicSmemBytes = 0;
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_kernel, c), "decode_combine_kernel");
+}
+
 size_t lstk_cuda_attn_decode_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim) {
     (void) n_head;
     (void) n_head_kv;
@@ -287,25 +328,7 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
         if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
         dev->decode_smem = smem;
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    decode::decode_split_kernel<<<(unsigned) grid, decode::kThreads, smem, s>>>(kmap, vmap, p);
-    if ((rc = launch_check("decode_split_kernel"))) return rc;
-
-    decode::CombineParams c;
-    c.n_seqs = n_seqs;
-    c.n_head = n_head;
-    c.n_head_kv = hkv;
-    c.group = group;
-    c.n_hg = n_hg;
-    c.grid = (int) grid;
-    c.prefix = p.prefix;
-    c.part_o = p.part_o;
-    c.part_lse = p.part_lse;
-    c.out = out;
-    c.lse_out = lse_out;
-    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg, decode::kPartRows),
-                                    decode::kCombineThreads, 0, s>>>(c);
-    return launch_check("decode_combine_kernel");
+    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
@@ -530,25 +553,7 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
         if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
         dev->decode_smem = smem;
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    decode::decode_split_kernel<<<(unsigned) grid, decode::kThreads, smem, s>>>(kmap, vmap, p);
-    if ((rc = launch_check("decode_split_kernel"))) return rc;
-
-    decode::CombineParams c;
-    c.n_seqs = n_seqs;
-    c.n_head = n_head;
-    c.n_head_kv = hkv;
-    c.group = group;
-    c.n_hg = n_hg;
-    c.grid = (int) grid;
-    c.prefix = p.prefix;
-    c.part_o = p.part_o;
-    c.part_lse = p.part_lse;
-    c.out = out;
-    c.lse_out = lse_out;
-    decode::decode_combine_kernel<<<dim3((unsigned) n_seqs, (unsigned) n_hg, decode::kPartRows),
-                                    decode::kCombineThreads, 0, s>>>(c);
-    return launch_check("decode_combine_kernel");
+    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
