@@ -313,6 +313,16 @@ def run_b200(args):
     e2e_ms = float(t[0])
 
     c4_split = config4_split(L, dev, world) if world > 1 and not args.no_secondary else None
+    c5 = None
+    if not args.no_secondary:
+        # config 5 on every rank (its own continuous batch; weak scaling), slowest rank's time
+        c5 = config5_stack(L, dev)
+        t5 = torch.tensor([c5["ms_per_step"]], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t5, op=dist.ReduceOp.MAX)
+        c5["ms_per_step_max_over_ranks"] = round(float(t5[0]), 3)
+        c5["n_gpus"] = world
+        c5["tokens_per_s_all_gpus"] = round(world * c5["tokens_per_step"] / (float(t5[0]) / 1e3), 1)
 
     hbm_peak, tc_peak, peak_src = peaks()
     achieved = read_bytes / (dec_ms / 1e3) / 1e9  # decode kernel alone, this rank
@@ -348,6 +358,7 @@ def run_b200(args):
             line["secondary"] = secondary(L, dev, tc_peak, hbm_peak)
             if c4_split is not None:
                 line["secondary"]["config4_kv_split"] = c4_split
+            line["secondary"]["config5_stack"] = c5
     barrier()
     if world > 1:
         dist.destroy_process_group()
@@ -487,6 +498,111 @@ def secondary(L, dev, tc_peak, hbm_peak):
                                   "ms_eager": round(ms4e, 4), "timing": "CUDA graph of 10 back-to-back decodes"}
     L.check_status()
     return res
+
+
+def config5_stack(L, dev, n_layers=48, n_pools=16, warmup=1, steps=3, seed=5):
+    """Config 5 on this GPU: one continuous-batching step of a 48-layer Qwen3-30B-A3B attention
+    stack = 8 fresh 512-token prompt chunks + 256 decode sequences (ctx U[512, 16384]) per step.
+    Per layer: input RMSNorm (torch), fused Wqkv projection (cuBLAS bf16 via torch.matmul), kv_append (QK-norm, RoPE,
+    f16 K/V scatter), causal prefill of the chunks and split-K decode of the 256 sequences over
+    the paged cache (this library), Wo projection (cuBLAS) and the residual add. The 48 layers'
+    KV (213 GB) does not fit one GPU: layer l uses KV pool l % n_pools (same page layout, own
+    data); bytes and FLOPs are still counted per layer. Returns timing, tokens/s and the roofline
+    model time (decode KV bytes at HBM peak + projection FLOPs at tensor peak)."""
+    import torch
+
+    from localstack_b200.kv_cache import KvCache
+
+    hidden, n_pre, pre_len, n_dec = 2048, 8, 512, 256
+    rng = np.random.default_rng(seed)
+    dec_ctx = rng.integers(512, 16384 + 1, n_dec).astype(np.int64)
+    n_pages = int(((dec_ctx + 1 + PAGE - 1) // PAGE).sum()) + n_pre * (pre_len // PAGE)
+    kv = KvCache(n_pages * PAGE)
+    kv.set_free_blocks(rng.permutation(n_pages).astype(np.uint32))
+    seqs = list(range(n_pre + n_dec))
+    cells, pos = [], []
+    for i in range(n_pre):  # fresh prompts: positions 0..511
+        c, ps = kv.alloc(i, pre_len)
+        cells.append(c)
+        pos.append(ps)
+    for i in range(n_dec):  # cached context, then this step's token
+        kv.alloc(n_pre + i, int(dec_ctx[i]))
+    for i in range(n_dec):
+        c, ps = kv.alloc(n_pre + i, 1)
+        cells.append(c)
+        pos.append(ps)
+    bt, lens = kv.block_tables(np.array(seqs))
+    T = n_pre * pre_len + n_dec
+    i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
+    cells_t = torch.from_numpy(np.concatenate(cells).astype(np.int64)).to(dev)
+    pos_t = i32(np.concatenate(pos))
+    bt_pre, bt_dec = i32(bt[:n_pre]), i32(bt[n_pre:])
+    lens_dec = i32(lens[n_pre:])
+    starts = i32(np.arange(n_pre + 1) * pre_len)
+    p0, kvl_pre = i32(np.zeros(n_pre)), i32(np.full(n_pre, pre_len))
+    pools = []
+    for _ in range(n_pools):
+        kc, vc = L.alloc_cache(n_pages * PAGE, HKV, dev), L.alloc_cache(n_pages * PAGE, HKV, dev)
+        kc.normal_()
+        vc.normal_()
+        pools.append((kc, vc))
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w_qkv = [torch.randn((hidden, (HQ + 2 * HKV) * D), generator=g, device=dev, dtype=torch.bfloat16) * 0.02
+             for _ in range(n_layers)]
+    w_o = [torch.randn((HQ * D, hidden), generator=g, device=dev, dtype=torch.bfloat16) * 0.02
+           for _ in range(n_layers)]
+    gamma = torch.ones(D, device=dev)
+    rope = L.rope_table(16384 + 2, dev)
+    x0 = torch.randn((T, hidden), generator=g, device=dev, dtype=torch.bfloat16)
+    q16 = torch.empty((T, HQ, D), dtype=torch.float16, device=dev)
+    attn = torch.empty((T, HQ, D), dtype=torch.float32, device=dev)
+    ws_dec = L.DecodeWorkspace(n_dec, HQ, HKV, dev)
+    ws_pre = torch.empty(max(256, L.lib().lstk_cuda_attn_prefill_workspace_size(
+        n_pre, HQ, HKV, D, pre_len, bt.shape[1], n_pre * pre_len, 1)), dtype=torch.uint8, device=dev)
+    n_tok_pre = n_pre * pre_len
+    max_dec = int(lens_dec.max())
+
+    def step():
+        x = x0
+        for layer in range(n_layers):
+            kc, vc = pools[layer % n_pools]
+            # the layer's input RMSNorm (outside the attention node; keeps the residual stream and
+            # so the f16 K/V in range over 48 layers)
+            qkv = torch.nn.functional.rms_norm(x, (hidden,), eps=1e-6) @ w_qkv[layer]
+            L.kv_append(kc, vc, qkv[:, :HQ * D], qkv[:, HQ * D:(HQ + HKV) * D], qkv[:, (HQ + HKV) * D:], pos_t,
+                        cells_t, rope, gamma, gamma, 1e-6, q_out=q16)
+            L.attn_prefill(kc, vc, q16[:n_tok_pre], starts, p0, kvl_pre, bt_pre, pre_len, SCALE,
+                           out=attn[:n_tok_pre], workspace=ws_pre)
+            L.attn_decode(kc, vc, q16[n_tok_pre:], bt_dec, lens_dec, SCALE, max_seq_len=max_dec,
+                          out=attn[n_tok_pre:], workspace=ws_dec)
+            x = x + attn.view(T, HQ * D).to(torch.bfloat16) @ w_o[layer]
+        return x
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        y = step()
+    b.record()
+    torch.cuda.synchronize()
+    L.check_status()
+    ms = a.elapsed_time(b) / steps
+    finite = bool(torch.isfinite(y.float()).all())
+    dec_bytes = float((dec_ctx + 1).sum()) * HKV * D * 2 * 2 * n_layers
+    proj_flops = float(T) * 2 * hidden * ((HQ + 2 * HKV) * D + HQ * D) * n_layers
+    pre_flops = 4.0 * D * HQ * n_pre * pre_len * (pre_len + 1) / 2 * n_layers
+    hbm_peak, tc_peak, _ = peaks()
+    model_ms = (dec_bytes / (hbm_peak * 1e9) + (proj_flops + pre_flops) / (tc_peak * 1e12)) * 1e3
+    del pools
+    torch.cuda.empty_cache()
+    return {"ms_per_step": round(ms, 3), "tokens_per_s": round(T / (ms / 1e3), 1), "tokens_per_step": T,
+            "layers": n_layers, "kv_pools": n_pools, "decode_kv_bytes_per_step": dec_bytes,
+            "projection_gflop_per_step": round(proj_flops / 1e9, 1), "roofline_model_ms": round(model_ms, 3),
+            "frac_of_roofline": round(model_ms / ms, 4), "finite": finite,
+            "note": "projections on cuBLAS (torch.matmul bf16); attention path on this library; "
+                    "layer l reads KV pool l % 16 (213 GB of per-layer KV does not fit one GPU)"}
 
 
 def config4_split(L, dev, world):

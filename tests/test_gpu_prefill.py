@@ -68,6 +68,12 @@ def test_chunked_prefill_with_prior_context_30b_shape():
     assert np.all(np.abs(out.astype(np.float64) - gg) <= gap + 2e-3 + 1e-2 * np.abs(gg))
 
 
+def test_long_ragged_batch():
+    # Sequences of very different lengths (one with no new tokens) and prior context in one call.
+    out, ex = _prefill_case([1100, 0, 40, 700, 1300], [0, 64, 2000, 100, 0], 32, 4, seed=21)
+    assert within(out, ex), max_err(out, ex)
+
+
 def test_f32_query_input():
     out, ex = _prefill_case([129, 64], [5, 0], 16, 8, seed=8, q_dtype=torch.float32)
     assert within(out, ex), max_err(out, ex)
