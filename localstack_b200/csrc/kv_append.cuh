@@ -11,12 +11,14 @@
 //
 // Work decomposition. A "row" is one (token, head) vector of 128 values; rows are numbered
 // token-major: for token t, rows [t*R, t*R + R) with R = Hq + 2*Hkv are Hq query heads, Hkv key
-// heads, Hkv value heads. Each warp takes 32 consecutive rows. Lane l owns elements
+// heads, Hkv value heads. Each warp takes 8 consecutive rows. Lane l owns elements
 // {2l, 2l+1, 64+2l, 65+2l} of every row - exactly its two NEOX pairs - so loads and stores are
-// 8-byte vectors, coalesced across the warp. Rows are staged into shared memory (row stride 129
-// floats) 8 at a time with all loads issued before any store, so a warp has 16 loads in flight
-// instead of one. Lane r then sums row r's squares sequentially in double (conflict-free thanks
-// to the padding), and the warp writes the rows out, lane r's row metadata broadcast by shuffle.
+// 8-byte vectors, coalesced across the warp. The warp's rows are staged into shared memory (row
+// stride 129 floats) with all loads issued before any store, so a warp has 16 loads in flight.
+// Lane r then sums row r's squares sequentially in double (conflict-free thanks to the padding),
+// and the warp writes the rows out, lane r's row metadata broadcast by shuffle. The kernel is
+// latency-bound at decode sizes (a few hundred rows), so the group is kept short: the serial
+// parts per warp are one round of loads, a 128-term double sum and 8 row writes.
 #pragma once
 
 #include "common.cuh"
@@ -25,8 +27,8 @@ namespace lstk {
 namespace append {
 
 constexpr int kD = 128;
-constexpr int kWarps = 2;
-constexpr int kRowsPerWarp = 32;
+constexpr int kWarps = 4;
+constexpr int kRowsPerWarp = 8;
 constexpr int kRowStride = kD + 1;  // padded shared-memory row
 constexpr int kBatch = 8;           // rows whose loads are in flight together
 
@@ -91,6 +93,10 @@ __device__ __forceinline__ __half2 h2(float a, float b) { return __halves2half2(
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
     __shared__ float stage[kWarps][kRowsPerWarp * kRowStride];
 
+    // Inputs may come from the previous kernel in the stream (programmatic dependent launch);
+    // the decode launched after this kernel may be staged right away (it waits for completion).
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int R = p.n_head + 2 * p.n_head_kv;
@@ -126,6 +132,20 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
             my_j = (int) (row0 + lane - my_t * R);
             if (my_j < n_qk) my_pos = p.positions[my_t];
             if (my_j >= p.n_head) my_cell = p.cells[my_t];
+        }
+
+        // RoPE rows of the group's first two tokens, loaded while the rows are staged (a group of
+        // 8 rows spans at most two tokens whenever a token has 8 or more rows, as every Qwen3
+        // shape does; rows of any further token load theirs in the write loop).
+        const int64_t t_first = row0 / R;
+        float4 cs_pre[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            if (t_first + u < p.n_tokens) {
+                const int pos = p.positions[t_first + u];
+                if (pos >= 0 && pos < p.rope_n_pos)
+                    cs_pre[u] = *reinterpret_cast<const float4 *>(p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
+            }
         }
 
         // Stage rows, kBatch at a time: all loads of a batch issued before its stores.
@@ -193,7 +213,9 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
 #pragma unroll
                 for (int e = 0; e < 4; e++) x[e] = __fmul_rn(__fmul_rn(x[e], scale), is_q ? qg[e] : kg[e]);
             }
-            const float4 cs = *reinterpret_cast<const float4 *>(p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
+            const float4 cs = t == t_first       ? cs_pre[0]
+                              : t == t_first + 1 ? cs_pre[1]
+                                                 : *reinterpret_cast<const float4 *>(p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
             // pair (2l, 64+2l) uses (cs.x, cs.y); pair (2l+1, 65+2l) uses (cs.z, cs.w)
             float o[4];
             o[0] = __fsub_rn(__fmul_rn(x[0], cs.x), __fmul_rn(x[2], cs.y));

@@ -133,6 +133,12 @@ constexpr size_t kDecodePartOBytes = sizeof(float) * decode::kMaxCtas * 2 * deco
 
 using namespace lstk;
 
+// A cudaLaunchKernelEx result and any launch error, as a status.
+static int launch_pdl_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg(what, e));
+    return launch_check(what);
+}
+
 extern "C" {
 
 int lstk_cuda_status(void *stream) {
@@ -207,18 +213,21 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     const int64_t rows = (int64_t) n_tokens * (n_head + 2 * layout->n_head_kv);
     const int64_t groups = (rows + append::kRowsPerWarp - 1) / append::kRowsPerWarp;
     const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * 16);
-    append::kv_append_kernel<<<(unsigned) blocks, append::kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    return launch_check("kv_append_kernel");
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) blocks);
+    cfg.blockDim = dim3(append::kWarps * 32);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, append::kv_append_kernel, p), "kv_append_kernel");
 }
 
 // Launches the split kernel and the combine kernel with programmatic stream serialization:
 // each grid can be scheduled while its predecessor in the stream finishes, and waits for it
 // (pdl_wait) before reading anything it produced.
-static int launch_pdl_check(cudaError_t e, const char *what) {
-    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg(what, e));
-    return launch_check(what);
-}
-
 static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const decode::Params &p, int grid,
                          size_t smem, cudaStream_t s) {
     cudaLaunchAttribute attr[1];
