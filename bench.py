@@ -614,9 +614,12 @@ def config5_stack(L, dev, n_layers=48, n_pools=16, warmup=1, steps=3, seed=5):
 
 def config4_split(L, dev, world):
     """Config 4 over all ranks: one 131072-token context whose pages are split into `world`
-    contiguous chunks (chunk r on rank r); per step every rank decodes its chunk, the [O | lse]
-    records are all-gathered over NCCL and merged on every rank. L2 is flushed before each timed
-    step (a chunk of 268 MB / world can fit in L2); time = max over ranks of the per-step sum."""
+    contiguous chunks (chunk r on rank r); per step every rank decodes its chunk and the partials
+    are exchanged and merged on every rank. Timed for both exchanges: "p2p" (one kernel: peer
+    stores into every rank's mailbox over NVLink, flag wait, merge) and "collective" (NCCL
+    all-gather of [O | lse] records + merge kernel). One step is captured in a CUDA graph; L2 is
+    flushed before each step (a chunk of 268 MB / world can fit in L2); time = max over ranks
+    of the mean per-step time."""
     import torch
     import torch.distributed as dist
 
@@ -633,37 +636,47 @@ def config4_split(L, dev, world):
     bt = torch.from_numpy(np.random.default_rng(4 + rank).permutation(n_local).astype(np.int32)[None]).to(dev)
     q = torch.randn((1, HQ, D), generator=torch.Generator(device=dev).manual_seed(4), device=dev)
     keys = torch.tensor([chunk_keys(ctx, s, e)], dtype=torch.int32, device=dev)
-    dec = KvSplitDecode(1, HQ, HKV, dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    step = lambda: dec(kc, vc, q, bt, keys, SCALE, max_seq_len=n_local * PAGE)
-    for _ in range(5):
-        step()
-    torch.cuda.synchronize()
-    # one step (decode, all_gather, merge) as a CUDA graph, so host launch latency stays out
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step()
-    reps = 30
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    dist.barrier()
-    torch.cuda.synchronize()
-    for a, b in evs:
-        flush.zero_()
-        a.record()
-        g.replay()
-        b.record()
-    torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b) for a, b in evs) / reps
-    del g
-    torch.cuda.synchronize()
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
-    L.check_status()
-    del dec
-    return {"n_gpus": world, "ms": round(ms, 4), "gbs": round(ctx * HKV * D * 4 / (ms / 1e3) / 1e9, 1),
-            "pages_per_rank": n_local, "exchange": "NCCL all_gather of [O | lse] records, LSE merge on every rank",
-            "l2": "flushed before each step", "timing": "CUDA graph of one step, max over ranks"}
+    # L2 flush by READING 256 MB: the cache is left full of clean lines (a flush by writing would
+    # leave dirty lines whose write-back then competes with the decode's reads).
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    align = torch.zeros(1, device=dev)
+    res = {"n_gpus": world, "pages_per_rank": n_local, "l2": "flushed (256 MB read) before each step",
+           "timing": "CUDA graph of one step, max over ranks"}
+    for exchange in ("p2p", "collective", "decode_only"):
+        dec = KvSplitDecode(1, HQ, HKV, dev, exchange="collective" if exchange == "decode_only" else exchange)
+        if exchange == "decode_only":  # this rank's chunk alone: the part of the step that shrinks with R
+            o_loc = torch.empty((1, HQ, D), device=dev)
+            step = lambda: L.attn_decode(kc, vc, q, bt, keys, SCALE, max_seq_len=n_local * PAGE, out=o_loc,
+                                         workspace=dec.ws)
+        else:
+            step = lambda: dec(kc, vc, q, bt, keys, SCALE, max_seq_len=n_local * PAGE)
+        for _ in range(5):
+            step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        reps = 30
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        for a, b in evs:
+            flush.sum()
+            dist.all_reduce(align)  # both ranks' streams start the step together
+            a.record()
+            g.replay()
+            b.record()
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        del g
+        L.check_status()
+        dec.close()
+        res[exchange] = {"ms": round(ms, 4), "gbs": round(ctx * HKV * D * 4 / (ms / 1e3) / 1e9, 1)}
+    res["ms"], res["gbs"] = res["p2p"]["ms"], res["p2p"]["gbs"]
+    return res
 
 
 # ---------------------------------------------------------------------------------------------

@@ -145,6 +145,27 @@ int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n
                          int32_t head_dim, int64_t o_part_stride, int64_t lse_part_stride, float *out,
                          float *lse_out, void *stream);
 
+/* ---- One context over several processes / GPUs: peer-memory exchange and merge -------------
+ * (no counterpart in the reference, which runs in one process). Rank r of R decodes its
+ * contiguous chunk of a sequence's pages with lstk_cuda_attn_decode(..., lse_out) and then calls
+ * lstk_cuda_attn_exchange_merge, which stores its rows (O, lse) straight into every rank's
+ * mailbox over NVLink (CUDA IPC mappings, plain stores), raises per-row flags, waits for the
+ * other ranks' flags (bounded by wait_ns, 0 = 1 s; on timeout LSTK_ERR_TIMEOUT in the device
+ * status and zero rows) and merges the R records by log-sum-exp into out [n_rows][128] (and
+ * lse_out, natural log, optional). Set-up per rank: lstk_cuda_mailbox_alloc (on the current
+ * device; zeroed; 64-byte IPC handle out), share the handles through any host channel,
+ * lstk_cuda_mailbox_open each peer's, and place the R pointers (own at [rank]) in a device
+ * array `mailboxes`. Every rank must make the same sequence of calls with the same n_rows; the
+ * calls advance an epoch kept in the mailbox, so they can be replayed from a CUDA graph. */
+size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim);
+int lstk_cuda_mailbox_alloc(size_t bytes, void **mailbox, void *ipc_handle);
+int lstk_cuda_mailbox_free(void *mailbox);
+int lstk_cuda_mailbox_open(const void *ipc_handle, void **peer_mailbox);
+int lstk_cuda_mailbox_close(void *peer_mailbox);
+int lstk_cuda_attn_exchange_merge(void *const *mailboxes, int32_t rank, int32_t n_ranks, const float *local_o,
+                                  const float *local_lse, int64_t n_rows, int32_t head_dim, uint64_t wait_ns,
+                                  float *out, float *lse_out, void *stream);
+
 /* ---- Paged causal prefill: replaces flash_attn_ext for a chunk of prompt tokens -------------
  * (src/qwen3.cpp:155-167 with n_tokens > 1). Sequence b's query tokens are rows
  * [q_seq_start[b], q_seq_start[b+1]) of q, at positions q_pos0[b], q_pos0[b]+1, ...; query

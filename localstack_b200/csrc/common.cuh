@@ -33,6 +33,7 @@ enum : int {
     kSiteDecodeWaitEmpty = 13,
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
+    kSiteExchangeWait = 30,
 };
 
 __device__ __forceinline__ void report(DeviceStatus *st, int code, int where, int detail) {

@@ -3,6 +3,7 @@
 // (except lstk_cuda_status, whose job is to synchronise and read the device status word).
 #include "common.cuh"
 #include "decode.cuh"
+#include "exchange.cuh"
 #include "host_util.h"
 #include "kv_append.cuh"
 #include "prefill.cuh"
@@ -11,6 +12,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -444,6 +446,84 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
     }
     prefill::prefill_kernel<<<(unsigned) grid, prefill::kThreads, prefill::kSmemBytes, s>>>(qmap, kmap, vmap, p);
     return launch_check("prefill_kernel");
+}
+
+size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim) {
+    if (n_ranks <= 0 || n_rows < 0 || head_dim != exchange::kD) return 0;
+    return exchange::mailbox_bytes(n_ranks, n_rows);
+}
+
+int lstk_cuda_mailbox_alloc(size_t bytes, void **mailbox, void *ipc_handle) {
+    if (!mailbox || !ipc_handle || bytes == 0) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_mailbox_alloc: bad arguments");
+    *mailbox = nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaMalloc(mailbox)", e));
+    if ((e = cudaMemset(p, 0, bytes)) != cudaSuccess ||
+        (e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(ipc_handle), p)) != cudaSuccess) {
+        cudaFree(p);
+        return set_error(LSTK_ERR_CUDA, cuda_msg("mailbox set-up", e));
+    }
+    *mailbox = p;
+    return clear_error();
+}
+
+int lstk_cuda_mailbox_free(void *mailbox) {
+    if (!mailbox) return clear_error();
+    const cudaError_t e = cudaFree(mailbox);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFree(mailbox)", e));
+    return clear_error();
+}
+
+int lstk_cuda_mailbox_open(const void *ipc_handle, void **peer_mailbox) {
+    if (!ipc_handle || !peer_mailbox) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_mailbox_open: bad arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(peer_mailbox, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaIpcOpenMemHandle", e));
+    return clear_error();
+}
+
+int lstk_cuda_mailbox_close(void *peer_mailbox) {
+    if (!peer_mailbox) return clear_error();
+    const cudaError_t e = cudaIpcCloseMemHandle(peer_mailbox);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaIpcCloseMemHandle", e));
+    return clear_error();
+}
+
+int lstk_cuda_attn_exchange_merge(void *const *mailboxes, int32_t rank, int32_t n_ranks, const float *local_o,
+                                  const float *local_lse, int64_t n_rows, int32_t head_dim, uint64_t wait_ns,
+                                  float *out, float *lse_out, void *stream) {
+    if (!mailboxes || !local_o || !local_lse || !out || n_ranks <= 0 || rank < 0 || rank >= n_ranks || n_rows < 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_exchange_merge: bad arguments");
+    if (head_dim != exchange::kD) return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_exchange_merge: head_dim must be 128");
+    if (n_rows == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(local_o, &dev);
+    if (rc) return rc;
+    exchange::Params p;
+    p.mailboxes = reinterpret_cast<uint8_t *const *>(mailboxes);
+    p.rank = rank;
+    p.n_ranks = n_ranks;
+    p.n_rows = n_rows;
+    p.local_o = local_o;
+    p.local_lse = local_lse;
+    p.wait_ns = wait_ns ? wait_ns : 1000000000ull;
+    p.out = out;
+    p.lse_out = lse_out;
+    p.status = dev->status;
+    // Every CTA must be resident at once (they push before they wait): 8 small CTAs per SM.
+    const int64_t grid = std::min<int64_t>({n_rows, (int64_t) dev->n_sms * 8, (int64_t) exchange::kMaxCtas});
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3(exchange::kThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, exchange::exchange_merge_kernel, p), "exchange_merge_kernel");
 }
 
 }  // extern "C"

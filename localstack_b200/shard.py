@@ -7,18 +7,24 @@ attention node shards in two ways, both built here on the single-GPU C ABI:
   each to the least-loaded rank. A rank holds its own sequences' pages, block tables and queries
   and runs the ordinary decode; nothing crosses GPUs on the data path.
 * One long sequence: its page list is cut into R contiguous chunks, chunk r's pages resident on
-  rank r. Each rank decodes its chunk with lse_out into one record [O (rows x D) | lse (rows)];
-  the records are all-gathered (NCCL on GPUs) and every rank merges them by log-sum-exp with
-  lstk_cuda_attn_merge, reading the parts straight out of the gathered buffer through the
-  merge's part strides. The merged output is therefore replicated on every rank.
+  rank r. Each rank decodes its chunk with lse_out, then the partials are exchanged and merged
+  by log-sum-exp, so the merged output is replicated on every rank. Two exchanges:
+  - "p2p" (default on GPUs): lstk_cuda_attn_exchange_merge stores each rank's rows straight into
+    every rank's mailbox over NVLink (CUDA IPC mappings set up once through the process group),
+    waits on per-row flags and merges, all in one kernel;
+  - "collective": one record [O (rows x D) | lse (rows)] per rank, all-gathered through the
+    process group (NCCL on GPUs, gloo on CPUs) and merged with lstk_cuda_attn_merge straight
+    out of the gathered buffer through the merge's part strides.
 """
+import ctypes
 import heapq
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from .attn import HEAD_DIM, DecodeWorkspace, attn_decode, attn_merge
+from ._lib import check, lib
+from .attn import HEAD_DIM, DecodeWorkspace, _p, _stream, attn_decode, attn_merge
 
 
 def lpt_partition(lengths, world):
@@ -72,27 +78,77 @@ def all_gather_records(gathered, local, group=None):
 class KvSplitDecode:
     """Decode of sequences whose pages are split over the ranks of `group` in contiguous chunks.
 
-    Every rank calls it with the same n_seqs / n_head; rank r passes its own chunk's block tables
-    and per-sequence key counts (chunk_keys). Returns the merged output [n_seqs][n_head][D] f32,
-    identical on every rank, and keeps the merged natural-log lse in `self.lse`."""
+    Every rank calls it with the same n_seqs / n_head, the same number of times; rank r passes
+    its own chunk's block tables and per-sequence key counts (chunk_keys). Returns the merged
+    output [n_seqs][n_head][D] f32, identical on every rank, and keeps the merged natural-log
+    lse in `self.lse`. Call close() on every rank before the process group goes away."""
 
-    def __init__(self, n_seqs, n_head, n_head_kv, device, group=None):
+    def __init__(self, n_seqs, n_head, n_head_kv, device, group=None, exchange="p2p", wait_ns=0):
+        if exchange not in ("p2p", "collective"):
+            raise ValueError("exchange must be 'p2p' or 'collective'")
         self.group = group
         self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.exchange = exchange
+        self.wait_ns = int(wait_ns)
         self.n_seqs, self.n_head = n_seqs, n_head
         self.rows = n_seqs * n_head
         rec = self.rows * HEAD_DIM + self.rows
         self.local = torch.empty(rec, dtype=torch.float32, device=device)
-        self.gathered = torch.empty(self.world * rec, dtype=torch.float32, device=device)
         self.ws = DecodeWorkspace(n_seqs, n_head, n_head_kv, device)
         self.out = torch.empty((n_seqs, n_head, HEAD_DIM), dtype=torch.float32, device=device)
         self.lse = torch.empty((n_seqs, n_head), dtype=torch.float32, device=device)
+        self._own, self._peers = None, []
+        if exchange == "collective":
+            self.gathered = torch.empty(self.world * rec, dtype=torch.float32, device=device)
+        else:
+            self._open_mailboxes(device)
+
+    def _open_mailboxes(self, device):
+        L = lib()
+        nbytes = L.lstk_cuda_mailbox_bytes(self.world, self.rows, HEAD_DIM)
+        own, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            check(L.lstk_cuda_mailbox_alloc(nbytes, ctypes.byref(own), handle))
+        self._own = own
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(own.value)
+                continue
+            peer = ctypes.c_void_p()
+            check(L.lstk_cuda_mailbox_open(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)))
+            self._peers.append(peer)
+            ptrs.append(peer.value)
+        self.mailboxes = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=self.group)
+
+    def close(self):
+        """Releases the peer mappings and the own mailbox once every rank is done with them."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still writes into another's mailbox
+        L = lib()
+        for peer in self._peers:
+            check(L.lstk_cuda_mailbox_close(peer))
+        self._peers = []
+        dist.barrier(group=self.group)  # no rank still maps this rank's mailbox
+        check(L.lstk_cuda_mailbox_free(self._own))
+        self._own = None
 
     def __call__(self, k_cache, v_cache, q, block_tables, chunk_lens, scale=None, max_seq_len=0):
         o_loc, lse_loc = record_views(self.local, self.rows)
         attn_decode(k_cache, v_cache, q, block_tables, chunk_lens, scale, max_seq_len,
                     out=o_loc[0].view(self.n_seqs, self.n_head, HEAD_DIM),
                     lse_out=lse_loc[0].view(self.n_seqs, self.n_head), workspace=self.ws)
+        if self.exchange == "p2p":
+            check(lib().lstk_cuda_attn_exchange_merge(_p(self.mailboxes), self.rank, self.world, _p(o_loc[0]),
+                                                      _p(lse_loc[0]), self.rows, HEAD_DIM, self.wait_ns,
+                                                      _p(self.out), _p(self.lse), _stream()))
+            return self.out
         all_gather_records(self.gathered, self.local, self.group)
         o_parts, lse_parts = record_views(self.gathered, self.rows)
         attn_merge(o_parts, lse_parts, out=self.out.view(self.rows, HEAD_DIM), lse_out=self.lse.view(self.rows))

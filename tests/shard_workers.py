@@ -106,13 +106,34 @@ def kv_split_nccl(rank, world, port, result_dir):
         s, e = page_chunks((ctx + 31) // 32, world)[rank]
         n = chunk_keys(ctx, s, e)
         f16 = lambda a: torch.from_numpy(a.view(np.int16)).to(dev).view(torch.float16)
-        dec = KvSplitDecode(1, hq, hkv, dev)
-        out = dec(f16(kc), f16(vc), torch.from_numpy(q).to(dev), torch.from_numpy(_chunk_table(bt, s, e)).to(dev),
-                  torch.tensor([n], dtype=torch.int32, device=dev), SCALE)
-        torch.cuda.synchronize()
-        L.check_status()
+        args = (f16(kc), f16(vc), torch.from_numpy(q).to(dev), torch.from_numpy(_chunk_table(bt, s, e)).to(dev),
+                torch.tensor([n], dtype=torch.int32, device=dev), SCALE)
         ex = O.paged_attn(q, [0], [ctx - 1], kc, vc, bt, [ctx], SCALE, mode=O.MODE_EXACT)
-        res["split"] = [within(out.cpu().numpy(), ex), max_err(out.cpu().numpy(), ex)]
+        for exchange in ("p2p", "collective"):
+            dec = KvSplitDecode(1, hq, hkv, dev, exchange=exchange)
+            for _ in range(3):  # repeated calls: epochs / banks alternate
+                out = dec(*args)
+            torch.cuda.synchronize()
+            L.check_status()
+            res[f"split_{exchange}"] = [within(out.cpu().numpy(), ex), max_err(out.cpu().numpy(), ex)]
+            if exchange == "p2p":
+                # one step captured in a CUDA graph and replayed
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    dec(*args)
+                torch.cuda.current_stream().wait_stream(side)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    dec(*args)
+                dec.out.zero_()
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize()
+                L.check_status()
+                res["split_p2p_graph"] = [within(dec.out.cpu().numpy(), ex), max_err(dec.out.cpu().numpy(), ex)]
+                del g
+            dec.close()
     finally:
         dist.destroy_process_group()
     with open(os.path.join(result_dir, f"rank{rank}.json"), "w") as f:

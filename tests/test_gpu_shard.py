@@ -42,6 +42,89 @@ def test_records_and_strided_merge(R):
     assert np.allclose(lse.cpu().numpy(), ex_lse.reshape(hq), atol=1e-3)
 
 
+def _mailbox(n_ranks, rows):
+    import ctypes
+    lib = L.lib()
+    own, h = ctypes.c_void_p(), (ctypes.c_char * 64)()
+    assert lib.lstk_cuda_mailbox_alloc(lib.lstk_cuda_mailbox_bytes(n_ranks, rows, 128), ctypes.byref(own), h) == 0
+    return own
+
+
+@pytest.mark.gpu
+def test_exchange_merge_single_rank_epochs_and_graph():
+    """R = 1: the merged rows are the local rows exactly, over several calls (epochs advance in
+    the mailbox) and from a CUDA graph replayed with new inputs."""
+    import ctypes
+    lib = L.lib()
+    rows = 32
+    own = _mailbox(1, rows)
+    try:
+        boxes = torch.tensor([own.value], dtype=torch.int64, device="cuda")
+        o = torch.empty(rows, 128, device="cuda")
+        lse = torch.empty(rows, device="cuda")
+        out = torch.empty_like(o)
+        lse_out = torch.empty_like(lse)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        call = lambda: lib.lstk_cuda_attn_exchange_merge(P(boxes), 0, 1, P(o), P(lse), rows, 128, 0, P(out),
+                                                         P(lse_out), ctypes.c_void_p(
+                                                             torch.cuda.current_stream().cuda_stream))
+        for i in range(3):
+            o.normal_()
+            lse.normal_()
+            assert call() == 0
+            torch.cuda.synchronize()
+            assert torch.equal(out, o) and torch.equal(lse_out, lse)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            call()
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(g):
+            call()
+        for i in range(3):
+            o.normal_()
+            lse.normal_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, o) and torch.equal(lse_out, lse)
+        del g
+        L.check_status()
+    finally:
+        torch.cuda.synchronize()
+        lib.lstk_cuda_mailbox_free(own)
+
+
+@pytest.mark.gpu
+def test_exchange_merge_times_out_when_a_peer_never_writes():
+    """Failure detection: rank 0 of 2 waits for source 1's flags, which nothing sets; the bounded
+    wait (20 ms here) runs out, the kernel records LSTK_ERR_TIMEOUT and returns zeros, and the
+    device stays usable."""
+    import ctypes
+    lib = L.lib()
+    rows = 8
+    own, other = _mailbox(2, rows), _mailbox(2, rows)
+    try:
+        boxes = torch.tensor([own.value, other.value], dtype=torch.int64, device="cuda")
+        o = torch.randn(rows, 128, device="cuda")
+        lse = torch.randn(rows, device="cuda")
+        out = torch.full_like(o, 7.0)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        assert lib.lstk_cuda_attn_exchange_merge(P(boxes), 0, 2, P(o), P(lse), rows, 128, 20_000_000, P(out),
+                                                 None, ctypes.c_void_p(
+                                                     torch.cuda.current_stream().cuda_stream)) == 0
+        with pytest.raises(L.LstkError) as e:
+            L.check_status()
+        assert e.value.code == -3
+        assert torch.count_nonzero(out).item() == 0
+        L.check_status()  # cleared by the read; the context still works
+        assert torch.equal(torch.ones(4, device="cuda") * 2, torch.full((4,), 2.0, device="cuda"))
+    finally:
+        torch.cuda.synchronize()
+        lib.lstk_cuda_mailbox_free(own)
+        lib.lstk_cuda_mailbox_free(other)
+
+
 @pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_kv_split_nccl_two_ranks(tmp_path):
@@ -63,5 +146,7 @@ def test_kv_split_nccl_two_ranks(tmp_path):
             else:
                 os.environ[k] = v
     for r in range(2):
-        ok, err = json.load(open(os.path.join(tmp_path, f"rank{r}.json")))["split"]
-        assert ok, (r, err)
+        res = json.load(open(os.path.join(tmp_path, f"rank{r}.json")))
+        for key in ("split_p2p", "split_collective", "split_p2p_graph"):
+            ok, err = res[key]
+            assert ok, (r, key, err)
