@@ -10,15 +10,21 @@
 // (64, G, 128/G) loads exactly that row order. K/V tiles are 128 keys = 4 pages, each page
 // fetched by TMA through the block table (box (64, 1, 32), 128-byte swizzle).
 //
-// Pipeline (one CTA per SM: 192 KiB of shared memory, 512 TMEM columns):
-//   warp 4  TMA producer: Q once, then K_j / V_j into double buffers.
-//   warp 5  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
+// Pipeline (one CTA per SM: 224 KiB of shared memory, 512 TMEM columns):
+//   warp 8  TMA producer: Q once, then K_j / V_j into double buffers.
+//   warp 9  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
 //           waiting for softmax j, so the tensor core computes the next scores while the
-//           softmax warps work; then O += P_j V_j with P_j from shared memory.
-//   warps 0-3  softmax: thread r owns row r (TMEM lane r): loads S_j, applies the causal mask,
-//           online max / exp2 / sum, rescales its O row in TMEM when the max moved, writes P_j
-//           (f16) into shared memory in the MMA operand layout. Epilogue: O / l -> f32 out.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (f32, 128 lanes = 128 rows).
+//           softmax warps work; then O += P_j V_j with P_j from shared memory buffer j%2.
+//   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and the 64 score columns
+//           of half w/4, so two warps on each SM sub-partition share the tile's exp work. Per
+//           tile: tcgen05.ld of its 64 scores, causal mask, row max (the two halves exchange
+//           theirs through spare TMEM columns), P = 2^(s*scale - m) as f16 pairs and their sum,
+//           P written into its 64-key half of the shared-memory operand. The running max only
+//           moves (and O is rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
+//           the softmax rarely waits for the previous PV; P is double-buffered, so writing P_j
+//           never waits for PV_{j-1} either. Epilogue: O / l -> f32 out, 64 columns per warp.
+// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (f32, 128 lanes = 128 rows), row-max exchange
+// cols [384,388) (two per iteration parity), row-sum exchange [388,390).
 //
 // Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
 //   Q, K, P: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
@@ -38,16 +44,19 @@ constexpr int kD = 128;
 constexpr int kPage = 32;
 constexpr int kTile = kBM * kD * 2;  // 32 KiB
 constexpr int kSub = kTile / 2;      // 16 KiB: 128 rows x 128 B
-constexpr int kThreads = 192;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kWarpTma = 8;
+constexpr int kWarpMma = 9;
+constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColXmax = 384, kColXsum = 388;
 
 // Shared memory carve-up (offsets from a 1024-aligned base).
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;       // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
-constexpr int kOffP = kOffV + 2 * kTile;
-constexpr int kOffBar = kOffP + kTile;
+constexpr int kOffP = kOffV + 2 * kTile;   // 2 buffers
+constexpr int kOffBar = kOffP + 2 * kTile;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
 
 struct Params {
@@ -68,12 +77,14 @@ struct Barriers {
     uint64_t q_full;
     uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
     uint64_t s_full[2];
-    uint64_t p_full;
+    uint64_t p_full;  // one arrival per softmax warp
     uint64_t o_done;
     uint64_t mma_drain;
+    uint64_t pair[4];  // per TMEM quadrant: the two softmax warps sharing its rows
     uint32_t tmem_base;
     int abort;
 };
+static_assert(kOffBar + sizeof(Barriers) + 1024 <= 232448, "shared memory over the 227 KiB limit");
 
 // ---- tcgen05 wrappers ---------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -135,6 +146,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float v[32]) {
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v)) : "memory");
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -154,6 +174,49 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
 constexpr uint32_t idesc_f16(bool b_mn_major) {
     return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t) (kBN >> 3) << 17) | ((uint32_t) (kBM >> 4) << 24);
 }
+
+// Three-input max (one instruction on sm_100a).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Softmax numerator for two adjacent scores with packed instructions: x = s * scale_log2 - mu
+// for both (fma.f32x2), rounded to an f16 pair, 2^x for both (ex2.approx.f16x2; P is consumed
+// as f16 by the PV MMA anyway), and the two f16 results added in f32 to a running pair of row
+// sums (add.f32x2), so the normaliser sums exactly the P the tensor core multiplies. Returns the
+// f16 pair (lower half = first score).
+__device__ __forceinline__ uint32_t softmax_pair(float s0, float s1, uint64_t scale2, uint64_t neg_mu2,
+                                                 uint64_t &sum2) {
+    uint32_t p;
+    asm("{\n\t"
+        ".reg .b64 x, y;\n\t"
+        ".reg .f32 a, b;\n\t"
+        ".reg .b16 lo, hi;\n\t"
+        "mov.b64 x, {%2, %3};\n\t"
+        "fma.rn.f32x2 y, x, %4, %5;\n\t"
+        "mov.b64 {a, b}, y;\n\t"
+        "cvt.rn.f16x2.f32 %0, b, a;\n\t"
+        "ex2.approx.f16x2 %0, %0;\n\t"
+        "mov.b32 {lo, hi}, %0;\n\t"
+        "cvt.f32.f16 a, lo;\n\t"
+        "cvt.f32.f16 b, hi;\n\t"
+        "mov.b64 x, {a, b};\n\t"
+        "add.f32x2 %1, %1, x;\n\t"
+        "}"
+        : "=r"(p), "+l"(sum2)
+        : "f"(s0), "f"(s1), "l"(scale2), "l"(neg_mu2));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    return ((uint64_t) __float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+
+// The running max is only moved (and O rescaled) when a tile's max exceeds it by more than this
+// many powers of two; otherwise P uses the stale max, so its entries stay below 2^8.
+constexpr float kRescaleThreshold = 8.f;
 
 extern __shared__ __align__(1024) uint8_t dyn_smem[];
 
@@ -200,12 +263,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_init(smem_u32(&bars->v_empty[i]), 1);
             mbar_init(smem_u32(&bars->s_full[i]), 1);
         }
-        mbar_init(smem_u32(&bars->p_full), 4);  // one arrival per softmax warp
+        mbar_init(smem_u32(&bars->p_full), kSoftmaxWarps);
+        for (int q = 0; q < 4; q++) mbar_init(smem_u32(&bars->pair[q]), 2);
         mbar_init(smem_u32(&bars->o_done), 1);
         mbar_init(smem_u32(&bars->mma_drain), 1);
         fence_barrier_init();
     }
-    if (warp == 5) {
+    if (warp == kWarpMma) {
         tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
         tmem_relinquish();
     }
@@ -214,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
 
-    if (warp == 4) {
+    if (warp == kWarpTma) {
         // ---- TMA producer ----
         if (lane == 0 && n_tiles > 0) {
             prefetch_tensormap(&qmap);
@@ -257,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 n_v++;
             }
             if (!ok) {
-                report(p.status, kStatusTimeout, kSitePrefillWait, 4);
+                report(p.status, kStatusTimeout, kSitePrefillWait, kWarpTma);
                 *abort_flag = 1;
             }
             if (*abort_flag) {
@@ -269,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     mbar_wait_bounded(smem_u32(&bars->v_full[j & 1]), (uint32_t) (j >> 1) & 1, nullptr);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kWarpMma) {
         // ---- MMA issuer ----
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_qk = idesc_f16(false);
@@ -308,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t aoff = (uint32_t) ((kk >> 2) * kSub + (kk & 3) * 32);
                     const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
-                    mma_f16_ss(tmem + kColO, sdesc_sw128(sP + aoff, 16, 1024),
+                    mma_f16_ss(tmem + kColO, sdesc_sw128(sP + buf * kTile + aoff, 16, 1024),
                                sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
@@ -316,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 mma_commit(smem_u32(&bars->v_empty[buf]));
             }
             if (!ok) {
-                report(p.status, kStatusTimeout, kSitePrefillWait, 5);
+                report(p.status, kStatusTimeout, kSitePrefillWait, kWarpMma);
                 *abort_flag = 1;
             }
             // Every MMA issued so far completes before TMEM can be released.
@@ -324,14 +388,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
         }
     } else {
-        // ---- softmax warps 0..3: thread r owns query row r ----
-        const int r = threadIdx.x;
-        const uint32_t lane_base = tmem + ((uint32_t) (warp * 32) << 16);
+        // ---- softmax warps 0..7: warp w owns rows 32*(w%4).. and score columns 64*(w/4).. ----
+        const int hf = warp >> 2;
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // row within the tile
+        const uint32_t lane_base = tmem + ((uint32_t) (quad * 32) << 16);
         const int tq = tok0 + r / G;  // query token index within the sequence
         const int head = kvh * G + r % G;
-        const int qpos = pos0 + tq;
-        const int row_keys = min(kv_len, qpos + 1);  // keys [0, row_keys) are visible
-        float m = -INFINITY, l = 0.f;
+        const int row_keys = min(kv_len, pos0 + tq + 1);  // keys [0, row_keys) are visible
+        const uint32_t pair_bar = smem_u32(&bars->pair[quad]);
+        uint32_t pair_uses = 0;
+        // Both warps sharing these rows have passed this point (bounded; false on timeout / abort).
+        auto pair_sync = [&]() -> bool {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pair_bar);
+            const bool okw = __all_sync(0xffffffffu, mbar_wait_bounded(pair_bar, pair_uses & 1, abort_flag));
+            pair_uses++;
+            tc_fence_after();
+            return okw;
+        };
+        const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
+        float m = -INFINITY, l = 0.f;  // l: this warp's half of the row sum
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
             const int buf = j & 1;
@@ -342,81 +420,98 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 break;
             }
             tc_fence_after();
-            float s[128];
-#pragma unroll
-            for (int c = 0; c < 4; c++) tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + c * 32, s + c * 32);
+            float sc[64];
+            tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, sc);
+            tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf + 32, sc + 32);
             tmem_wait_ld();
-            const int kbase = j * kBN;
-            float tmax = -INFINITY;
-            if (kbase + kBN <= row_keys) {
+            const int kbase = j * kBN + 64 * hf;  // key index of this warp's first column
+            if (kbase + 64 > row_keys) {
 #pragma unroll
-                for (int c = 0; c < 128; c++) {
-                    s[c] *= p.scale_log2;
-                    tmax = fmaxf(tmax, s[c]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 128; c++) {
-                    s[c] = (kbase + c < row_keys) ? s[c] * p.scale_log2 : -INFINITY;
-                    tmax = fmaxf(tmax, s[c]);
-                }
+                for (int c = 0; c < 64; c++) sc[c] = (kbase + c < row_keys) ? sc[c] : -INFINITY;
             }
-            const float m_new = fmaxf(m, tmax);
+            // Row max of the raw scores (the scale is positive): 8 independent max3 chains.
+            float mx[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) mx[i] = fmaxf(sc[i], sc[8 + i]);
+#pragma unroll
+            for (int c = 16; c < 64; c += 16)
+#pragma unroll
+                for (int i = 0; i < 8; i++) mx[i] = max3(mx[i], sc[c + i], sc[c + 8 + i]);
+            const float half_max =
+                fmaxf(max3(mx[0], mx[1], mx[2]), fmaxf(max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            // Exchange the half-row maxima through TMEM (columns by iteration parity, so a warp
+            // that runs ahead never overwrites a value its partner has not read).
+            tmem_st1(lane_base + kColXmax + 2 * buf + hf, half_max);
+            tmem_wait_st();
+            if (!pair_sync()) {
+                ok = false;
+                break;
+            }
+            const float other = tmem_ld1(lane_base + kColXmax + 2 * buf + (hf ^ 1));
+            tmem_wait_ld();
+            const float m_tile = fmaxf(half_max, other) * p.scale_log2;
+            const bool move = m_tile > m + kRescaleThreshold;  // always true for the first visible tile
+            const float m_new = move ? m_tile : m;
+            const float alpha = move ? fast_exp2(m - m_new) : 1.f;
             const float mu = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = fast_exp2(m - mu);
-            float rs = 0.f;
-            uint32_t pk[64];
+            const uint64_t neg_mu2 = pack_f32x2(-mu, -mu);
+            uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};  // independent pairs of partial row sums
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const float a = fast_exp2(s[2 * c] - mu);
-                const float bb = fast_exp2(s[2 * c + 1] - mu);
-                rs += a + bb;
-                pk[c] = pack_half2(a, bb);
-            }
-            // P_{j-1} consumed and O updated by PV_{j-1} before P_j / the rescale are written.
-            if (j > 0) {
+            for (int c = 0; c < 32; c++) pk[c] = softmax_pair(sc[2 * c], sc[2 * c + 1], scale2, neg_mu2, sum2[c & 3]);
+            // A moved max rescales O, which PV_{j-1} must have finished updating (PV_{j-2} has:
+            // S_j ready implies it). P_j goes to buffer j%2, last read by PV_{j-2}: no wait.
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
                 if (!__all_sync(0xffffffffu,
                                 mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (j - 1) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        float o[32];
-                        tmem_ld32(lane_base + kColO + c * 32, o);
-                        tmem_wait_ld();
+                for (int c = 0; c < 2; c++) {
+                    float o[32];
+                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] *= alpha;
-                        tmem_st32(lane_base + kColO + c * 32, o);
-                    }
-                    tmem_wait_st();
+                    for (int i = 0; i < 32; i++) o[i] *= alpha;
+                    tmem_st32(lane_base + kColO + 64 * hf + c * 32, o);
                 }
+                tmem_wait_st();
             }
-            // P row r into the K-major swizzled operand tile (two 64-key sub-tiles).
+            // P row r, keys 64*hf.., into sub-tile hf of the K-major swizzled operand buffer.
+            const uint32_t pbase = sP + buf * kTile + hf * kSub;
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-#pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    const uint32_t addr = sP + h * kSub + sw128_offset((uint32_t) r, (uint32_t) c);
-                    const int w0 = h * 32 + c * 4;
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[w0]),
-                                 "r"(pk[w0 + 1]), "r"(pk[w0 + 2]), "r"(pk[w0 + 3])
-                                 : "memory");
-                }
-            }
+            for (int c = 0; c < 8; c++)
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(pbase + sw128_offset((uint32_t) r, (uint32_t) c)),
+                             "r"(pk[4 * c]), "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                             : "memory");
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
+            const float rs = (__uint_as_float((uint32_t) sum2[0]) + __uint_as_float((uint32_t) (sum2[0] >> 32))) +
+                             (__uint_as_float((uint32_t) sum2[1]) + __uint_as_float((uint32_t) (sum2[1] >> 32))) +
+                             (__uint_as_float((uint32_t) sum2[2]) + __uint_as_float((uint32_t) (sum2[2] >> 32))) +
+                             (__uint_as_float((uint32_t) sum2[3]) + __uint_as_float((uint32_t) (sum2[3] >> 32)));
             l = l * alpha + rs;
             m = m_new;
         }
-        // Epilogue: O / l for this row.
+        // Epilogue: O / (l_0 + l_1); this warp writes its 64 output columns of the row.
         if (ok && n_tiles > 0)
             ok = __all_sync(0xffffffffu,
                             mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (n_tiles - 1) & 1, abort_flag));
+        float l_row = 0.f;
+        if (ok && n_tiles > 0) {
+            tc_fence_after();
+            tmem_st1(lane_base + kColXsum + hf, l);
+            tmem_wait_st();
+            ok = pair_sync();
+            if (ok) {
+                l_row = l + tmem_ld1(lane_base + kColXsum + (hf ^ 1));
+                tmem_wait_ld();
+            }
+        }
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) {
             report(p.status, kStatusTimeout, kSitePrefillWait, warp);
@@ -424,13 +519,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         tc_fence_after();
         const bool live = tq < n_q;
-        float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD;
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD + 64 * hf;
+        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < 2; c++) {
             float o[32];
             if (n_tiles > 0 && ok) {
-                tmem_ld32(lane_base + kColO + c * 32, o);
+                tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
                 tmem_wait_ld();
             } else {
 #pragma unroll
@@ -448,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 5) tmem_dealloc(tmem, kTmemCols);
+    if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
 }
 
 // f32 -> f16 copy of q for the tensor-core path (when the caller passes f32 queries).
