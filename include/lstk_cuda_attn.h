@@ -115,6 +115,18 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
                           float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
                           void *stream);
 
+/* Decode over a key range only (one context split across GPUs, or any partial pass): every
+ * sequence attends to its keys [kv_begin, min(kv_end, seq_lens[b])) - kv_begin a multiple of
+ * block_size - with the same arguments and results as lstk_cuda_attn_decode otherwise; lse_out
+ * gives the weights lstk_cuda_attn_merge needs to combine ranges. A sequence with no key in the
+ * range gets zeros and lse -inf. */
+int lstk_cuda_attn_decode_partial(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                  const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                  const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                  int32_t max_seq_len, int32_t kv_begin, int32_t kv_end, float scale, float *out,
+                                  float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
+                                  void *stream);
+
 /* ---- Paged decode with no caller workspace (no counterpart in the reference) ----------------
  * Same computation, arguments and results as lstk_cuda_attn_decode, minus the workspace: the
  * split-K scratch is a fixed array compiled into this library (about 5.3 MiB, held on every

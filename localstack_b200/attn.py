@@ -90,11 +90,13 @@ class DecodeWorkspace:
 
 
 def attn_decode(k_cache, v_cache, q, block_tables, seq_lens, scale=None, max_seq_len=0, out=None, lse_out=None,
-                want_lse=False, workspace=None, n_ctas=0, stream=None):
+                want_lse=False, workspace=None, n_ctas=0, stream=None, kv_range=None):
     """Paged decode attention, one query token per sequence (src/qwen3.cpp:155-167).
 
     q [B][Hq][D] f32/f16; block_tables int32 [B][max_blocks]; seq_lens int32 [B]. Returns out
-    [B][Hq][D] f32 (and lse [B][Hq] natural log when want_lse)."""
+    [B][Hq][D] f32 (and lse [B][Hq] natural log when want_lse). kv_range=(begin, end) restricts
+    every sequence to its keys [begin, min(end, len)) (begin a multiple of 32; the partial
+    entry point), for results to be combined with attn_merge."""
     L = layout_of(k_cache)
     B, Hq, _ = q.shape
     if scale is None:
@@ -107,10 +109,17 @@ def attn_decode(k_cache, v_cache, q, block_tables, seq_lens, scale=None, max_seq
         lse_out = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
     if workspace is None or workspace.n_seqs < B:
         workspace = DecodeWorkspace(B, Hq, L.n_head_kv, q.device)
-    check(lib().lstk_cuda_attn_decode(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B, Hq,
-                                      _p(block_tables), block_tables.shape[1], _p(seq_lens), int(max_seq_len),
-                                      float(scale), _p(out), _p(lse_out), _p(workspace.buf), workspace.buf.numel(),
-                                      int(n_ctas), _stream(stream)))
+    if kv_range is None:
+        check(lib().lstk_cuda_attn_decode(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B, Hq,
+                                          _p(block_tables), block_tables.shape[1], _p(seq_lens), int(max_seq_len),
+                                          float(scale), _p(out), _p(lse_out), _p(workspace.buf),
+                                          workspace.buf.numel(), int(n_ctas), _stream(stream)))
+    else:
+        check(lib().lstk_cuda_attn_decode_partial(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B,
+                                                  Hq, _p(block_tables), block_tables.shape[1], _p(seq_lens),
+                                                  int(max_seq_len), int(kv_range[0]), int(kv_range[1]),
+                                                  float(scale), _p(out), _p(lse_out), _p(workspace.buf),
+                                                  workspace.buf.numel(), int(n_ctas), _stream(stream)))
     return (out, lse_out) if want_lse else out
 
 

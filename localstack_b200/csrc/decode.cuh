@@ -50,6 +50,8 @@ struct Params {
     const int32_t *block_tables;
     int max_blocks;
     const int32_t *seq_lens;
+    int kv_page0;  // key range of every sequence: [kv_page0 * 32, kv_end) (whole sequence: 0, INT_MAX)
+    int kv_end;
     int n_seqs, n_head, n_head_kv, group, n_hg;
     int64_t n_pages;
     float scale_log2;  // softmax scale * log2(e)
@@ -62,6 +64,12 @@ struct Params {
 };
 
 __host__ __device__ inline int64_t range_lo(int c, int64_t P, int G) { return ((int64_t) c * P) / G; }
+
+// Keys of sequence b inside the call's range, counted from the range's first page.
+__device__ __forceinline__ int range_len(const Params &p, int32_t len) {
+    len = len < 0 ? 0 : min(len, p.max_blocks * kPage);
+    return max(0, min(len, p.kv_end) - p.kv_page0 * kPage);
+}
 
 // Index of the CTA whose range [lo_c, lo_{c+1}) contains page-group x.
 __device__ inline int cta_of(int64_t x, int64_t P, int G) {
@@ -263,12 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         const int b0 = threadIdx.x * per;
         int32_t local = 0;
         for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
-            int32_t len = p.seq_lens[b];
-            if (len < 0 || len > p.max_blocks * kPage) {
-                report(p.status, kStatusBadIndex, kSiteDecodeLen, b);
-                len = len < 0 ? 0 : p.max_blocks * kPage;
-            }
-            local += (len + kPage - 1) / kPage;
+            const int32_t len = p.seq_lens[b];
+            if (len < 0 || len > p.max_blocks * kPage) report(p.status, kStatusBadIndex, kSiteDecodeLen, b);
+            local += (range_len(p, len) + kPage - 1) / kPage;
         }
         chunk_sum[threadIdx.x] = local;
         __syncthreads();
@@ -284,9 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         int32_t acc = chunk_sum[threadIdx.x];
         for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
             pfx[b] = acc;
-            int32_t len = p.seq_lens[b];
-            len = len < 0 ? 0 : min(len, p.max_blocks * kPage);
-            acc += (len + kPage - 1) / kPage;
+            acc += (range_len(p, p.seq_lens[b]) + kPage - 1) / kPage;
         }
         if (threadIdx.x == kThreads - 1) pfx[p.n_seqs] = acc;
         if (threadIdx.x == 0) {
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                     ok = false;
                     break;
                 }
-                const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + cur.p];
+                const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + p.kv_page0 + cur.p];
                 const int nh = min(kHeadsPerGroup, p.n_head_kv - cur.hg * kHeadsPerGroup);
                 const uint32_t fb = smem_u32(&full[s]);
                 if (pid < 0 || pid >= p.n_pages) {
@@ -379,10 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                 }
                 break;
             }
-            const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + cur.p];
+            const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + p.kv_page0 + cur.p];
             if (active && pid >= 0 && pid < p.n_pages) {
-                int len = p.seq_lens[cur.b];
-                len = len < 0 ? 0 : min(len, p.max_blocks * kPage);
+                const int len = range_len(p, p.seq_lens[cur.b]);
                 const int valid = min(kPage, len - cur.p * kPage);
                 const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
                 process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage, valid,

@@ -271,11 +271,11 @@ size_t lstk_cuda_attn_decode_workspace_size(int32_t n_seqs, int32_t n_head, int3
     return decode_ws_prefix_bytes(n_seqs) + kDecodePartLseBytes + kDecodePartOBytes;
 }
 
-int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
-                          int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
-                          int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, float scale,
-                          float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
-                          void *stream) {
+static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                        int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
+                        int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, int32_t kv_begin,
+                        int32_t kv_end, float scale, float *out, float *lse_out, void *workspace,
+                        size_t workspace_bytes, int32_t n_ctas, void *stream) {
     int rc = check_layout(layout, "lstk_cuda_attn_decode");
     if (rc) return rc;
     const int hkv = layout->n_head_kv;
@@ -297,6 +297,10 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
         return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode: workspace too small");
     if (max_seq_len <= 0 || max_seq_len > max_blocks_per_seq * layout->block_size)
         max_seq_len = max_blocks_per_seq * layout->block_size;
+    if (kv_begin < 0 || kv_end < kv_begin || kv_begin % layout->block_size != 0 ||
+        kv_begin > max_blocks_per_seq * layout->block_size)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_partial: kv_begin must be a page multiple <= kv_end");
+    max_seq_len = std::max(0, std::min(max_seq_len, kv_end) - kv_begin);
     if (n_seqs == 0) return clear_error();
     DeviceInfo *dev = nullptr;
     if ((rc = bind_device(k_cache, &dev))) return rc;
@@ -317,6 +321,8 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
     p.block_tables = block_tables;
     p.max_blocks = max_blocks_per_seq;
     p.seq_lens = seq_lens;
+    p.kv_page0 = kv_begin / layout->block_size;
+    p.kv_end = kv_end;
     p.n_seqs = n_seqs;
     p.n_head = n_head;
     p.n_head_kv = hkv;
@@ -340,6 +346,27 @@ int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, con
         dev->decode_smem = smem;
     }
     return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
+}
+
+int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
+                          int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
+                          int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, float scale,
+                          float *out, float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
+                          void *stream) {
+    return decode_range(layout, k_cache, v_cache, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq,
+                        seq_lens, max_seq_len, 0, INT32_MAX, scale, out, lse_out, workspace, workspace_bytes, n_ctas,
+                        stream);
+}
+
+int lstk_cuda_attn_decode_partial(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                  const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                  const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                  int32_t max_seq_len, int32_t kv_begin, int32_t kv_end, float scale, float *out,
+                                  float *lse_out, void *workspace, size_t workspace_bytes, int32_t n_ctas,
+                                  void *stream) {
+    return decode_range(layout, k_cache, v_cache, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq,
+                        seq_lens, max_seq_len, kv_begin, kv_end, scale, out, lse_out, workspace, workspace_bytes,
+                        n_ctas, stream);
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
@@ -620,6 +647,8 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     p.block_tables = block_tables;
     p.max_blocks = max_blocks_per_seq;
     p.seq_lens = seq_lens;
+    p.kv_page0 = 0;
+    p.kv_end = INT32_MAX;
     p.n_seqs = n_seqs;
     p.n_head = n_head;
     p.n_head_kv = hkv;

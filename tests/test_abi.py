@@ -90,6 +90,17 @@ def test_validation_errors_without_gpu():
     assert rc == _lib.LSTK_OK
 
 
+def test_decode_partial_validates_range():
+    lib = L.lib()
+    lay = _layout()
+    fake = ctypes.c_void_p(1 << 20)
+    args = lambda b, e: (ctypes.byref(lay), fake, fake, fake, _lib.DTYPE_F32, 1, 16, fake, 2, fake, 64, b, e,
+                         ctypes.c_float(0.1), fake, NULL, fake, 1 << 30, 0, NULL)
+    assert lib.lstk_cuda_attn_decode_partial(*args(16, 64)) == _lib.LSTK_ERR_INVALID_ARG  # not a page multiple
+    assert lib.lstk_cuda_attn_decode_partial(*args(64, 32)) == _lib.LSTK_ERR_INVALID_ARG  # end before begin
+    assert lib.lstk_cuda_attn_decode_partial(*args(-32, 32)) == _lib.LSTK_ERR_INVALID_ARG
+
+
 def test_exchange_entry_points_validate():
     lib = L.lib()
     assert lib.lstk_cuda_mailbox_bytes(2, 32, 128) > 2 * 2 * 32 * 129 * 4

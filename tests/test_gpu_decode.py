@@ -202,3 +202,46 @@ def test_append_and_decode_replay_in_cuda_graph():
     assert torch.equal(o_g, o_e) and torch.equal(q_g, q_e)
     assert torch.equal(kc_g.view(torch.int16), kc_e.view(torch.int16))
     del g
+
+
+def test_decode_partial_key_ranges_merge_to_whole():
+    """lstk_cuda_attn_decode_partial over page-aligned key ranges, each against the oracle on
+    the same keys, and the LSE merge of the ranges against the whole decode (ragged batch: the
+    ranges cut some sequences and miss others entirely)."""
+    rng = np.random.default_rng(31)
+    lens = [5000, 33, 700, 4096]
+    Hq, Hkv = 32, 4
+    bt, n_pages = scattered_block_tables(rng, lens)
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    q = random_q(rng, len(lens), Hq)
+    dev = "cuda"
+    f16 = lambda a: torch.from_numpy(a.view(np.int16)).to(dev).view(torch.float16)
+    kc_t, vc_t, q_t, bt_t = f16(kc), f16(vc), torch.from_numpy(q).to(dev), torch.from_numpy(bt).to(dev)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device=dev)
+    ranges = [(0, 64), (64, 1024), (1024, 4096), (4096, 1 << 30)]
+    parts, lses = [], []
+    B = len(lens)
+    for a, b in ranges:
+        o, lse = L.attn_decode(kc_t, vc_t, q_t, bt_t, lens_t, SCALE, want_lse=True, kv_range=(a, b))
+        parts.append(o.reshape(B * Hq, 128))
+        lses.append(lse.reshape(B * Hq))
+        # oracle on the same keys: the sub-range of every sequence's pages
+        sub_lens = np.array([max(0, min(n, b) - a) for n in lens], np.int32)
+        sub_bt = np.ascontiguousarray(bt[:, a // 32:]) if a // 32 < bt.shape[1] else np.zeros((B, 1), np.int32)
+        if sub_bt.shape[1] == 0:
+            sub_bt = np.zeros((B, 1), np.int32)
+        ex = O.paged_attn(q, np.arange(B), np.maximum(sub_lens - 1, 0), kc, vc, sub_bt, sub_lens, SCALE,
+                          mode=O.MODE_EXACT)
+        got = o.cpu().numpy()
+        for i in range(B):
+            if sub_lens[i] == 0:
+                assert np.all(got[i] == 0) and np.all(np.isneginf(lse.cpu().numpy()[i]))
+            else:
+                assert within(got[i], ex[i]), (a, b, i, max_err(got[i], ex[i]))
+    merged, _ = L.attn_merge(torch.stack(parts), torch.stack(lses))
+    L.check_status()
+    lens_np = np.asarray(lens, np.int32)
+    ex_whole = O.paged_attn(q, np.arange(B), lens_np - 1, kc, vc, bt, lens_np, SCALE, mode=O.MODE_EXACT)
+    # the merged ranges meet the same tolerance against the exact whole-context result
+    assert within(merged.cpu().numpy(), ex_whole.reshape(B * Hq, 128)), max_err(merged.cpu().numpy(),
+                                                                                 ex_whole.reshape(B * Hq, 128))
