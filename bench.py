@@ -321,7 +321,7 @@ def run_b200(args):
 
     c4_split = config4_split(L, dev, world) if world > 1 and not args.no_secondary else None
     c5 = None
-    if not args.no_secondary:
+    if not args.no_secondary and not args.no_config5:
         # config 5 on every rank (its own continuous batch; weak scaling), slowest rank's time
         c5 = config5_stack(L, dev)
         t5 = torch.tensor([c5["ms_per_step"]], dtype=torch.float64, device=dev)
@@ -365,7 +365,8 @@ def run_b200(args):
             line["secondary"] = secondary(L, dev, tc_peak, hbm_peak)
             if c4_split is not None:
                 line["secondary"]["config4_kv_split"] = c4_split
-            line["secondary"]["config5_stack"] = c5
+            if c5 is not None:
+                line["secondary"]["config5_stack"] = c5
     barrier()
     if world > 1:
         dist.destroy_process_group()
@@ -758,6 +759,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true", help="skip configs 1, 2 and 4")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help="sequences per GPU (64 = config 3)")
+    ap.add_argument("--no-config5", action="store_true", help="skip the 48-layer config-5 stack (71 GB of KV)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
