@@ -91,19 +91,29 @@ EncodeTiledFn encode_fn() {
 
 // 3-D f16 map over [dim2][dim1][dim0] (dim0 contiguous) with a (box0, box1, box2) box and
 // 128-byte swizzle; out-of-range boxes fill zeros.
-int encode_f16_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
-                  uint32_t box1, uint32_t box2) {
+static int encode_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t esize, uint64_t dim0,
+                     uint64_t dim1, uint64_t dim2, uint32_t box0, uint32_t box1, uint32_t box2) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[3] = {dim0, dim1, dim2};
-    const cuuint64_t strides[2] = {dim0 * 2, dim0 * dim1 * 2};
+    const cuuint64_t strides[2] = {dim0 * esize, dim0 * dim1 * esize};
     const cuuint32_t box[3] = {box0, box1, box2};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+    const CUresult r = fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
     return LSTK_OK;
+}
+
+int encode_f16_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
+                  uint32_t box1, uint32_t box2) {
+    return encode_3d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dim0, dim1, dim2, box0, box1, box2);
+}
+
+int encode_f32_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
+                  uint32_t box1, uint32_t box2) {
+    return encode_3d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dim0, dim1, dim2, box0, box1, box2);
 }
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
@@ -441,9 +451,10 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
         q16 = workspace;
     }
 
-    CUtensorMap qmap, kmap, vmap;
+    CUtensorMap qmap, kmap, vmap, omap;
     const int tpt = prefill::kBM / group;
     if ((rc = encode_f16_3d(&qmap, q16, 128, n_head, total_tokens, 64, group, tpt))) return rc;
+    if ((rc = encode_f32_3d(&omap, out, 128, n_head, total_tokens, 32, group, tpt))) return rc;
     if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
     if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
 
@@ -471,7 +482,7 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
         if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(prefill)", e));
         dev->prefill_attr = true;
     }
-    prefill::prefill_kernel<<<(unsigned) grid, prefill::kThreads, prefill::kSmemBytes, s>>>(qmap, kmap, vmap, p);
+    prefill::prefill_kernel<<<(unsigned) grid, prefill::kThreads, prefill::kSmemBytes, s>>>(qmap, kmap, vmap, omap, p);
     return launch_check("prefill_kernel");
 }
 

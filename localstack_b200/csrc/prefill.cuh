@@ -223,6 +223,7 @@ extern __shared__ __align__(1024) uint8_t dyn_smem[];
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
+                                                              const __grid_constant__ CUtensorMap omap,
                                                               const Params p) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -519,23 +520,52 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         tc_fence_after();
         const bool live = tq < n_q;
-        float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD + 64 * hf;
         const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        if (tok0 + kBM / G <= n_q && n_tiles > 0) {
+            // A full tile leaves through TMA stores: O / l is staged in the K buffers (free: the
+            // last QK and PV have completed) as four 32-column boxes of 128 rows x 128 B with the
+            // 128-byte swizzle, whose row order (token, head) is the tile's.
+            if (ok) {
 #pragma unroll
-        for (int c = 0; c < 2; c++) {
-            float o[32];
-            if (n_tiles > 0 && ok) {
-                tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
-                tmem_wait_ld();
-            } else {
+                for (int c = 0; c < 2; c++) {
+                    float o[32];
+                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
+                    tmem_wait_ld();
+                    const uint32_t box = sK + (uint32_t) (2 * hf + c) * kSub;
 #pragma unroll
-                for (int i = 0; i < 32; i++) o[i] = 0.f;
+                    for (int ch = 0; ch < 8; ch++)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                         box + sw128_offset((uint32_t) r, (uint32_t) ch)),
+                                     "f"(o[4 * ch] * inv), "f"(o[4 * ch + 1] * inv), "f"(o[4 * ch + 2] * inv),
+                                     "f"(o[4 * ch + 3] * inv)
+                                     : "memory");
+                }
+                fence_proxy_async_smem();
             }
-            if (live) {
+            asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
+            if (warp == 0 && lane == 0 && !*abort_flag) {
+                for (int bx = 0; bx < 4; bx++)
+                    tma_store_3d(&omap, sK + (uint32_t) bx * kSub, 32 * bx, kvh * G, q_begin + tok0);
+                tma_store_commit_wait();
+            }
+        } else {
+            float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD + 64 * hf;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4 *>(dst + c * 32 + i) =
-                        make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+            for (int c = 0; c < 2; c++) {
+                float o[32];
+                if (n_tiles > 0 && ok) {
+                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = 0.f;
+                }
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(dst + c * 32 + i) =
+                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                }
             }
         }
     }
