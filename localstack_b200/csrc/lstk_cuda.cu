@@ -482,8 +482,18 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
         if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(prefill)", e));
         dev->prefill_attr = true;
     }
-    prefill::prefill_kernel<<<(unsigned) grid, prefill::kThreads, prefill::kSmemBytes, s>>>(qmap, kmap, vmap, omap, p);
-    return launch_check("prefill_kernel");
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3(prefill::kThreads);
+    cfg.dynamicSmemBytes = prefill::kSmemBytes;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, prefill::prefill_kernel, qmap, kmap, vmap, omap, p),
+                            "prefill_kernel");
 }
 
 size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim) {

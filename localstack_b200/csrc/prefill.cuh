@@ -228,24 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
 
-    // Heaviest tiles (latest query positions) are launched first.
-    const int x = blockIdx.x;
-    const int kvh = x % p.n_head_kv;
-    const int rest = x / p.n_head_kv;
-    const int b = rest % p.n_seqs;
-    const int qt = p.n_qt - 1 - rest / p.n_seqs;
-    const int G = p.group;
-    const int tpt = kBM / G;  // tokens per query tile
-    const int q_begin = p.q_seq_start[b];
-    const int n_q = p.q_seq_start[b + 1] - q_begin;
-    const int tok0 = qt * tpt;
-    if (tok0 >= n_q) return;  // uniform across the CTA, before any barrier or TMEM use
-    const int kv_len = max(0, min(p.kv_lens[b], p.max_blocks * kPage));
-    const int pos0 = p.q_pos0[b];
-    const int last_tok = min(tok0 + tpt, n_q) - 1;
-    const int n_keys = max(0, min(kv_len, pos0 + last_tok + 1));
-    const int n_tiles = (n_keys + kBN - 1) / kBN;
-
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
     Barriers *bars = reinterpret_cast<Barriers *>(base + kOffBar);
     const uint32_t sQ = smem_u32(base + kOffQ);
@@ -278,6 +260,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    // The set-up above overlaps the previous kernel in the stream (programmatic dependent
+    // launch); everything below reads what earlier work produced.
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // Heaviest tiles (latest query positions) are launched first. A tile past its sequence's
+    // end (ragged batches) does nothing: no keys and no live rows.
+    const int x = blockIdx.x;
+    const int kvh = x % p.n_head_kv;
+    const int rest = x / p.n_head_kv;
+    const int b = rest % p.n_seqs;
+    const int qt = p.n_qt - 1 - rest / p.n_seqs;
+    const int G = p.group;
+    const int tpt = kBM / G;  // tokens per query tile
+    const int q_begin = p.q_seq_start[b];
+    const int n_q = p.q_seq_start[b + 1] - q_begin;
+    const int tok0 = qt * tpt;
+    const int kv_len = max(0, min(p.kv_lens[b], p.max_blocks * kPage));
+    const int pos0 = p.q_pos0[b];
+    const int last_tok = min(tok0 + tpt, n_q) - 1;
+    const int n_keys = tok0 < n_q ? max(0, min(kv_len, pos0 + last_tok + 1)) : 0;
+    const int n_tiles = (n_keys + kBN - 1) / kBN;
 
     if (warp == kWarpTma) {
         // ---- TMA producer ----
