@@ -10,24 +10,28 @@
 // (64, G, 128/G) loads exactly that row order. K/V tiles are 128 keys = 4 pages, each page
 // fetched by TMA through the block table (box (64, 1, 32), 128-byte swizzle).
 //
-// Pipeline (one CTA per SM: 224 KiB of shared memory, 512 TMEM columns):
+// Pipeline (one CTA per SM: 160 KiB of shared memory, 512 TMEM columns):
 //   warp 8  TMA producer: Q once, then K_j / V_j into double buffers.
 //   warp 9  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
 //           waiting for softmax j, so the tensor core computes the next scores while the
-//           softmax warps work; then O += P_j V_j with P_j from shared memory buffer j%2.
+//           softmax warps work; then O += P_j V_j with P_j read from tensor memory (TS form).
 //   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and the 64 score columns
 //           of half w/4, so two warps on each SM sub-partition share the tile's exp work. Per
 //           tile: tcgen05.ld of its 64 scores, causal mask, row max (the two halves exchange
 //           theirs through spare TMEM columns), P = 2^(s*scale - m) as f16 pairs and their sum,
-//           P written into its 64-key half of the shared-memory operand. The running max only
+//           P written back over the first 32 of its own 64 score columns. The running max only
 //           moves (and O is rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
-//           the softmax rarely waits for the previous PV; P is double-buffered, so writing P_j
-//           never waits for PV_{j-1} either. Epilogue: O / l -> f32 out, 64 columns per warp.
+//           the softmax rarely waits for the previous PV. Epilogue: O / l; a full tile is
+//           staged in the (then free) K buffers and leaves through TMA stores.
+// The kernel is launched with programmatic stream serialization: barrier and TMEM set-up overlap
+// the previous kernel, and griddepcontrol.wait precedes every read of earlier work.
 // TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (f32, 128 lanes = 128 rows), row-max exchange
-// cols [384,388) (two per iteration parity), row-sum exchange [388,390).
+// cols [384,388) (two per tile parity), row-sum exchange [388,390). P_j occupies S_j's columns
+// [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2} overwrites them only after PV_j, which
+// the tensor core executes first.
 //
 // Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
-//   Q, K, P: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
+//   Q, K: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
 //   V: the B operand of PV with N = head dim contiguous ("MN-major"): sub-tile h holds dims
 //      64h..64h+63 of all 128 keys; LBO = 16 KiB between the two dim halves, SBO = 1 KiB
 //      between groups of 8 keys.
@@ -55,8 +59,7 @@ constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColXmax = 384, kColXs
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;       // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
-constexpr int kOffP = kOffV + 2 * kTile;   // 2 buffers
-constexpr int kOffBar = kOffP + 2 * kTile;
+constexpr int kOffBar = kOffV + 2 * kTile;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
 
 struct Params {
@@ -107,6 +110,17 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// A operand from tensor memory (P), B from shared memory (V).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -233,7 +247,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const uint32_t sQ = smem_u32(base + kOffQ);
     const uint32_t sK = smem_u32(base + kOffK);
     const uint32_t sV = smem_u32(base + kOffV);
-    const uint32_t sP = smem_u32(base + kOffP);
     volatile int *abort_flag = &bars->abort;
 
     if (threadIdx.x == 0) {
@@ -373,13 +386,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     break;
                 }
                 tc_fence_after();
+                // P_j sits in TMEM over S_j: keys 0..63 in columns [0, 32), keys 64..127 in
+                // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
+                const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t aoff = (uint32_t) ((kk >> 2) * kSub + (kk & 3) * 32);
                     const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
-                    mma_f16_ss(tmem + kColO, sdesc_sw128(sP + buf * kTile + aoff, 16, 1024),
-                               sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
-                               (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + kColO, pcol + (uint32_t) ((kk >> 2) * 64 + (kk & 3) * 8),
+                               sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(smem_u32(&bars->o_done));
                 mma_commit(smem_u32(&bars->v_empty[buf]));
@@ -484,14 +498,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
                 tmem_wait_st();
             }
-            // P row r, keys 64*hf.., into sub-tile hf of the K-major swizzled operand buffer.
-            const uint32_t pbase = sP + buf * kTile + hf * kSub;
+            // P row r, keys 64*hf.., packed f16 pairs, over the first 32 of this warp's own 64
+            // score columns (already read; the partner warp's columns are untouched), where the
+            // PV MMA reads its A operand from tensor memory.
+            {
+                float pkf[32];
 #pragma unroll
-            for (int c = 0; c < 8; c++)
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(pbase + sw128_offset((uint32_t) r, (uint32_t) c)),
-                             "r"(pk[4 * c]), "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
-                             : "memory");
-            fence_proxy_async_smem();
+                for (int c = 0; c < 32; c++) pkf[c] = __uint_as_float(pk[c]);
+                tmem_st32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, pkf);
+            }
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
