@@ -135,3 +135,15 @@ def test_rope_table_host_fill():
     lib = L.lib()
     assert lib.lstk_rope_table_fill(None, 4, 128, 1e6, 1.0) == _lib.LSTK_ERR_INVALID_ARG
     assert lib.lstk_rope_table_bytes(4, 128) == 4 * 64 * 2 * 4
+
+
+def test_ggml_front_end_links_the_reference_graph_builder():
+    """Where the reference sources were present at build time, the ggml-compatible front end
+    exists and contains the reference's own graph builder and KvCache next to its entry points."""
+    lib = os.path.join(_lib.ROOT, "localstack_b200", "ggml_node", "_build", "libggml_node.so")
+    if not os.path.exists(lib):
+        pytest.skip("front end not built (reference sources absent)")
+    out = subprocess.run(["nm", "-D", "--defined-only", "-C", lib], capture_output=True, text=True, check=True).stdout
+    for sym in ("lstk_node_create", "lstk_node_step", "lstk_node_destroy", "lstk_node_last_error",
+                "qwen3_build_graph(", "KvCache::alloc(", "KvCache::fill_mask(", "ggml_flash_attn_ext("):
+        assert sym in out, sym
