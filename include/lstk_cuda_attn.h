@@ -157,6 +157,37 @@ int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n
                          int32_t head_dim, int64_t o_part_stride, int64_t lse_part_stride, float *out,
                          float *lse_out, void *stream);
 
+/* ---- Device-side KV bookkeeping for serving steps ------------------------------------------
+ * The state of KvCache (src/kv_cache.h:24-62) in caller-owned device memory: the LIFO stack of
+ * free 32-cell blocks, and per sequence slot its block table (position order) and length; plus
+ * the high-water mark. lstk_cuda_kv_alloc gives each listed slot (distinct slots, at most 2048)
+ * counts[i] new tokens (counts NULL: one each), in list order, exactly as sequential
+ * KvCache::alloc(slot, counts[i]) calls (src/kv_cache.cpp:59-83) would: new blocks are popped from
+ * the stack's top in slot order; token t of slot i (position len + t) goes to cells / positions
+ * [sum(counts[0..i)) + t] with cell = table[p / 32] * 32 + p % 32. A slot whose new blocks exceed
+ * what the stack holds after the slots before it, or its table row, gets nothing: ok[i] = 0 and
+ * its cells / positions are -1 (later slots may still fit, as with the reference). If the counts
+ * add up to more than max_tokens, nothing is allocated, every ok is 0 and the device status
+ * (lstk_cuda_status) reports LSTK_ERR_DEVICE_INDEX. lstk_cuda_kv_release is KvCache::truncate_seq
+ * (keep > 0) / remove_seq (keep <= 0) (src/kv_cache.cpp:85-132): freed blocks go back on the
+ * stack in the reference's order and the high-water mark is recomputed. The block_tables /
+ * seq_lens arrays are the ones lstk_cuda_attn_decode and lstk_cuda_attn_prefill read, so a step
+ * (allocate -> append -> attend) stays on the device and can be captured in a CUDA graph. Fill
+ * free_blocks / free_top like KvCache::init (or a permuted free list) before use. */
+typedef struct lstk_kv_pages {
+    uint32_t *free_blocks;  /* [n_blocks] stack, top at free_blocks[*free_top - 1] */
+    int32_t *free_top;      /* [1] */
+    int32_t *block_tables;  /* [n_slots][max_blocks] */
+    int32_t *seq_lens;      /* [n_slots] */
+    int32_t *used_hwm;      /* [1] */
+    int32_t n_slots;
+    int32_t max_blocks;
+    int32_t block_size;     /* 32 */
+} lstk_kv_pages;
+int lstk_cuda_kv_alloc(const lstk_kv_pages *state, const int32_t *slots, const int32_t *counts, int32_t n,
+                       int32_t max_tokens, int64_t *cells, int32_t *positions, int32_t *ok, void *stream);
+int lstk_cuda_kv_release(const lstk_kv_pages *state, int32_t slot, int32_t keep, void *stream);
+
 /* ---- One context over several processes / GPUs: peer-memory exchange and merge -------------
  * (no counterpart in the reference, which runs in one process). Rank r of R decodes its
  * contiguous chunk of a sequence's pages with lstk_cuda_attn_decode(..., lse_out) and then calls

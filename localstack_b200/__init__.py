@@ -16,3 +16,4 @@ from .attn import (  # noqa: F401
     rope_table,
     rope_table_host,
 )
+from .pages import DevicePages  # noqa: F401,E402

@@ -64,6 +64,13 @@ _SZ = ctypes.c_size_t
 _LP = ctypes.POINTER(KvLayout)
 
 
+class KvPages(ctypes.Structure):
+    """lstk_kv_pages (include/lstk_cuda_attn.h): device-side KvCache state."""
+    _fields_ = [("free_blocks", ctypes.c_void_p), ("free_top", ctypes.c_void_p), ("block_tables", ctypes.c_void_p),
+                ("seq_lens", ctypes.c_void_p), ("used_hwm", ctypes.c_void_p), ("n_slots", ctypes.c_int32),
+                ("max_blocks", ctypes.c_int32), ("block_size", ctypes.c_int32)]
+
+
 def declared_symbols():
     """Names of every function declared in include/lstk_cuda_attn.h."""
     with open(HEADER) as f:
@@ -103,6 +110,8 @@ def lib():
     L.lstk_cuda_attn_prefill_workspace_size.restype = _SZ
     L.lstk_cuda_attn_prefill.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _F, _P,
                                          _P, _SZ, _P]
+    L.lstk_cuda_kv_alloc.argtypes = [_P, _P, _P, _I32, _I32, _P, _P, _P, _P]
+    L.lstk_cuda_kv_release.argtypes = [_P, _I32, _I32, _P]
     _lib = L
     return L
 

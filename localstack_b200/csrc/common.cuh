@@ -34,6 +34,8 @@ enum : int {
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
     kSiteExchangeWait = 30,
+    kSitePagesSlot = 40,
+    kSitePagesTokens = 41,
 };
 
 __device__ __forceinline__ void report(DeviceStatus *st, int code, int where, int detail) {

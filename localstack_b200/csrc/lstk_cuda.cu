@@ -6,6 +6,7 @@
 #include "exchange.cuh"
 #include "host_util.h"
 #include "kv_append.cuh"
+#include "kv_pages.cuh"
 #include "prefill.cuh"
 
 #include "lstk_cuda_attn.h"
@@ -494,6 +495,43 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
     cfg.numAttrs = 1;
     return launch_pdl_check(cudaLaunchKernelEx(&cfg, prefill::prefill_kernel, qmap, kmap, vmap, omap, p),
                             "prefill_kernel");
+}
+
+static int pages_state(const lstk_kv_pages *st, pages::State *out) {
+    if (!st || !st->free_blocks || !st->free_top || !st->block_tables || !st->seq_lens || !st->used_hwm ||
+        st->n_slots <= 0 || st->max_blocks <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_kv_pages: bad state");
+    if (st->block_size != pages::kBlock)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_kv_pages: block_size must be 32");
+    *out = {st->free_blocks, st->free_top, st->block_tables, st->seq_lens, st->used_hwm, st->n_slots, st->max_blocks};
+    return LSTK_OK;
+}
+
+int lstk_cuda_kv_alloc(const lstk_kv_pages *state, const int32_t *slots, const int32_t *counts, int32_t n,
+                       int32_t max_tokens, int64_t *cells, int32_t *positions, int32_t *ok, void *stream) {
+    pages::State st;
+    int rc = pages_state(state, &st);
+    if (rc) return rc;
+    if (n < 0 || max_tokens < 0 || (n > 0 && (!slots || !ok || (max_tokens > 0 && (!cells || !positions)))))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_alloc: bad arguments");
+    if (n > pages::kMaxSlots) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_kv_alloc: more than 2048 slots");
+    if (n == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(state->block_tables, &dev))) return rc;
+    pages::alloc_kernel<<<1, pages::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(st, slots, counts, n, max_tokens,
+                                                                                    cells, positions, ok, dev->status);
+    return launch_check("alloc_kernel");
+}
+
+int lstk_cuda_kv_release(const lstk_kv_pages *state, int32_t slot, int32_t keep, void *stream) {
+    pages::State st;
+    int rc = pages_state(state, &st);
+    if (rc) return rc;
+    if (slot < 0 || slot >= state->n_slots) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_release: bad slot");
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(state->block_tables, &dev))) return rc;
+    pages::release_kernel<<<1, pages::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(st, slot, keep);
+    return launch_check("release_kernel");
 }
 
 size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim) {

@@ -90,6 +90,25 @@ def test_validation_errors_without_gpu():
     assert rc == _lib.LSTK_OK
 
 
+def test_kv_pages_validation_without_gpu():
+    lib = L.lib()
+    fake = 0x10000
+    st = lambda bs=32, n_slots=4: _lib.KvPages(fake, fake, fake, fake, fake, n_slots, 8, bs)
+    alloc = lambda state, slots=fake, n=1, cap=1, cells=fake: lib.lstk_cuda_kv_alloc(state, slots, NULL, n, cap, cells,
+                                                                                     fake, fake, NULL)
+    assert alloc(None) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st(bs=16))) == _lib.LSTK_ERR_UNSUPPORTED
+    assert alloc(ctypes.byref(st(n_slots=0))) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st()), slots=NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st()), n=-1) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st()), cap=-1) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st()), cells=NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert alloc(ctypes.byref(st()), n=2049, cap=2049) == _lib.LSTK_ERR_CAPACITY
+    assert alloc(ctypes.byref(st()), n=0) == _lib.LSTK_OK
+    assert lib.lstk_cuda_kv_release(ctypes.byref(st()), 4, 0, NULL) == _lib.LSTK_ERR_INVALID_ARG
+    assert lib.lstk_cuda_kv_release(ctypes.byref(st()), -1, 0, NULL) == _lib.LSTK_ERR_INVALID_ARG
+
+
 def test_decode_partial_validates_range():
     lib = L.lib()
     lay = _layout()
