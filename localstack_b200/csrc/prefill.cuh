@@ -10,25 +10,34 @@
 // (64, G, 128/G) loads exactly that row order. K/V tiles are 128 keys = 4 pages, each page
 // fetched by TMA through the block table (box (64, 1, 32), 128-byte swizzle).
 //
-// Pipeline (one CTA per SM: 160 KiB of shared memory, 512 TMEM columns):
-//   warp 8  TMA producer: Q once, then K_j / V_j into double buffers.
+// Pipeline (one CTA per SM: 163 KiB of shared memory, 512 TMEM columns):
+//   warps 8, 10  TMA producers: Q once and K_j (warp 8), V_j (warp 10), each into a double
+//           buffer; the block table is read a warp at a time, one chunk of 32 pages ahead.
 //   warp 9  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
 //           waiting for softmax j, so the tensor core computes the next scores while the
 //           softmax warps work; then O += P_j V_j with P_j read from tensor memory (TS form).
-//   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and the 64 score columns
-//           of half w/4, so two warps on each SM sub-partition share the tile's exp work. Per
-//           tile: tcgen05.ld of its 64 scores, causal mask, row max (the two halves exchange
-//           theirs through spare TMEM columns), P = 2^(s*scale - m) as f16 pairs and their sum,
-//           P written back over the first 32 of its own 64 score columns. The running max only
-//           moves (and O is rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
-//           the softmax rarely waits for the previous PV. Epilogue: O / l; a full tile is
-//           staged in the (then free) K buffers and leaves through TMA stores.
+//   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and key half w/4 of every
+//           tile (its 64 score columns), so two warps on each SM sub-partition share the tile's
+//           exp work. Each key half keeps its own running max, row sum and O accumulator (O_0,
+//           O_1), so the halves never wait for each other inside the loop. Per tile: tcgen05.ld
+//           of its 64 scores, causal mask, row max, P = 2^(s*scale - m) as f16 pairs, their sum
+//           by mixed-precision adds, P written back over the first 32 of its 64 score columns.
+//           The running max only moves (and O_h is rescaled in TMEM) when a tile's max exceeds
+//           it by more than 2^8, so the softmax rarely waits for the previous PV. Epilogue: the
+//           halves swap (m, l) per row through shared memory and merge O = (O_0 2^(m_0-M) +
+//           O_1 2^(m_1-M)) / (l_0 2^(m_0-M) + l_1 2^(m_1-M)); a full tile is staged in the (then
+//           free) K buffers and leaves through TMA stores.
 // The kernel is launched with programmatic stream serialization: barrier and TMEM set-up overlap
 // the previous kernel, and griddepcontrol.wait precedes every read of earlier work.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (f32, 128 lanes = 128 rows), row-max exchange
-// cols [384,388) (two per tile parity), row-sum exchange [388,390). P_j occupies S_j's columns
-// [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2} overwrites them only after PV_j, which
-// the tensor core executes first.
+// TMEM: S0 cols [0,128), S1 [128,256), O_0 [256,384), O_1 [384,512) (f32, 128 lanes = 128 rows).
+// P_j occupies S_j's columns [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2}
+// overwrites them only after PV_j, which the tensor core executes first.
+// Every mbarrier wait is on a parity at most one phase from the arrivals: per-buffer barriers
+// (K, V, S, P), and the o_done phases are waited in order.
+// Measured limit: per 128-key tile the tensor core runs 8 SS MMAs (S) and 8 TS MMAs (PV) of
+// 128x128x16; alternating the two forms costs well above the nominal 64 cycles per MMA, and
+// the issuing thread stays blocked on the MMA queue, so the softmax (about half the tile time)
+// is hidden and the kernel is bound by the tensor pipe's rate for this mix.
 //
 // Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
 //   Q, K: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
@@ -49,18 +58,19 @@ constexpr int kPage = 32;
 constexpr int kTile = kBM * kD * 2;  // 32 KiB
 constexpr int kSub = kTile / 2;      // 16 KiB: 128 rows x 128 B
 constexpr int kSoftmaxWarps = 8;
-constexpr int kWarpTma = 8;
+constexpr int kWarpTmaK = 8;   // Q and K producer
 constexpr int kWarpMma = 9;
-constexpr int kThreads = 320;
+constexpr int kWarpTmaV = 10;  // V producer
+constexpr int kThreads = 352;
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColXmax = 384, kColXsum = 388;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 384;
 
 // Shared memory carve-up (offsets from a 1024-aligned base).
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;       // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
 constexpr int kOffBar = kOffV + 2 * kTile;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
+constexpr int kSmemBytes = kOffBar + 2304 + 1024;  // + barriers and row statistics + alignment slack
 
 struct Params {
     int n_seqs, n_head, n_head_kv, group, n_qt;
@@ -80,14 +90,18 @@ struct Barriers {
     uint64_t q_full;
     uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
     uint64_t s_full[2];
-    uint64_t p_full;  // one arrival per softmax warp
+    // P_j of key half h: one arrival per softmax warp of that half, on p_full[h][j % 2]. A barrier
+    // per S buffer keeps every wait within one phase of the arrivals: P_{j+2} needs S_{j+2},
+    // which the MMA issuer creates only after it has seen P_j.
+    uint64_t p_full[2][2];
     uint64_t o_done;
     uint64_t mma_drain;
-    uint64_t pair[4];  // per TMEM quadrant: the two softmax warps sharing its rows
     uint32_t tmem_base;
     int abort;
+    float row_m[2][kBM], row_l[2][kBM];  // per key half: running max (log2 domain) and sum per row
 };
-static_assert(kOffBar + sizeof(Barriers) + 1024 <= 232448, "shared memory over the 227 KiB limit");
+static_assert(sizeof(Barriers) <= 2304, "barrier block over its reserved bytes");
+static_assert(kSmemBytes <= 232448, "shared memory over the 227 KiB limit");
 
 // ---- tcgen05 wrappers ---------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -198,28 +212,26 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 
 // Softmax numerator for two adjacent scores with packed instructions: x = s * scale_log2 - mu
 // for both (fma.f32x2), rounded to an f16 pair, 2^x for both (ex2.approx.f16x2; P is consumed
-// as f16 by the PV MMA anyway), and the two f16 results added in f32 to a running pair of row
-// sums (add.f32x2), so the normaliser sums exactly the P the tensor core multiplies. Returns the
-// f16 pair (lower half = first score).
-__device__ __forceinline__ uint32_t softmax_pair(float s0, float s1, uint64_t scale2, uint64_t neg_mu2,
-                                                 uint64_t &sum2) {
+// as f16 by the PV MMA anyway), and the two f16 results added to two f32 row sums by
+// mixed-precision adds (add.f32.f16), so the normaliser sums exactly the P the tensor core
+// multiplies. Returns the f16 pair (lower half = first score).
+__device__ __forceinline__ uint32_t softmax_pair(float s0, float s1, uint64_t scale2, uint64_t neg_mu2, float &sum_lo,
+                                                 float &sum_hi) {
     uint32_t p;
     asm("{\n\t"
         ".reg .b64 x, y;\n\t"
         ".reg .f32 a, b;\n\t"
         ".reg .b16 lo, hi;\n\t"
-        "mov.b64 x, {%2, %3};\n\t"
-        "fma.rn.f32x2 y, x, %4, %5;\n\t"
+        "mov.b64 x, {%3, %4};\n\t"
+        "fma.rn.f32x2 y, x, %5, %6;\n\t"
         "mov.b64 {a, b}, y;\n\t"
         "cvt.rn.f16x2.f32 %0, b, a;\n\t"
         "ex2.approx.f16x2 %0, %0;\n\t"
         "mov.b32 {lo, hi}, %0;\n\t"
-        "cvt.f32.f16 a, lo;\n\t"
-        "cvt.f32.f16 b, hi;\n\t"
-        "mov.b64 x, {a, b};\n\t"
-        "add.f32x2 %1, %1, x;\n\t"
+        "add.f32.f16 %1, lo, %1;\n\t"
+        "add.f32.f16 %2, hi, %2;\n\t"
         "}"
-        : "=r"(p), "+l"(sum2)
+        : "=r"(p), "+f"(sum_lo), "+f"(sum_hi)
         : "f"(s0), "f"(s1), "l"(scale2), "l"(neg_mu2));
     return p;
 }
@@ -259,8 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_init(smem_u32(&bars->v_empty[i]), 1);
             mbar_init(smem_u32(&bars->s_full[i]), 1);
         }
-        mbar_init(smem_u32(&bars->p_full), kSoftmaxWarps);
-        for (int q = 0; q < 4; q++) mbar_init(smem_u32(&bars->pair[q]), 2);
+        for (int h = 0; h < 2; h++)
+            for (int i = 0; i < 2; i++) mbar_init(smem_u32(&bars->p_full[h][i]), kSoftmaxWarps / 2);
         mbar_init(smem_u32(&bars->o_done), 1);
         mbar_init(smem_u32(&bars->mma_drain), 1);
         fence_barrier_init();
@@ -296,59 +308,82 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int n_keys = tok0 < n_q ? max(0, min(kv_len, pos0 + last_tok + 1)) : 0;
     const int n_tiles = (n_keys + kBN - 1) / kBN;
 
-    if (warp == kWarpTma) {
-        // ---- TMA producer ----
-        if (lane == 0 && n_tiles > 0) {
-            prefetch_tensormap(&qmap);
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
+    if (warp == kWarpTmaK || warp == kWarpTmaV) {
+        // ---- TMA producers: warp 8 streams Q and the K tiles, warp 10 the V tiles, each into
+        // its own double buffer, so a K tile never waits behind the PV that frees a V buffer.
+        // The block table is read a warp at a time (lane i: page 32c + i, one chunk ahead) and
+        // lane 0 issues the copies. ----
+        const bool is_k = warp == kWarpTmaK;
+        if (n_tiles > 0) {
+            if (lane == 0) {
+                if (is_k) {
+                    prefetch_tensormap(&qmap);
+                    prefetch_tensormap(&kmap);
+                } else {
+                    prefetch_tensormap(&vmap);
+                }
+            }
             const int32_t *bt = p.block_tables + (int64_t) b * p.max_blocks;
-            mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
-            for (int h = 0; h < 2; h++)
-                tma_load_3d(sQ + h * kSub, &qmap, smem_u32(&bars->q_full), h * 64, kvh * G, q_begin + tok0);
-            int n_k = 0, n_v = 0;  // K and V tiles issued
+            const int n_pg = (n_keys + kPage - 1) / kPage;  // pages holding visible keys
+            auto load_chunk = [&](int chunk) -> int {
+                const int pi = chunk * 32 + lane;
+                int cell = (int) p.n_cells;  // out of bounds: TMA fills zeros
+                if (pi < n_pg) {
+                    const int32_t pid = bt[pi];
+                    if (pid >= 0 && pid < p.n_pages) cell = pid * kPage;
+                    else if (is_k) report(p.status, kStatusBadIndex, kSitePrefillPage, pid);
+                }
+                return cell;
+            };
+            int cur = load_chunk(0);
+            int nxt = n_pg > 32 ? load_chunk(1) : (int) p.n_cells;
+            if (is_k && lane == 0) {
+                mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
+                for (int h = 0; h < 2; h++)
+                    tma_load_3d(sQ + h * kSub, &qmap, smem_u32(&bars->q_full), h * 64, kvh * G, q_begin + tok0);
+            }
+            const uint32_t dst0 = is_k ? sK : sV;
+            const CUtensorMap *map = is_k ? &kmap : &vmap;
+            int n_issued = 0;
             bool ok = true;
-            for (int j = 0; j < n_tiles && ok; j++) {
-                const int buf = j & 1;
-                const uint32_t use = (uint32_t) (j >> 1);
+            for (int j = 0; j < n_tiles; j++) {
+                if (j > 0 && (j & 7) == 0) {  // next 32 pages: 8 tiles
+                    cur = nxt;
+                    nxt = (j / 8 + 1) * 32 < n_pg ? load_chunk(j / 8 + 1) : (int) p.n_cells;
+                }
                 int cell0[4];
-                for (int q = 0; q < 4; q++) {
-                    const int pi = j * 4 + q;
-                    cell0[q] = (int) p.n_cells;  // out of bounds: TMA fills zeros
-                    if (pi * kPage < n_keys) {
-                        const int32_t pid = bt[pi];
-                        if (pid >= 0 && pid < p.n_pages) cell0[q] = pid * kPage;
-                        else report(p.status, kStatusBadIndex, kSitePrefillPage, pid);
+#pragma unroll
+                for (int q = 0; q < 4; q++) cell0[q] = __shfl_sync(0xffffffffu, cur, (j & 7) * 4 + q);
+                if (lane == 0) {
+                    const int buf = j & 1;
+                    const uint32_t use = (uint32_t) (j >> 1);
+                    const uint32_t empty = smem_u32(is_k ? &bars->k_empty[buf] : &bars->v_empty[buf]);
+                    const uint32_t full = smem_u32(is_k ? &bars->k_full[buf] : &bars->v_full[buf]);
+                    if (use > 0) ok = mbar_wait_bounded(empty, (use - 1) & 1, abort_flag);
+                    if (ok) {
+                        mbar_arrive_expect_tx(full, kTile);
+                        for (int q = 0; q < 4; q++)
+                            for (int h = 0; h < 2; h++)
+                                tma_load_3d(dst0 + buf * kTile + h * kSub + q * (kPage * 128), map, full, h * 64, kvh,
+                                            cell0[q]);
                     }
                 }
-                if (use > 0) ok = mbar_wait_bounded(smem_u32(&bars->k_empty[buf]), (use - 1) & 1, abort_flag);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
-                mbar_arrive_expect_tx(smem_u32(&bars->k_full[buf]), kTile);
-                for (int q = 0; q < 4; q++)
-                    for (int h = 0; h < 2; h++)
-                        tma_load_3d(sK + buf * kTile + h * kSub + q * (kPage * 128), &kmap,
-                                    smem_u32(&bars->k_full[buf]), h * 64, kvh, cell0[q]);
-                n_k++;
-                if (use > 0) ok = mbar_wait_bounded(smem_u32(&bars->v_empty[buf]), (use - 1) & 1, abort_flag);
-                if (!ok) break;
-                mbar_arrive_expect_tx(smem_u32(&bars->v_full[buf]), kTile);
-                for (int q = 0; q < 4; q++)
-                    for (int h = 0; h < 2; h++)
-                        tma_load_3d(sV + buf * kTile + h * kSub + q * (kPage * 128), &vmap,
-                                    smem_u32(&bars->v_full[buf]), h * 64, kvh, cell0[q]);
-                n_v++;
+                n_issued++;
             }
-            if (!ok) {
-                report(p.status, kStatusTimeout, kSitePrefillWait, kWarpTma);
-                *abort_flag = 1;
-            }
-            if (*abort_flag) {
-                // Drain: every load still in flight lands before shared memory is released.
-                mbar_wait_bounded(smem_u32(&bars->q_full), 0, nullptr);
-                for (int j = max(0, n_k - 2); j < n_k; j++)
-                    mbar_wait_bounded(smem_u32(&bars->k_full[j & 1]), (uint32_t) (j >> 1) & 1, nullptr);
-                for (int j = max(0, n_v - 2); j < n_v; j++)
-                    mbar_wait_bounded(smem_u32(&bars->v_full[j & 1]), (uint32_t) (j >> 1) & 1, nullptr);
+            if (lane == 0) {
+                if (!ok) {
+                    report(p.status, kStatusTimeout, kSitePrefillWait, warp);
+                    *abort_flag = 1;
+                }
+                if (*abort_flag) {
+                    // Drain: every load still in flight lands before shared memory is released.
+                    if (is_k) mbar_wait_bounded(smem_u32(&bars->q_full), 0, nullptr);
+                    for (int j = max(0, n_issued - 2); j < n_issued; j++)
+                        mbar_wait_bounded(smem_u32(is_k ? &bars->k_full[j & 1] : &bars->v_full[j & 1]),
+                                          (uint32_t) (j >> 1) & 1, nullptr);
+                }
             }
         }
     } else if (warp == kWarpMma) {
@@ -380,21 +415,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     break;
                 }
                 const int buf = j & 1;
-                if (!mbar_wait_bounded(smem_u32(&bars->p_full), (uint32_t) j & 1, abort_flag) ||
-                    !mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
+                if (!mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
                 // P_j sits in TMEM over S_j: keys 0..63 in columns [0, 32), keys 64..127 in
                 // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
+                // Key half h accumulates into its own O_h, as soon as its four warps are done.
                 const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
+                for (int h = 0; h < 2 && ok; h++) {
+                    if (!mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
-                    mma_f16_ts(tmem + kColO, pcol + (uint32_t) ((kk >> 2) * 64 + (kk & 3) * 8),
-                               sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    for (int kq = 0; kq < 4; kq++) {
+                        const int kk = 4 * h + kq;
+                        const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
+                        mma_f16_ts(tmem + (h ? kColO1 : kColO0), pcol + (uint32_t) (h * 64 + kq * 8),
+                                   sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
+                                   (j > 0 || kq > 0) ? 1u : 0u);
+                    }
                 }
+                if (!ok) break;
                 mma_commit(smem_u32(&bars->o_done));
                 mma_commit(smem_u32(&bars->v_empty[buf]));
             }
@@ -407,28 +451,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
         }
     } else {
-        // ---- softmax warps 0..7: warp w owns rows 32*(w%4).. and score columns 64*(w/4).. ----
+        // ---- softmax warps 0..7: warp w owns rows 32*(w%4).. and the key half w/4 of every
+        // tile (score columns 64*(w/4)..); each half keeps its own running max, sum and O ----
         const int hf = warp >> 2;
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // row within the tile
         const uint32_t lane_base = tmem + ((uint32_t) (quad * 32) << 16);
+        const uint32_t ocol = lane_base + (hf ? kColO1 : kColO0);
         const int tq = tok0 + r / G;  // query token index within the sequence
         const int head = kvh * G + r % G;
         const int row_keys = min(kv_len, pos0 + tq + 1);  // keys [0, row_keys) are visible
-        const uint32_t pair_bar = smem_u32(&bars->pair[quad]);
-        uint32_t pair_uses = 0;
-        // Both warps sharing these rows have passed this point (bounded; false on timeout / abort).
-        auto pair_sync = [&]() -> bool {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(pair_bar);
-            const bool okw = __all_sync(0xffffffffu, mbar_wait_bounded(pair_bar, pair_uses & 1, abort_flag));
-            pair_uses++;
-            tc_fence_after();
-            return okw;
-        };
         const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
-        float m = -INFINITY, l = 0.f;  // l: this warp's half of the row sum
+        float m = -INFINITY, l = 0.f;  // this key half's running max (log2 domain) and sum
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
             const int buf = j & 1;
@@ -456,29 +490,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             for (int c = 16; c < 64; c += 16)
 #pragma unroll
                 for (int i = 0; i < 8; i++) mx[i] = max3(mx[i], sc[c + i], sc[c + 8 + i]);
-            const float half_max =
-                fmaxf(max3(mx[0], mx[1], mx[2]), fmaxf(max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            // Exchange the half-row maxima through TMEM (columns by iteration parity, so a warp
-            // that runs ahead never overwrites a value its partner has not read).
-            tmem_st1(lane_base + kColXmax + 2 * buf + hf, half_max);
-            tmem_wait_st();
-            if (!pair_sync()) {
-                ok = false;
-                break;
-            }
-            const float other = tmem_ld1(lane_base + kColXmax + 2 * buf + (hf ^ 1));
-            tmem_wait_ld();
-            const float m_tile = fmaxf(half_max, other) * p.scale_log2;
+            const float m_tile =
+                fmaxf(max3(mx[0], mx[1], mx[2]), fmaxf(max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                p.scale_log2;
             const bool move = m_tile > m + kRescaleThreshold;  // always true for the first visible tile
             const float m_new = move ? m_tile : m;
             const float alpha = move ? fast_exp2(m - m_new) : 1.f;
             const float mu = m_new == -INFINITY ? 0.f : m_new;
             const uint64_t neg_mu2 = pack_f32x2(-mu, -mu);
-            uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};  // independent pairs of partial row sums
+            float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial row sums
             uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 32; c++) pk[c] = softmax_pair(sc[2 * c], sc[2 * c + 1], scale2, neg_mu2, sum2[c & 3]);
-            // A moved max rescales O, which PV_{j-1} must have finished updating (PV_{j-2} has:
+            for (int c = 0; c < 32; c++)
+                pk[c] = softmax_pair(sc[2 * c], sc[2 * c + 1], scale2, neg_mu2, rsum[2 * (c & 3)], rsum[2 * (c & 3) + 1]);
+            // A moved max rescales O_hf, which PV_{j-1} must have finished updating (PV_{j-2} has:
             // S_j ready implies it). P_j goes to buffer j%2, last read by PV_{j-2}: no wait.
             if (j > 0 && __any_sync(0xffffffffu, move)) {
                 if (!__all_sync(0xffffffffu,
@@ -488,18 +513,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < 4; c++) {
                     float o[32];
-                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
+                    tmem_ld32(ocol + c * 32, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; i++) o[i] *= alpha;
-                    tmem_st32(lane_base + kColO + 64 * hf + c * 32, o);
+                    tmem_st32(ocol + c * 32, o);
                 }
-                tmem_wait_st();
             }
             // P row r, keys 64*hf.., packed f16 pairs, over the first 32 of this warp's own 64
-            // score columns (already read; the partner warp's columns are untouched), where the
+            // score columns (already read; the other half's columns are untouched), where the
             // PV MMA reads its A operand from tensor memory.
             {
                 float pkf[32];
@@ -510,37 +534,47 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
-            const float rs = (__uint_as_float((uint32_t) sum2[0]) + __uint_as_float((uint32_t) (sum2[0] >> 32))) +
-                             (__uint_as_float((uint32_t) sum2[1]) + __uint_as_float((uint32_t) (sum2[1] >> 32))) +
-                             (__uint_as_float((uint32_t) sum2[2]) + __uint_as_float((uint32_t) (sum2[2] >> 32))) +
-                             (__uint_as_float((uint32_t) sum2[3]) + __uint_as_float((uint32_t) (sum2[3] >> 32)));
+            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[hf][buf]));
+            const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
             l = l * alpha + rs;
             m = m_new;
         }
-        // Epilogue: O / (l_0 + l_1); this warp writes its 64 output columns of the row.
-        if (ok && n_tiles > 0)
-            ok = __all_sync(0xffffffffu,
-                            mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (n_tiles - 1) & 1, abort_flag));
-        float l_row = 0.f;
-        if (ok && n_tiles > 0) {
-            tc_fence_after();
-            tmem_st1(lane_base + kColXsum + hf, l);
-            tmem_wait_st();
-            ok = pair_sync();
-            if (ok) {
-                l_row = l + tmem_ld1(lane_base + kColXsum + (hf ^ 1));
-                tmem_wait_ld();
-            }
-        }
+        // Epilogue: after the last PV the halves swap (m, l) per row and merge
+        // O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M));
+        // warp w writes output columns 64*(w/4) .. +63.
+        // o_done phases in order: S_{n-1}, which this warp has seen, was issued before PV_{n-2},
+        // so that phase may still be open, and a parity wait must never skip one.
+        for (int jj = max(0, n_tiles - 2); ok && jj < n_tiles; jj++)
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) jj & 1, abort_flag));
+        bars->row_m[hf][r] = m;
+        bars->row_l[hf][r] = l;
+        tc_fence_before();
+        asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
+        tc_fence_after();
+        const float m_o = bars->row_m[hf ^ 1][r], l_o = bars->row_l[hf ^ 1][r];
+        const float mm = fmaxf(m, m_o);
+        const float a_me = l > 0.f ? fast_exp2(m - mm) : 0.f;
+        const float a_ot = l_o > 0.f ? fast_exp2(m_o - mm) : 0.f;
+        const float den = l * a_me + l_o * a_ot;
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        const float c0 = (hf == 0 ? a_me : a_ot) * inv;  // weight of O_0
+        const float c1 = (hf == 0 ? a_ot : a_me) * inv;  // weight of O_1
+        const bool use0 = c0 > 0.f, use1 = c1 > 0.f;      // an O that never saw a visible key is not read
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) {
             report(p.status, kStatusTimeout, kSitePrefillWait, warp);
             *abort_flag = 1;
         }
-        tc_fence_after();
         const bool live = tq < n_q;
-        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        // Output columns 64*hf + 32c .. +31 of row r: the merged O / l.
+        auto merged = [&](int c, float o[32]) {
+            float a[32], b2[32];
+            tmem_ld32(lane_base + kColO0 + 64 * hf + 32 * c, a);
+            tmem_ld32(lane_base + kColO1 + 64 * hf + 32 * c, b2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] = (use0 ? a[i] * c0 : 0.f) + (use1 ? b2[i] * c1 : 0.f);
+        };
         if (tok0 + kBM / G <= n_q && n_tiles > 0) {
             // A full tile leaves through TMA stores: O / l is staged in the K buffers (free: the
             // last QK and PV have completed) as four 32-column boxes of 128 rows x 128 B with the
@@ -549,15 +583,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     float o[32];
-                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
-                    tmem_wait_ld();
+                    merged(c, o);
                     const uint32_t box = sK + (uint32_t) (2 * hf + c) * kSub;
 #pragma unroll
                     for (int ch = 0; ch < 8; ch++)
                         asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
                                          box + sw128_offset((uint32_t) r, (uint32_t) ch)),
-                                     "f"(o[4 * ch] * inv), "f"(o[4 * ch + 1] * inv), "f"(o[4 * ch + 2] * inv),
-                                     "f"(o[4 * ch + 3] * inv)
+                                     "f"(o[4 * ch]), "f"(o[4 * ch + 1]), "f"(o[4 * ch + 2]), "f"(o[4 * ch + 3])
                                      : "memory");
                 }
                 fence_proxy_async_smem();
@@ -574,8 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             for (int c = 0; c < 2; c++) {
                 float o[32];
                 if (n_tiles > 0 && ok) {
-                    tmem_ld32(lane_base + kColO + 64 * hf + c * 32, o);
-                    tmem_wait_ld();
+                    merged(c, o);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i++) o[i] = 0.f;
@@ -583,8 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 if (live) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4 *>(dst + c * 32 + i) =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                        *reinterpret_cast<float4 *>(dst + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
                 }
             }
         }

@@ -74,6 +74,33 @@ def test_long_ragged_batch():
     assert within(out, ex), max_err(out, ex)
 
 
+def test_long_prompt_many_key_tiles():
+    """An 8192-token prompt (64 key tiles per query tile, 2048 CTAs), repeated: the pipeline's
+    barriers must hold over long runs (a parity wait that skips a phase stalls until its bound and
+    reports a timeout). Checked against a plain fp32 torch restatement of causal attention over
+    the gathered pages (the oracle is too slow at this size)."""
+    rng = np.random.default_rng(44)
+    T, Hq, Hkv = 8192, 32, 4
+    bt, n_pages = scattered_block_tables(rng, [T])
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    q16 = random_q(rng, T, Hq).astype(np.float16)
+    k_t, v_t, bt_t, q_t = _f16(kc), _f16(vc), torch.from_numpy(bt).to(DEV), torch.from_numpy(q16).to(DEV)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=DEV)
+    for _ in range(3):
+        out = L.attn_prefill(k_t, v_t, q_t, i32(0, T), i32(0), i32(T), bt_t, T, SCALE)
+        L.check_status()
+    cells = (bt_t[0].long()[:, None] * 32 + torch.arange(32, device=DEV)).reshape(-1)[:T]
+    K, V, Q = k_t[cells].float(), v_t[cells].float(), q_t.float()
+    mask = torch.ones(T, T, dtype=torch.bool, device=DEV).tril()
+    G = Hq // Hkv
+    ref = torch.empty(T, Hq, 128, device=DEV)
+    for h in range(Hq):
+        s = (Q[:, h] @ K[:, h // G].T) * SCALE
+        ref[:, h] = torch.softmax(s.masked_fill(~mask, float("-inf")), dim=-1) @ V[:, h // G]
+    got, want = out.cpu().numpy(), ref.cpu().numpy()
+    assert within(got, want), max_err(got, want)
+
+
 def test_f32_query_input():
     out, ex = _prefill_case([129, 64], [5, 0], 16, 8, seed=8, q_dtype=torch.float32)
     assert within(out, ex), max_err(out, ex)
