@@ -79,7 +79,8 @@ int lstk_rope_table_fill(float *host_table, int32_t n_pos, int32_t head_dim, flo
  *   K head rows: the same with k_gamma -> f16 (round-to-nearest-even) into k_cache at cells[t];
  *   V head rows: -> f16 into v_cache at cells[t].
  * Inputs are token-major rows [T][H][D] (f32 or bf16) with a per-token stride in elements, so a
- * fused QKV projection output can be passed as three views. q_gamma / k_gamma may be NULL
+ * fused QKV projection output can be passed as three views; strides are whole 16-byte units
+ * (multiples of 4 f32 / 8 bf16 elements) and all pointers 16-byte aligned. q_gamma / k_gamma may be NULL
  * (no QK-norm, as for Qwen2, src/qwen3.cpp:139-140). positions must be < rope_n_pos and cells
  * < n_cells; offending tokens are skipped and set LSTK_ERR_DEVICE_INDEX in the device status.
  * Every f32 operation is separately rounded, so the written f16 pages are bit-identical to a

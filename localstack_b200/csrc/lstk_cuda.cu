@@ -32,6 +32,7 @@ struct DeviceInfo {
     DeviceStatus *status = nullptr;
     size_t decode_smem = 0;
     bool prefill_attr = false;
+    bool append_smem_set = false;
 };
 
 DeviceInfo g_devices[kMaxDevices];
@@ -191,8 +192,12 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: NULL pointer or empty rope table");
     const int hd = layout->head_dim;
     if (q_row_stride < (int64_t) n_head * hd || k_row_stride < (int64_t) layout->n_head_kv * hd ||
-        v_row_stride < (int64_t) layout->n_head_kv * hd || q_row_stride % 4 || k_row_stride % 4 || v_row_stride % 4)
-        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: row strides too small or not multiples of 4");
+        v_row_stride < (int64_t) layout->n_head_kv * hd)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: row strides too small");
+    const int64_t smul = in_dtype == LSTK_DTYPE_BF16 ? 8 : 4;  // rows start on 16-byte boundaries
+    if (q_row_stride % smul || k_row_stride % smul || v_row_stride % smul)
+        return set_error(LSTK_ERR_INVALID_ARG,
+                         "lstk_cuda_kv_append: row strides must be multiples of 16 bytes (4 f32 / 8 bf16 elements)");
     if (!aligned(q_in, 16) || !aligned(k_in, 16) || !aligned(v_in, 16) || !aligned(q_out, 16) ||
         !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(rope_table, 16))
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: pointers must be 16-byte aligned");
@@ -224,14 +229,26 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     p.q_out_f16 = q_out_dtype == LSTK_DTYPE_F16;
     p.status = dev->status;
     const int64_t rows = (int64_t) n_tokens * (n_head + 2 * layout->n_head_kv);
-    const int64_t groups = (rows + append::kRowsPerWarp - 1) / append::kRowsPerWarp;
+    // Rows per warp: 32 when there are enough rows for two full waves of such groups, fewer for
+    // short (decode-step) appends, which are bound by one warp's chain of dependent steps.
+    const int64_t full = (int64_t) dev->n_sms * append::kWarps * 3 * 2;  // 3 CTAs per SM, 2 waves
+    const int max_rpw = (in_dtype == LSTK_DTYPE_F32 || q_out_dtype == LSTK_DTYPE_F32) ? 16 : 32;
+    p.rows_per_warp = std::min(max_rpw, rows >= full * 32 ? 32 : rows >= full * 16 ? 16 : 8);
+    const int64_t groups = (rows + p.rows_per_warp - 1) / p.rows_per_warp;
     const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * 16);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
+    if (!dev->append_smem_set) {
+        const cudaError_t e = cudaFuncSetAttribute(append::kv_append_kernel,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, append::kSmemBytes);
+        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(kv_append)", e));
+        dev->append_smem_set = true;
+    }
     cfg.gridDim = dim3((unsigned) blocks);
     cfg.blockDim = dim3(append::kWarps * 32);
+    cfg.dynamicSmemBytes = append::kSmemBytes;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cfg.attrs = attr;
     cfg.numAttrs = 1;

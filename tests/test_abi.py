@@ -76,6 +76,8 @@ def test_validation_errors_without_gpu():
                                                 8 * 128, 1, 16, fake, fake, NULL, NULL, 1e-6, fake, 10, fake, 0, NULL)
     assert lib.lstk_cuda_kv_append(*args(dt=1)) == _lib.LSTK_ERR_UNSUPPORTED
     assert lib.lstk_cuda_kv_append(*args(qs=100)) == _lib.LSTK_ERR_INVALID_ARG
+    # bf16 rows must start on 16-byte boundaries: a stride of 8-element multiples
+    assert lib.lstk_cuda_kv_append(*args(dt=_lib.DTYPE_BF16, qs=16 * 128 + 4)) == _lib.LSTK_ERR_INVALID_ARG
     assert lib.lstk_cuda_kv_append(*args(ptr=ctypes.c_void_p(0x10002))) == _lib.LSTK_ERR_INVALID_ARG
     # prefill: GQA group 3 cannot tile 128 rows
     rc = lib.lstk_cuda_attn_prefill(ctypes.byref(_layout(hkv=4)), fake, fake, fake, 1, 1, 12, fake, 1, 1, fake, fake,
