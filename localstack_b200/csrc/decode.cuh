@@ -509,17 +509,28 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     den = warp_sum_xor(den, 1);
     if (lane == 0) red_sum[warp] = den;
     __syncthreads();
-    // Pass 3: warp k sums pieces k, k + 8, ...
+    // Pass 3: warp k sums pieces k, k + 8, ..., loading 8 of them at a time before any use, so a
+    // long sequence split over many CTAs costs a few memory round trips, not one per piece.
+    constexpr int kBatch = 8;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int i = warp; i < n_pc; i += kCombineWarps) {
-        const float wv = wt_s[i];
-        if (wv > 0.f) {
-            const float4 v = reinterpret_cast<const float4 *>(p.part_o + (int64_t) row_s[i] * kD)[lane];
-            acc.x += wv * v.x;
-            acc.y += wv * v.y;
-            acc.z += wv * v.z;
-            acc.w += wv * v.w;
+    for (int i0 = warp; i0 < n_pc; i0 += kCombineWarps * kBatch) {
+        float4 v[kBatch];
+        float wv[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int i = i0 + k * kCombineWarps;
+            wv[k] = i < n_pc ? wt_s[i] : 0.f;
+            v[k] = wv[k] > 0.f ? reinterpret_cast<const float4 *>(p.part_o + (int64_t) row_s[i] * kD)[lane]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            if (wv[k] > 0.f) {
+                acc.x += wv[k] * v[k].x;
+                acc.y += wv[k] * v[k].y;
+                acc.z += wv[k] * v[k].z;
+                acc.w += wv[k] * v[k].w;
+            }
         }
     }
     reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;

@@ -114,3 +114,34 @@ def test_append_bad_cell_reports_device_index():
     assert e.value.code == -6
     L.check_status()  # status is cleared once read
     assert torch.count_nonzero(kc[3]) > 0  # the valid token was still written
+
+
+@pytest.mark.parametrize("dtype,q_out_dtype", [("bf16", torch.float16), ("bf16", torch.float32),
+                                               ("f32", torch.float16)])
+def test_append_large_batch_wide_groups(dtype, q_out_dtype):
+    # Config-5 shape: 4352 tokens x (32 + 4 + 4) heads = 174,080 rows, QKV as strided views of one
+    # projection output; enough rows for 32-row groups (bf16 in, f16 Q out) or 16-row groups.
+    rng = np.random.default_rng(6)
+    T, n_cells = 4352, 8192
+    pos = rng.integers(0, 16384, T).astype(np.int32)
+    cells = rng.permutation(n_cells)[:T].astype(np.int64)
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 32, 4, n_cells, pos, cells, dtype=dtype, q_out_dtype=q_out_dtype,
+                                            fused_rows=True, seed=7)
+    assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
+    if q_out_dtype == torch.float16:
+        assert np.array_equal(q.astype(np.float16), q_ref.astype(np.float16))
+    else:
+        assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_append_groups_spanning_many_tokens(dtype):
+    # Hq 1 / Hkv 1: 3 rows per token, and enough rows for 32-row (bf16) / 16-row (f32) groups, so
+    # one group spans up to 12 tokens and the RoPE rows past its first four load in the write loop.
+    rng = np.random.default_rng(8)
+    T = 40000
+    pos = rng.integers(0, 16384, T).astype(np.int32)
+    cells = rng.permutation(T).astype(np.int64)
+    q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 1, 1, T, pos, cells, dtype=dtype, seed=9)
+    assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
+    assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32))
