@@ -12,15 +12,15 @@
 // Work decomposition. A "row" is one (token, head) vector of 128 values; rows are numbered
 // token-major: for token t, rows [t*R, t*R + R) with R = Hq + 2*Hkv are Hq query heads, Hkv key
 // heads, Hkv value heads. Each warp takes up to 32 consecutive rows (8 or 16 for short appends,
-// whose time is one warp's chain of dependent steps). Lane l owns elements
-// {2l, 2l+1, 64+2l, 65+2l} of every row - exactly its two NEOX pairs - so stores are coalesced
-// across the warp. The rows are staged into shared memory with 16-byte cp.async copies (a bf16
-// row is 16 chunks, so one warp instruction moves two rows), every copy of the group in flight
-// at once and no registers held, keeping the input type. Lane r then sums row r's squares
+// whose time is one warp's chain of dependent steps; at most 16 with f32 data). The rows, and
+// the RoPE rows of the group's first four tokens, are staged into shared memory with 16-byte
+// cp.async copies (a bf16 row is 16 chunks, so one warp instruction moves two rows), every copy
+// of the group in flight at once and no registers held. Lane r then sums row r's squares
 // sequentially in double: independent chains across the lanes, where the sequential order
-// leaves no parallelism inside a row. Lane r also prepares row r's kind, destination and RoPE
-// slot, so the warp's write loop over the rows is shuffles and branch-free arithmetic; the RoPE
-// rows of the group's first four tokens are loaded up front.
+// leaves no parallelism inside a row; it also prepares row r's kind, destination and RoPE slot.
+// The warp writes four rows per step: lanes 8s..8s+7 take one row, lane c its NEOX pairs
+// [8c, 8c+8) (elements 8c..8c+7 and 64+8c..64+8c+7), loaded and stored as 16-byte vectors with
+// branch-free arithmetic, so the per-row shuffles and address work are shared by four rows.
 #pragma once
 
 #include "common.cuh"
@@ -37,8 +37,12 @@ constexpr int kRowsPerWarp = 32;  // at most; the launch picks 8, 16 or 32 (Para
 // word (the sum) has 4-way conflicts, small next to the sum's dependent double adds.
 constexpr int kStrideBf16Words = 68;
 constexpr int kStrideF32 = 132;
-constexpr int kWarpStageBytes = kRowsPerWarp * kStrideF32 * 4;
-constexpr int kSmemBytes = kWarps * kWarpStageBytes;
+constexpr int kRowBytes = 32 * kStrideBf16Words * 4;  // rows of one group: 32 bf16 rows or 16 f32 rows
+static_assert(kRowBytes >= 16 * kStrideF32 * 4, "f32 groups hold at most 16 rows");
+constexpr int kCsTokens = 4;                               // RoPE rows staged per group
+constexpr int kWarpStageBytes = kRowBytes + kCsTokens * kD * 4;
+constexpr int kGammaBytes = 2 * kD * 4;
+constexpr int kSmemBytes = kGammaBytes + kWarps * kWarpStageBytes;
 
 struct Params {
     const void *q_in;
@@ -86,7 +90,8 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
-    extern __shared__ float stage_smem[];
+    extern __shared__ __align__(16) uint8_t stage_smem[];
+    float *s_gamma = reinterpret_cast<float *>(stage_smem);  // [2][128]: q_gamma, k_gamma (1 when absent)
 
     // Inputs may come from the previous kernel in the stream (programmatic dependent launch);
     // the decode launched after this kernel may be staged right away (it waits for completion).
@@ -94,30 +99,21 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < kD; i += blockDim.x) {
+        s_gamma[i] = p.q_gamma != nullptr ? p.q_gamma[i] : 1.f;
+        s_gamma[kD + i] = p.k_gamma != nullptr ? p.k_gamma[i] : 1.f;
+    }
+    __syncthreads();
     const int R = p.n_head + 2 * p.n_head_kv;
     const int n_qk = p.n_head + p.n_head_kv;
     const int64_t n_rows = (int64_t) p.n_tokens * R;
     const int rpw = p.rows_per_warp;
     const int64_t n_groups = (n_rows + rpw - 1) / rpw;
-    uint8_t *stage = reinterpret_cast<uint8_t *>(stage_smem) + warp * kWarpStageBytes;
+    uint8_t *stage = stage_smem + kGammaBytes + warp * kWarpStageBytes;
     const uint32_t stage_u32 = smem_u32(stage);
     const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);  // bf16 pairs
     const float *sf = reinterpret_cast<const float *>(stage);        // f32
-
-    // This lane's weight elements (2l, 2l+1, 64+2l, 65+2l) for Q and K rows.
-    float qg[4] = {1.f, 1.f, 1.f, 1.f}, kg[4] = {1.f, 1.f, 1.f, 1.f};
-    if (p.q_gamma != nullptr) {
-        qg[0] = p.q_gamma[2 * lane];
-        qg[1] = p.q_gamma[2 * lane + 1];
-        qg[2] = p.q_gamma[64 + 2 * lane];
-        qg[3] = p.q_gamma[65 + 2 * lane];
-    }
-    if (p.k_gamma != nullptr) {
-        kg[0] = p.k_gamma[2 * lane];
-        kg[1] = p.k_gamma[2 * lane + 1];
-        kg[2] = p.k_gamma[64 + 2 * lane];
-        kg[3] = p.k_gamma[65 + 2 * lane];
-    }
+    const float *s_cs = reinterpret_cast<const float *>(stage + kRowBytes);  // [kCsTokens][64] (cos, sin)
 
     for (int64_t grp = (int64_t) blockIdx.x * kWarps + warp; grp < n_groups; grp += (int64_t) gridDim.x * kWarps) {
         const int64_t row0 = grp * rpw;
@@ -159,21 +155,20 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
                     t++;
                 }
             }
-            cp_async_wait_all();
         }
-
-        // RoPE rows (cos, sin) of the group's first four tokens; the position of token t_first + u
-        // comes from the lane holding that token's first row in the group.
-        float4 cs_pre[4];
+        // RoPE rows (64 (cos, sin) pairs, 512 B) of the group's first kCsTokens tokens, staged the
+        // same way; the position of token t_first + u comes from the lane holding that token's
+        // first row in the group. Rows of a token with a bad position are never read.
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < kCsTokens; u++) {
             const int64_t first_row = (t_first + u) * R - row0;
             const int src = (int) (first_row < 0 ? 0 : (first_row > 31 ? 31 : first_row));
             const int pos = __shfl_sync(0xffffffffu, my_pos, src);
-            cs_pre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (first_row < nr && pos >= 0 && pos < p.rope_n_pos)
-                cs_pre[u] = *reinterpret_cast<const float4 *>(p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
+                cp_async_16(stage_u32 + (uint32_t) (kRowBytes + u * kD * 4 + lane * 16),
+                            p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
         }
+        cp_async_wait_all();
         __syncwarp();
 
         // Lane r: ggml rms_norm scale of row r (Q and K rows with a weight), sequential double sum.
@@ -221,60 +216,89 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         }
         const int my_u = (int) (my_t - t_first);  // RoPE slot (>= 4: loaded in the loop)
 
-        // Write out row by row; lane l produces its two NEOX pairs (2l, 64+2l), (2l+1, 65+2l).
-        // Branch-free arithmetic per row (selects), so unrolled rows overlap.
-#pragma unroll 4
-        for (int r = 0; r < nr; r++) {
-            const int kind = __shfl_sync(0xffffffffu, my_kind, r);
-            const int64_t dst = __shfl_sync(0xffffffffu, my_dst, r);
-            const float scale = __shfl_sync(0xffffffffu, my_scale, r);
-            const int u = __shfl_sync(0xffffffffu, my_u, r);
-            float x[4];
+        // Write out: lanes 8s..8s+7 take row r0 + s, four rows per warp instruction; lane c = lane & 7
+        // owns NEOX pairs [8c, 8c+8) - elements 8c..8c+7 and 64+8c..64+8c+7 - moved as 16-byte
+        // vectors. Branch-free arithmetic per element (selects).
+        const int sub = lane >> 3, c = lane & 7;
+        for (int r0 = 0; r0 < nr; r0 += 4) {
+            const int r = r0 + sub;
+            const int from = r < nr ? r : r0;
+            const int kind = __shfl_sync(0xffffffffu, my_kind, from);
+            const int64_t dst = __shfl_sync(0xffffffffu, my_dst, from);
+            const float scale = __shfl_sync(0xffffffffu, my_scale, from);
+            const int u = __shfl_sync(0xffffffffu, my_u, from);
+            const int pos = __shfl_sync(0xffffffffu, my_pos, from);
+            if (r >= nr || kind == 3) continue;  // no warp collective below
+            float x[16];
             if (p.in_bf16) {
-                const uint32_t w0 = sw[r * kStrideBf16Words + lane], w1 = sw[r * kStrideBf16Words + 32 + lane];
-                x[0] = __uint_as_float(w0 << 16);
-                x[1] = __uint_as_float(w0 & 0xffff0000u);
-                x[2] = __uint_as_float(w1 << 16);
-                x[3] = __uint_as_float(w1 & 0xffff0000u);
+                const uint8_t *row = stage + r * (kStrideBf16Words * 4);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(row + h * 128 + c * 16);
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        x[8 * h + 2 * e] = __uint_as_float(ws[e] << 16);
+                        x[8 * h + 2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
+                    }
+                }
             } else {
-                const float2 a = *reinterpret_cast<const float2 *>(sf + r * kStrideF32 + 2 * lane);
-                const float2 b = *reinterpret_cast<const float2 *>(sf + r * kStrideF32 + 64 + 2 * lane);
-                x[0] = a.x;
-                x[1] = a.y;
-                x[2] = b.x;
-                x[3] = b.y;
+                const float *row = sf + r * kStrideF32;
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        const float4 v = *reinterpret_cast<const float4 *>(row + h * 64 + c * 8 + q * 4);
+                        x[8 * h + 4 * q] = v.x;
+                        x[8 * h + 4 * q + 1] = v.y;
+                        x[8 * h + 4 * q + 2] = v.z;
+                        x[8 * h + 4 * q + 3] = v.w;
+                    }
             }
-            if (kind == 3) continue;
-            const bool is_q = kind == 0;
+            const bool is_q = kind == 0, is_v = kind == 2;
             const bool normed = is_q ? p.q_gamma != nullptr : p.k_gamma != nullptr;
-            float y[4];
+            const float *g = s_gamma + (is_q ? 0 : kD);
+            // (cos, sin) of pairs 8c..8c+7: staged for the group's first tokens, else from the table
+            // (Q / K rows have a checked position; V rows use none of it)
+            const float *csr = u < kCsTokens ? s_cs + u * kD
+                                             : is_v ? s_cs
+                                                    : reinterpret_cast<const float *>(p.rope + (int64_t) pos * (kD / 2));
+            float o[16];
 #pragma unroll
-            for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], scale), is_q ? qg[e] : kg[e]);
-            float4 cs = u == 0 ? cs_pre[0] : u == 1 ? cs_pre[1] : u == 2 ? cs_pre[2] : cs_pre[3];
-            if (u >= 4 && kind != 2) {  // Q / K rows have a checked position; V rows need none
-                const int pos = __shfl_sync(0xffffffffu, my_pos, r);
-                cs = *reinterpret_cast<const float4 *>(p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
+            for (int e = 0; e < 8; e++) {
+                const int i = 8 * c + e;  // pair (i, i + 64)
+                float a = x[e], b = x[8 + e];
+                const float ya = __fmul_rn(__fmul_rn(a, scale), g[i]);
+                const float yb = __fmul_rn(__fmul_rn(b, scale), g[i + 64]);
+                a = normed ? ya : a;
+                b = normed ? yb : b;
+                const float cx = csr[2 * i], sy = csr[2 * i + 1];
+                const float oa = __fsub_rn(__fmul_rn(a, cx), __fmul_rn(b, sy));
+                const float ob = __fadd_rn(__fmul_rn(a, sy), __fmul_rn(b, cx));
+                o[e] = is_v ? x[e] : oa;  // V rows are stored as read
+                o[8 + e] = is_v ? x[8 + e] : ob;
             }
-            float w[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) w[e] = normed ? y[e] : x[e];
-            // pair (2l, 64+2l) uses (cs.x, cs.y); pair (2l+1, 65+2l) uses (cs.z, cs.w)
-            float o[4];
-            o[0] = __fsub_rn(__fmul_rn(w[0], cs.x), __fmul_rn(w[2], cs.y));
-            o[2] = __fadd_rn(__fmul_rn(w[0], cs.y), __fmul_rn(w[2], cs.x));
-            o[1] = __fsub_rn(__fmul_rn(w[1], cs.z), __fmul_rn(w[3], cs.w));
-            o[3] = __fadd_rn(__fmul_rn(w[1], cs.w), __fmul_rn(w[3], cs.z));
-            const bool is_v = kind == 2;
-#pragma unroll
-            for (int e = 0; e < 4; e++) o[e] = is_v ? x[e] : o[e];  // V rows are stored as read
             if (is_q && !p.q_out_f16) {
                 float *d = reinterpret_cast<float *>(p.q_out) + dst;
-                *reinterpret_cast<float2 *>(d + 2 * lane) = make_float2(o[0], o[1]);
-                *reinterpret_cast<float2 *>(d + 64 + 2 * lane) = make_float2(o[2], o[3]);
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int q = 0; q < 2; q++)
+                        *reinterpret_cast<float4 *>(d + h * 64 + c * 8 + q * 4) =
+                            make_float4(o[8 * h + 4 * q], o[8 * h + 4 * q + 1], o[8 * h + 4 * q + 2], o[8 * h + 4 * q + 3]);
             } else {
                 __half *d = (is_q ? reinterpret_cast<__half *>(p.q_out) : is_v ? p.v_cache : p.k_cache) + dst;
-                *reinterpret_cast<__half2 *>(d + 2 * lane) = h2(o[0], o[1]);
-                *reinterpret_cast<__half2 *>(d + 64 + 2 * lane) = h2(o[2], o[3]);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint4 v;
+                    uint32_t *vw = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const __half2 hh = h2(o[8 * h + 2 * e], o[8 * h + 2 * e + 1]);
+                        vw[e] = *reinterpret_cast<const uint32_t *>(&hh);
+                    }
+                    *reinterpret_cast<uint4 *>(d + h * 64 + c * 8) = v;
+                }
             }
         }
         __syncwarp();
