@@ -145,3 +145,55 @@ def test_append_groups_spanning_many_tokens(dtype):
     q, kc, vc, q_ref, kc_ref, vc_ref = _run(T, 1, 1, T, pos, cells, dtype=dtype, seed=9)
     assert np.array_equal(kc, kc_ref) and np.array_equal(vc, vc_ref)
     assert np.array_equal(q.view(np.uint32), q_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_append_rms_sum_hard_rows(dtype):
+    """Rows that stress the sequential double sum of squares: values spanning many orders of
+    magnitude (where summation order changes the rounding), denormal squares next to normal ones,
+    a single nonzero, and zeros, in f32 and bf16. Pages and Q must equal the oracle's."""
+    rng = np.random.default_rng(11)
+    T, Hq, Hkv, D = 64, 16, 8, 128
+    R = Hq + 2 * Hkv
+
+    def rows(n):
+        out = rng.standard_normal((n, D)).astype(np.float32) * 2
+        kinds = rng.integers(0, 5, n)
+        for r in range(n):
+            if kinds[r] == 1:  # magnitudes from 1e-20 to 1e3: the exact bound fails
+                out[r] *= (10.0 ** rng.uniform(-20, 3, D)).astype(np.float32)
+            elif kinds[r] == 2:  # tiny values with denormal squares next to normal ones
+                out[r, ::3] = 1e-21
+            elif kinds[r] == 3:  # one nonzero element
+                out[r] = 0
+                out[r, rng.integers(D)] = 7.5
+            elif kinds[r] == 4:  # all zeros
+                out[r] = 0
+        return out
+
+    q_in = rows(T * Hq).reshape(T, Hq, D)
+    k_in = rows(T * Hkv).reshape(T, Hkv, D)
+    v_in = rng.standard_normal((T, Hkv, D)).astype(np.float32)
+    if dtype == "bf16":
+        bits = lambda a: (torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).view(torch.int16).numpy()
+                          .view(np.uint16))
+        q_h, k_h, v_h = bits(q_in), bits(k_in), bits(v_in)
+    else:
+        q_h, k_h, v_h = q_in, k_in, v_in
+    pos = np.arange(T, dtype=np.int32) * 7
+    cells = rng.permutation(256)[:T].astype(np.int64)
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kc_ref = np.zeros((256, Hkv, D), np.uint16)
+    vc_ref = np.zeros_like(kc_ref)
+    q_ref = O.kv_append(q_h, k_h, v_h, pos, cells, kc_ref, vc_ref, g, g, 1e-6, 1e6, 1.0, in_dtype=dtype)
+    dev = "cuda"
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    kc, vc = L.alloc_cache(256, Hkv, dev), L.alloc_cache(256, Hkv, dev)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    q = L.kv_append(kc, vc, t(q_in).to(tdt), t(k_in).to(tdt), t(v_in).to(tdt), t(pos), t(cells),
+                    L.rope_table(int(pos.max()) + 1, dev), t(g), t(g), 1e-6)
+    L.check_status()
+    assert np.array_equal(kc.cpu().view(torch.int16).numpy().view(np.uint16), kc_ref)
+    assert np.array_equal(vc.cpu().view(torch.int16).numpy().view(np.uint16), vc_ref)
+    assert np.array_equal(q.cpu().numpy().view(np.uint32), q_ref.view(np.uint32))
+    assert R == 32
