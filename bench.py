@@ -212,6 +212,59 @@ def cpu_baseline_sample(w, budget_s=12.0):
                       f"{dt:.2f} s, K/V bytes only"}
 
 
+def cpu_reference_model(budget_s=6.0):
+    """The reference's own cost model for configs 1 and 2 on the host cores: ggml_flash_attn_ext
+    as a dense masked scan over n_kv cells (Engine::n_kv_for, src/engine.cpp:193-196) with the
+    KvCache::fill_mask mask (src/kv_cache.cpp:140-150), timed with the oracle's C port (ggml
+    precision model, all host threads) on seeded random f16 caches. Config 1: one decode step of
+    the 1.7B shape (512 cached tokens + 1). Config 2: query rows of the 2048-token prompt, a
+    bounded sample scaled to the whole prompt (every row scans all n_kv cells, whatever its
+    position, so the cost is linear in rows)."""
+    from localstack_b200.kv_cache import KvCache, n_kv_for
+    from oracle import oracle as O
+
+    threads = O.hardware_threads()
+    rng = np.random.default_rng(12)
+    size, hq, hkv = 4096, 16, 8
+    f16 = lambda *shape: rng.standard_normal(shape).astype(np.float16).view(np.uint16)
+    kc, vc = f16(size, hkv, D), f16(size, hkv, D)
+    out = {"threads": threads, "kind": "port", "cache_cells": size}
+    # config 1
+    kv = KvCache(size)
+    _, pos = kv.alloc(0, 513)
+    n_kv = n_kv_for(size, kv.used_hwm)
+    q = rng.standard_normal((1, hq, D)).astype(np.float32)
+    mask = kv.fill_mask(0, pos[-1:], n_kv)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s / 4:
+        O.flash_attn_ext(q, kc, vc, n_kv, mask, SCALE, mode=O.MODE_GGML, n_threads=threads)
+        reps += 1
+    out["config1_decode_us"] = round((time.perf_counter() - t0) / reps * 1e6, 1)
+    out["config1_n_kv"] = n_kv
+    # config 2
+    T = 2048
+    kv2 = KvCache(size)
+    _, pos2 = kv2.alloc(0, T)
+    n_kv2 = n_kv_for(size, kv2.used_hwm)
+    rows = 16
+    while True:
+        sel = np.linspace(0, T - 1, rows).astype(np.int32)
+        q2 = rng.standard_normal((rows, hq, D)).astype(np.float32)
+        m2 = kv2.fill_mask(0, pos2[sel], n_kv2)
+        t0 = time.perf_counter()
+        O.flash_attn_ext(q2, kc, vc, n_kv2, m2, SCALE, mode=O.MODE_GGML, n_threads=threads)
+        dt = time.perf_counter() - t0
+        if dt > budget_s / 8 or rows >= T:
+            break
+        rows = min(T, rows * 4)
+    ms = dt * T / rows * 1e3
+    out["config2_prefill_ms"] = round(ms, 2)
+    out["config2_tflops"] = round(4.0 * D * hq * T * (T + 1) / 2 / (ms / 1e3) / 1e12, 4)
+    out["config2_n_kv"] = n_kv2
+    out["sample"] = f"config 1: {reps} decode steps; config 2: {rows} of {T} query rows, scaled"
+    return out
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -393,6 +446,8 @@ def run_b200(args):
                 line["secondary"]["config4_kv_split"] = c4_split
             if c5 is not None:
                 line["secondary"]["config5_stack"] = c5
+            if world == 1 and not args.no_cpu:
+                line["secondary"]["cpu_reference_model"] = cpu_reference_model()
     barrier()
     if world > 1:
         dist.destroy_process_group()
