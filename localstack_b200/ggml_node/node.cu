@@ -804,4 +804,11 @@ int lstk_node_step(lstk_node_model *m, int32_t seq, const int32_t *tokens, int n
     return rc;
 }
 
+// KvCache::truncate_seq (keep > 0) / remove_seq (keep <= 0) on the model's cache
+// (src/kv_cache.cpp:85-132), as the server's prefix reuse does (src/server.cpp:212-219): keep
+// the common prefix, then step the rest of the new prompt.
+void lstk_node_truncate(lstk_node_model *m, int32_t seq, int32_t keep) {
+    if (m) m->kv.truncate_seq(seq, keep);
+}
+
 }  // extern "C"

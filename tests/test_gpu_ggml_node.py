@@ -128,3 +128,52 @@ def test_reference_graph_runs_on_the_backend(hq, hkv, prompt):
             assert int(np.argmax(logits)) == int(np.argmax(want)), i
     finally:
         lib.lstk_node_destroy(m)
+
+
+@pytest.mark.skipif(not os.path.exists(LIB), reason="libggml_node.so not built (needs the reference sources)")
+def test_prefix_reuse_through_the_reference_cache():
+    """The server's prefix reuse (src/server.cpp:212-219): prompt A, then the reference's own
+    KvCache::truncate_seq to the prefix A shares with prompt B, then the rest of B. The logits must
+    match a fresh model stepping all of B, and the numpy forward pass of B."""
+    _lib.lib()
+    lib = ctypes.CDLL(LIB)
+    lib.lstk_node_create.restype = ctypes.c_void_p
+    lib.lstk_node_create.argtypes = [ctypes.c_int] * 7 + [ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                                          ctypes.POINTER(ctypes.c_void_p)]
+    lib.lstk_node_step.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    lib.lstk_node_truncate.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32]
+    lib.lstk_node_destroy.argtypes = [ctypes.c_void_p]
+    lib.lstk_node_last_error.restype = ctypes.c_char_p
+    rng = np.random.default_rng(21)
+    hq, hkv, n_layer, n_embd, n_ff, n_vocab, kv_size = 8, 2, 2, 256, 512, 512, 1024
+    W, order = _weights(rng, n_layer, n_embd, n_ff, hq, hkv, n_vocab)
+    ptrs = (ctypes.c_void_p * len(order))(*[a.ctypes.data for a in order])
+    a_toks = rng.integers(0, n_vocab, 70).astype(np.int32)
+    b_toks = np.concatenate([a_toks[:37], rng.integers(0, n_vocab, 30)]).astype(np.int32)  # shares 37 tokens
+    reuse = lib.lstk_node_create(n_layer, n_embd, n_ff, hq, hkv, n_vocab, kv_size, 1e6, 1e-6, 1, ptrs)
+    fresh = lib.lstk_node_create(n_layer, n_embd, n_ff, hq, hkv, n_vocab, kv_size, 1e6, 1e-6, 1, ptrs)
+    assert reuse and fresh, lib.lstk_node_last_error().decode()
+    try:
+        logits = np.empty(n_vocab, np.float32)
+        assert lib.lstk_node_step(reuse, 3, a_toks.ctypes.data, len(a_toks), logits.ctypes.data) == 0
+        lib.lstk_node_truncate(reuse, 3, 37)
+        rest = np.ascontiguousarray(b_toks[37:])
+        got = np.empty(n_vocab, np.float32)
+        assert lib.lstk_node_step(reuse, 3, rest.ctypes.data, len(rest), got.ctypes.data) == 0, \
+            lib.lstk_node_last_error().decode()
+        want = np.empty(n_vocab, np.float32)
+        assert lib.lstk_node_step(fresh, 3, b_toks.ctypes.data, len(b_toks), want.ctypes.data) == 0
+        ref = RefModel(W, n_layer, hq, hkv, 1e6, 1e-6).step(b_toks)
+        scale = np.max(np.abs(ref))
+        assert np.max(np.abs(got - want)) <= 1e-3 * scale + 1e-4, np.max(np.abs(got - want))
+        assert np.max(np.abs(got - ref)) <= 2e-2 * scale + 2e-3
+        assert int(np.argmax(got)) == int(np.argmax(ref))
+        # then one more decode step on the reused sequence
+        nxt = np.array([int(np.argmax(got))], np.int32)
+        assert lib.lstk_node_step(reuse, 3, nxt.ctypes.data, 1, got.ctypes.data) == 0
+        assert lib.lstk_node_step(fresh, 3, nxt.ctypes.data, 1, want.ctypes.data) == 0
+        assert np.max(np.abs(got - want)) <= 1e-3 * scale + 1e-4
+    finally:
+        lib.lstk_node_destroy(reuse)
+        lib.lstk_node_destroy(fresh)
+
