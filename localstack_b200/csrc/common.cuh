@@ -143,9 +143,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t sr
                  "r"(src), "r"(c0), "r"(c1), "r"(c2)
                  : "memory");
 }
-__device__ __forceinline__ void tma_store_commit_wait() {
+// Commits the issued bulk stores and waits until they have read their shared-memory source (the
+// buffer may then be reused or released). The global writes complete asynchronously; they are
+// part of the grid's work, so stream order and griddepcontrol.wait in a dependent grid see them.
+__device__ __forceinline__ void tma_store_commit_wait_read() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {

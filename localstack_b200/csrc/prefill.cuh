@@ -598,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (warp == 0 && lane == 0 && !*abort_flag) {
                 for (int bx = 0; bx < 4; bx++)
                     tma_store_3d(&omap, sK + (uint32_t) bx * kSub, 32 * bx, kvh * G, q_begin + tok0);
-                tma_store_commit_wait();
+                tma_store_commit_wait_read();
             }
         } else {
             float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD + 64 * hf;
