@@ -103,6 +103,8 @@ def attn_decode(k_cache, v_cache, q, block_tables, seq_lens, scale=None, max_seq
         scale = 1.0 / math.sqrt(HEAD_DIM)
     if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
         raise ValueError("block_tables and seq_lens must be int32")
+    if not (q.is_contiguous() and block_tables.is_contiguous() and seq_lens.is_contiguous()):
+        raise ValueError("q, block_tables and seq_lens must be contiguous")
     if out is None:
         out = torch.empty((B, Hq, HEAD_DIM), dtype=torch.float32, device=q.device)
     if want_lse and lse_out is None:
@@ -152,8 +154,18 @@ def attn_prefill(k_cache, v_cache, q, q_seq_start, q_pos0, kv_lens, block_tables
     B = q_pos0.shape[0]
     if scale is None:
         scale = 1.0 / math.sqrt(HEAD_DIM)
+    if q.dtype not in (torch.float16, torch.float32) or not q.is_contiguous():
+        raise ValueError("q must be a contiguous f16 or f32 tensor [total_tokens][Hq][128]")
+    for name, t in (("q_seq_start", q_seq_start), ("q_pos0", q_pos0), ("kv_lens", kv_lens),
+                    ("block_tables", block_tables)):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    if q_seq_start.numel() != B + 1 or kv_lens.numel() != B or block_tables.shape[0] != B:
+        raise ValueError("q_seq_start [B+1], q_pos0 / kv_lens [B] and block_tables [B][max_blocks] must agree")
     if out is None:
         out = torch.empty((total, Hq, HEAD_DIM), dtype=torch.float32, device=q.device)
+    elif out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < total * Hq * HEAD_DIM:
+        raise ValueError("out must be a contiguous f32 tensor with total_tokens * Hq * 128 elements")
     need = lib().lstk_cuda_attn_prefill_workspace_size(B, Hq, L.n_head_kv, HEAD_DIM, int(max_q_len),
                                                        block_tables.shape[1], total, _DT[q.dtype])
     if workspace is None or workspace.numel() < need:

@@ -168,3 +168,24 @@ def test_ggml_front_end_links_the_reference_graph_builder():
     for sym in ("lstk_node_create", "lstk_node_step", "lstk_node_truncate", "lstk_node_destroy", "lstk_node_last_error",
                 "qwen3_build_graph(", "KvCache::alloc(", "KvCache::fill_mask(", "ggml_flash_attn_ext("):
         assert sym in out, sym
+
+
+def test_python_wrappers_validate_before_launch():
+    # Wrong index dtypes, shapes or strided tensors are refused in Python, before any launch.
+    import torch
+    kc = torch.zeros(64, 8, 128, dtype=torch.float16)
+    q = torch.zeros(4, 16, 128, dtype=torch.float16)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32)
+    bt = torch.zeros(1, 2, dtype=torch.int32)
+    with pytest.raises(ValueError):  # q_seq_start int64
+        L.attn_prefill(kc, kc, q, torch.tensor([0, 4]), i32(0), i32(4), bt, 4)
+    with pytest.raises(ValueError):  # q_seq_start must have B + 1 entries
+        L.attn_prefill(kc, kc, q, i32(0, 2, 4), i32(0), i32(4), bt, 4)
+    with pytest.raises(ValueError):  # strided q
+        L.attn_prefill(kc, kc, torch.zeros(4, 32, 128, dtype=torch.float16)[:, ::2], i32(0, 4), i32(0), i32(4), bt, 4)
+    with pytest.raises(ValueError):  # bf16 q is not a prefill input
+        L.attn_prefill(kc, kc, q.bfloat16(), i32(0, 4), i32(0), i32(4), bt, 4)
+    with pytest.raises(ValueError):  # int64 block tables
+        L.attn_decode(kc, kc, q[:1], bt.long(), i32(4))
+    with pytest.raises(ValueError):  # strided block tables
+        L.attn_decode(kc, kc, q[:1], torch.zeros(1, 4, dtype=torch.int32)[:, ::2], i32(4))
