@@ -1,5 +1,5 @@
-// gguf.h - the one GGUF name the reference's model headers mention (an opaque parsed file). The
-// front end builds its weights directly and never parses GGUF.
+// gguf.h - the one GGUF name the reference's model headers mention: the parsed file, defined by
+// the front end's own GGUF reader (node.cu).
 #pragma once
 
 struct gguf_context;

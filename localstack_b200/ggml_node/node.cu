@@ -32,6 +32,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <memory>
 #include <string>
 #include <unordered_map>
 #include <unordered_set>
@@ -337,12 +339,310 @@ ggml_tensor *ggml_clamp(ggml_context *ctx, ggml_tensor *a, float min, float max)
     return t;
 }
 
-// The GGUF loader's members that src/qwen3.cpp references (hyperparameter and weight lookup from a
-// file). The front end builds hyperparameters and weights directly, so these answer "absent".
-int64_t GgufModel::get_int(const std::string &, int64_t def) const { return def; }
-double GgufModel::get_float(const std::string &, double def) const { return def; }
-ggml_tensor *GgufModel::tensor(const std::string &) const { return nullptr; }
-bool GgufModel::info(const std::string &, GgufTensorInfo &) const { return false; }
+// ---------------------------------------------------------------------------------------------
+// GGUF reader: the model file format of llama.cpp (versions 2 and 3): "GGUF", version,
+// tensor count, metadata count; typed metadata key/value pairs; the tensor index (name,
+// dimensions, ggml type, offset); tensor data from the first multiple of general.alignment
+// (default 32) after the index. Written here from the published format; GgufModel's members
+// (declared by the reference's gguf_model.h) are served from it, so the reference's own
+// qwen3_load_hparams / qwen3_map_weights read real files. Tensors load as f32 (the projections
+// run on f32 GEMMs): F32, F16, BF16 and Q8_0 (blocks of 32: an f16 scale and 32 int8) convert;
+// other ggml types are refused with their type id.
+
+struct GgufValue {
+    uint32_t type = 0;
+    int64_t i = 0;
+    double f = 0.0;
+    std::string s;
+    bool is_num = false;
+};
+
+struct gguf_context {
+    uint32_t version = 0;
+    std::unordered_map<std::string, GgufValue> kv;
+    struct Tensor {
+        std::string name;
+        uint32_t type = 0;
+        int64_t ne[4] = {1, 1, 1, 1};
+        uint32_t n_dims = 0;
+        uint64_t offset = 0;
+    };
+    std::vector<Tensor> tensors;
+    std::unordered_map<std::string, size_t> by_name;
+};
+
+namespace {
+
+enum : uint32_t {  // GGUF metadata value types
+    kGgufU8 = 0, kGgufI8, kGgufU16, kGgufI16, kGgufU32, kGgufI32, kGgufF32, kGgufBool, kGgufString,
+    kGgufArray, kGgufU64, kGgufI64, kGgufF64
+};
+constexpr uint32_t kTypeF32 = 0, kTypeF16 = 1, kTypeQ8_0 = 8, kTypeBF16 = 30;  // ggml tensor types
+
+struct Reader {
+    std::FILE *f;
+    bool ok = true;
+    template <class T> T get() {
+        T v{};
+        if (ok && std::fread(&v, sizeof(T), 1, f) != 1) ok = false;
+        return v;
+    }
+    std::string str() {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || n > (1u << 20)) {
+            ok = false;
+            return {};
+        }
+        std::string s(n, '\0');
+        if (n && std::fread(&s[0], 1, n, f) != n) ok = false;
+        return s;
+    }
+    void skip(uint64_t n) {
+        if (ok && std::fseek(f, (long) n, SEEK_CUR) != 0) ok = false;
+    }
+    // One value of `type`; numbers and strings are kept, arrays skipped element by element.
+    GgufValue value(uint32_t type, int depth = 0) {
+        GgufValue v;
+        v.type = type;
+        switch (type) {
+        case kGgufU8: v.i = get<uint8_t>(); v.is_num = true; break;
+        case kGgufI8: v.i = get<int8_t>(); v.is_num = true; break;
+        case kGgufU16: v.i = get<uint16_t>(); v.is_num = true; break;
+        case kGgufI16: v.i = get<int16_t>(); v.is_num = true; break;
+        case kGgufU32: v.i = get<uint32_t>(); v.is_num = true; break;
+        case kGgufI32: v.i = get<int32_t>(); v.is_num = true; break;
+        case kGgufBool: v.i = get<uint8_t>(); v.is_num = true; break;
+        case kGgufU64: v.i = (int64_t) get<uint64_t>(); v.is_num = true; break;
+        case kGgufI64: v.i = get<int64_t>(); v.is_num = true; break;
+        case kGgufF32: v.f = get<float>(); v.i = (int64_t) v.f; v.is_num = true; break;
+        case kGgufF64: v.f = get<double>(); v.i = (int64_t) v.f; v.is_num = true; break;
+        case kGgufString: v.s = str(); break;
+        case kGgufArray: {
+            const uint32_t et = get<uint32_t>();
+            const uint64_t n = get<uint64_t>();
+            static const int fixed[] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+            if (!ok || et > kGgufF64 || depth > 2) {
+                ok = false;
+            } else if (et != kGgufString && et != kGgufArray) {
+                skip(n * (uint64_t) fixed[et]);
+            } else {
+                for (uint64_t k = 0; k < n && ok; k++) value(et, depth + 1);
+            }
+            break;
+        }
+        default: ok = false;
+        }
+        if (v.is_num && type != kGgufF32 && type != kGgufF64) v.f = (double) v.i;
+        return v;
+    }
+};
+
+// Row of n values of ggml type `type` -> f32. False for a type this loader does not convert.
+bool to_f32(uint32_t type, const uint8_t *src, int64_t n, float *dst) {
+    switch (type) {
+    case kTypeF32: std::memcpy(dst, src, (size_t) n * 4); return true;
+    case kTypeF16:
+        for (int64_t i = 0; i < n; i++) dst[i] = ggml_fp16_to_fp32(reinterpret_cast<const uint16_t *>(src)[i]);
+        return true;
+    case kTypeBF16:
+        for (int64_t i = 0; i < n; i++) {
+            const uint32_t b = (uint32_t) reinterpret_cast<const uint16_t *>(src)[i] << 16;
+            std::memcpy(&dst[i], &b, 4);
+        }
+        return true;
+    case kTypeQ8_0:
+        for (int64_t blk = 0; blk < n / 32; blk++) {
+            const uint8_t *b = src + blk * 34;
+            uint16_t dh;
+            std::memcpy(&dh, b, 2);
+            const float d = ggml_fp16_to_fp32(dh);
+            for (int j = 0; j < 32; j++) dst[blk * 32 + j] = d * (float) (int8_t) b[2 + j];
+        }
+        return true;
+    default: return false;
+    }
+}
+
+// Bytes of n values of a type this loader converts (0 for others).
+size_t type_bytes(uint32_t type, int64_t n) {
+    switch (type) {
+    case kTypeF32: return (size_t) n * 4;
+    case kTypeF16:
+    case kTypeBF16: return (size_t) n * 2;
+    case kTypeQ8_0: return (size_t) (n / 32) * 34;
+    default: return 0;
+    }
+}
+
+}  // namespace
+
+GgufModel::~GgufModel() { close(); }
+
+void GgufModel::close() {
+    delete gguf;
+    gguf = nullptr;
+    loaded.clear();
+}
+
+bool GgufModel::open(const std::string &file, std::string &err) {
+    close();
+    path = file;
+    std::FILE *f = std::fopen(file.c_str(), "rb");
+    if (!f) {
+        err = "cannot open " + file;
+        return false;
+    }
+    Reader r{f};
+    auto *g = new gguf_context();
+    const uint32_t magic = r.get<uint32_t>();
+    g->version = r.get<uint32_t>();
+    const uint64_t n_tensors = r.get<uint64_t>(), n_kv = r.get<uint64_t>();
+    if (!r.ok || magic != 0x46554747u || (g->version != 2 && g->version != 3) || n_tensors > (1u << 24) ||
+        n_kv > (1u << 20)) {
+        err = "not a GGUF v2/v3 file: " + file;
+        delete g;
+        std::fclose(f);
+        return false;
+    }
+    for (uint64_t k = 0; k < n_kv && r.ok; k++) {
+        std::string key = r.str();
+        const uint32_t type = r.get<uint32_t>();
+        GgufValue v = r.value(type);
+        if (r.ok) g->kv[key] = v;
+    }
+    for (uint64_t k = 0; k < n_tensors && r.ok; k++) {
+        gguf_context::Tensor t;
+        t.name = r.str();
+        t.n_dims = r.get<uint32_t>();
+        if (t.n_dims > 4) r.ok = false;
+        for (uint32_t d = 0; d < t.n_dims && r.ok; d++) t.ne[d] = (int64_t) r.get<uint64_t>();
+        t.type = r.get<uint32_t>();
+        t.offset = r.get<uint64_t>();
+        if (r.ok) {
+            g->by_name[t.name] = g->tensors.size();
+            g->tensors.push_back(t);
+        }
+    }
+    if (!r.ok) {
+        err = "truncated or malformed GGUF header: " + file;
+        delete g;
+        std::fclose(f);
+        return false;
+    }
+    auto al = g->kv.find("general.alignment");
+    const uint64_t align = al != g->kv.end() && al->second.is_num && al->second.i > 0 ? (uint64_t) al->second.i : 32;
+    const uint64_t pos = (uint64_t) std::ftell(f);
+    data_offset = (size_t) ((pos + align - 1) / align * align);
+    std::fclose(f);
+    gguf = g;
+    auto ar = g->kv.find("general.architecture");
+    arch = ar != g->kv.end() ? ar->second.s : "";
+    return true;
+}
+
+bool GgufModel::has(const std::string &key) const { return gguf && gguf->kv.count(key); }
+
+int64_t GgufModel::get_int(const std::string &key, int64_t def) const {
+    if (!gguf) return def;
+    auto it = gguf->kv.find(key);
+    return it != gguf->kv.end() && it->second.is_num ? it->second.i : def;
+}
+
+double GgufModel::get_float(const std::string &key, double def) const {
+    if (!gguf) return def;
+    auto it = gguf->kv.find(key);
+    return it != gguf->kv.end() && it->second.is_num ? it->second.f : def;
+}
+
+std::string GgufModel::get_str(const std::string &key, const std::string &def) const {
+    if (!gguf) return def;
+    auto it = gguf->kv.find(key);
+    return it != gguf->kv.end() && it->second.type == kGgufString ? it->second.s : def;
+}
+
+ggml_tensor *GgufModel::tensor(const std::string &name) const {
+    auto it = loaded.find(name);
+    return it != loaded.end() ? it->second : nullptr;
+}
+
+bool GgufModel::info(const std::string &name, GgufTensorInfo &out) const {
+    if (!gguf) return false;
+    auto it = gguf->by_name.find(name);
+    if (it == gguf->by_name.end()) return false;
+    const gguf_context::Tensor &t = gguf->tensors[it->second];
+    out.type = (ggml_type) t.type;
+    for (int d = 0; d < 4; d++) out.ne[d] = t.ne[d];
+    out.file_offset = data_offset + t.offset;
+    out.nbytes = type_bytes(t.type, t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3]);
+    return true;
+}
+
+// Reads every tensor (except skip(name)) as f32 into one device buffer owned by this model.
+bool GgufModel::load_all(ggml_backend_t, std::string &err, const std::function<bool(const std::string &)> &skip) {
+    if (!gguf) {
+        err = "GGUF file not open";
+        return false;
+    }
+    wctx = ggml_init({0, nullptr, true});
+    std::vector<std::pair<const gguf_context::Tensor *, ggml_tensor *>> todo;
+    for (const auto &t : gguf->tensors) {
+        if (skip && skip(t.name)) continue;
+        const int64_t n = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
+        if (type_bytes(t.type, n) == 0 || (t.type == kTypeQ8_0 && t.ne[0] % 32 != 0)) {
+            err = "tensor " + t.name + ": ggml type " + std::to_string(t.type) +
+                  " is not supported (F32, F16, BF16, Q8_0)";
+            return false;
+        }
+        if (t.ne[2] != 1 || t.ne[3] != 1) {
+            err = "tensor " + t.name + ": more than two dimensions (stacked experts) is not supported";
+            return false;
+        }
+        ggml_tensor *w = ggml_new_tensor_2d(wctx, GGML_TYPE_F32, t.ne[0], t.ne[1]);
+        ggml_set_name(w, t.name.c_str());
+        todo.emplace_back(&t, w);
+    }
+    buffer = ggml_backend_alloc_ctx_tensors(wctx, nullptr);
+    if (!buffer) {
+        err = "device allocation for the weights failed";
+        return false;
+    }
+    std::FILE *f = std::fopen(path.c_str(), "rb");
+    if (!f) {
+        err = "cannot reopen " + path;
+        return false;
+    }
+    std::vector<uint8_t> raw;
+    std::vector<float> conv;
+    for (auto &[t, w] : todo) {
+        const int64_t n = t->ne[0] * t->ne[1];
+        raw.resize(type_bytes(t->type, n));
+        conv.resize((size_t) n);
+        if (std::fseek(f, (long) (data_offset + t->offset), SEEK_SET) != 0 ||
+            std::fread(raw.data(), 1, raw.size(), f) != raw.size()) {
+            err = "tensor " + t->name + ": data past the end of the file";
+            std::fclose(f);
+            return false;
+        }
+        to_f32(t->type, raw.data(), n, conv.data());
+        cudaMemcpy(w->data, conv.data(), conv.size() * 4, cudaMemcpyHostToDevice);
+        loaded[t->name] = w;
+    }
+    std::fclose(f);
+    return true;
+}
+
+size_t GgufModel::total_bytes() const {
+    size_t s = 0;
+    if (gguf)
+        for (const auto &t : gguf->tensors) s += type_bytes(t.type, t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3]);
+    return s;
+}
+
+size_t GgufModel::loaded_bytes() const {
+    size_t s = 0;
+    for (const auto &kv : loaded) s += nbytes(kv.second);
+    return s;
+}
 
 // ---------------------------------------------------------------------------------------------
 // Device kernels for the ops around the attention node (f32).
@@ -510,6 +810,7 @@ struct lstk_node_model {
     Qwen3HParams hp;
     Qwen3Weights w;
     KvCache kv;
+    std::unique_ptr<GgufModel> file;  // weights loaded from a GGUF file (lstk_node_create_gguf)
     ggml_context *wctx = nullptr;
     ggml_backend_buffer_t wbuf = nullptr;
     cublasHandle_t blas = nullptr;
@@ -762,7 +1063,45 @@ void lstk_node_destroy(lstk_node_model *m) {
     cudaFree(m->rope);
     ggml_backend_buffer_free(m->wbuf);
     ggml_free(m->wctx);
+    if (m->file) {
+        ggml_backend_buffer_free(m->file->buffer);
+        ggml_free(m->file->wctx);
+    }
     delete m;
+}
+
+// A dense Qwen3 / Qwen2 model from a GGUF file: the reference's own qwen3_load_hparams and
+// qwen3_map_weights (src/qwen3.cpp:16-90) read it through GgufModel; head_dim 128, no experts.
+lstk_node_model *lstk_node_create_gguf(const char *path, int kv_size) {
+    std::unique_ptr<lstk_node_model> m(new lstk_node_model());
+    m->file.reset(new GgufModel());
+    std::string err;
+    if (!m->file->open(path ? path : "", err) || !m->file->load_all(nullptr, err) ||
+        !qwen3_load_hparams(*m->file, m->hp, err)) {
+        g_err = err;
+        return nullptr;
+    }
+    if (m->hp.moe() || m->hp.head_dim != 128) {
+        g_err = "the front end runs dense models with head_dim 128";
+        return nullptr;
+    }
+    if (!qwen3_map_weights(*m->file, m->hp, m->w, false, err)) {
+        g_err = err;
+        return nullptr;
+    }
+    if (cublasCreate(&m->blas) != CUBLAS_STATUS_SUCCESS ||
+        !m->kv.init(nullptr, m->hp.n_layer, m->hp.n_head_kv * 128, m->hp.n_head_kv * 128, kv_size, GGML_TYPE_F16,
+                    err)) {
+        g_err = "model set-up failed " + err;
+        return nullptr;
+    }
+    cublasSetMathMode(m->blas, CUBLAS_PEDANTIC_MATH);
+    m->rope_n_pos = kv_size;
+    std::vector<float> rope(lstk_rope_table_bytes(kv_size, 128) / sizeof(float));
+    lstk_rope_table_fill(rope.data(), kv_size, 128, m->hp.rope_freq_base, 1.0f);
+    cudaMalloc(&m->rope, rope.size() * sizeof(float));
+    cudaMemcpy(m->rope, rope.data(), rope.size() * sizeof(float), cudaMemcpyHostToDevice);
+    return m.release();
 }
 
 // One engine step for sequence `seq`: its next n_tokens tokens. Follows Engine::make_step_inputs

@@ -165,7 +165,8 @@ def test_ggml_front_end_links_the_reference_graph_builder():
     if not os.path.exists(lib):
         pytest.skip("front end not built (reference sources absent)")
     out = subprocess.run(["nm", "-D", "--defined-only", "-C", lib], capture_output=True, text=True, check=True).stdout
-    for sym in ("lstk_node_create", "lstk_node_step", "lstk_node_truncate", "lstk_node_destroy", "lstk_node_last_error",
+    for sym in ("lstk_node_create", "lstk_node_create_gguf", "lstk_node_step", "lstk_node_truncate",
+                "lstk_node_destroy", "lstk_node_last_error",
                 "qwen3_build_graph(", "KvCache::alloc(", "KvCache::fill_mask(", "ggml_flash_attn_ext("):
         assert sym in out, sym
 

@@ -177,3 +177,80 @@ def test_prefix_reuse_through_the_reference_cache():
         lib.lstk_node_destroy(reuse)
         lib.lstk_node_destroy(fresh)
 
+
+
+def _gguf_model(tmp_path, rng, hq, hkv, n_layer, n_embd, n_ff, n_vocab, drop=None):
+    """A dense Qwen3 written as a GGUF file with mixed tensor types; returns (path, the f32 weights
+    the file holds, for the numpy model)."""
+    import gguf_file as G
+    W, _ = _weights(rng, n_layer, n_embd, n_ff, hq, hkv, n_vocab)
+    meta = {"general.architecture": "qwen3", "general.alignment": 32, "qwen3.block_count": n_layer,
+            "qwen3.embedding_length": n_embd, "qwen3.feed_forward_length": n_ff,
+            "qwen3.attention.head_count": hq, "qwen3.attention.head_count_kv": hkv,
+            "qwen3.attention.key_length": D, "qwen3.context_length": 4096,
+            "qwen3.attention.layer_norm_rms_epsilon": 1e-6, "qwen3.rope.freq_base": 1e6}
+    tensors, Wq = [], {"layers": []}
+
+    def add(name, a, ty):
+        raw, vals = G.encode(a, ty)
+        if name != drop:
+            tensors.append((name, list(a.shape[::-1]), ty, raw))
+        return vals
+
+    Wq["tok_embd"] = add("token_embd.weight", W["tok_embd"], G.F32)
+    Wq["output_norm"] = add("output_norm.weight", W["output_norm"], G.F32)
+    Wq["output"] = add("output.weight", W["output"], G.F16)
+    types = {"wq": G.Q8_0, "wk": G.F16, "wv": G.BF16, "wo": G.Q8_0, "ffn_gate": G.F16, "ffn_up": G.BF16,
+             "ffn_down": G.Q8_0}
+    names = {"attn_norm": "attn_norm", "wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output",
+             "q_norm": "attn_q_norm", "k_norm": "attn_k_norm", "ffn_norm": "ffn_norm", "ffn_gate": "ffn_gate",
+             "ffn_up": "ffn_up", "ffn_down": "ffn_down"}
+    for l, P in enumerate(W["layers"]):
+        Wq["layers"].append({k: add(f"blk.{l}.{names[k]}.weight", P[k], types.get(k, G.F32)) for k in names})
+    path = str(tmp_path / "model.gguf")
+    G.write(path, meta, tensors)
+    return path, Wq
+
+
+def _node_lib():
+    _lib.lib()
+    lib = ctypes.CDLL(LIB)
+    lib.lstk_node_create_gguf.restype = ctypes.c_void_p
+    lib.lstk_node_create_gguf.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    lib.lstk_node_step.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    lib.lstk_node_destroy.argtypes = [ctypes.c_void_p]
+    lib.lstk_node_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+@pytest.mark.skipif(not os.path.exists(LIB), reason="libggml_node.so not built (needs the reference sources)")
+def test_gguf_model_file(tmp_path):
+    """A GGUF file (F32 / F16 / BF16 / Q8_0 tensors) read by the front end's GGUF reader through
+    the reference's own qwen3_load_hparams / qwen3_map_weights, then a prompt and decode steps:
+    logits match the numpy model on the weights as the file stores them."""
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    rng = np.random.default_rng(31)
+    hq, hkv, n_layer, n_embd, n_ff, n_vocab = 8, 2, 2, 256, 512, 512
+    path, Wq = _gguf_model(tmp_path, rng, hq, hkv, n_layer, n_embd, n_ff, n_vocab)
+    lib = _node_lib()
+    m = lib.lstk_node_create_gguf(path.encode(), 1024)
+    assert m, lib.lstk_node_last_error().decode()
+    ref = RefModel(Wq, n_layer, hq, hkv, 1e6, 1e-6)
+    try:
+        for i, toks in enumerate([rng.integers(0, n_vocab, 50)] + [rng.integers(0, n_vocab, 1) for _ in range(2)]):
+            toks = np.ascontiguousarray(toks, np.int32)
+            logits = np.empty(n_vocab, np.float32)
+            assert lib.lstk_node_step(m, 0, toks.ctypes.data, len(toks), logits.ctypes.data) == 0, \
+                lib.lstk_node_last_error().decode()
+            want = ref.step(toks)
+            assert np.max(np.abs(logits - want)) <= 2e-2 * np.max(np.abs(want)) + 2e-3, i
+            assert int(np.argmax(logits)) == int(np.argmax(want)), i
+    finally:
+        lib.lstk_node_destroy(m)
+    # a file missing a required tensor: the reference's own error
+    (tmp_path / "missing").mkdir()
+    path2, _ = _gguf_model(tmp_path / "missing", np.random.default_rng(32), hq, hkv, n_layer, n_embd, n_ff,
+                           n_vocab, drop="blk.1.ffn_down.weight")
+    assert not lib.lstk_node_create_gguf(path2.encode(), 1024)
+    assert "missing tensor blk.1.ffn_down.weight" in lib.lstk_node_last_error().decode()
