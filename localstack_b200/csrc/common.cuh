@@ -33,6 +33,7 @@ enum : int {
     kSiteDecodeWaitEmpty = 13,
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
+    kSitePrefillSmem = 22,
     kSiteExchangeWait = 30,
     kSitePagesSlot = 40,
     kSitePagesTokens = 41,
@@ -143,11 +144,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t sr
                  "r"(src), "r"(c0), "r"(c1), "r"(c2)
                  : "memory");
 }
-// Commits the issued bulk stores and waits until they have read their shared-memory source (the
-// buffer may then be reused or released). The global writes complete asynchronously; they are
-// part of the grid's work, so stream order and griddepcontrol.wait in a dependent grid see them.
-__device__ __forceinline__ void tma_store_commit_wait_read() {
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+// Bulk stores: commit the issued ones as a group; wait until every committed group has read its
+// shared-memory source (the buffer may then be reused or released). The global writes complete
+// asynchronously; they are part of the grid's work, so stream order and griddepcontrol.wait in a
+// dependent grid see them.
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 

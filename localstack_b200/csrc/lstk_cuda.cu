@@ -492,8 +492,11 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
     p.status = dev->status;
-    const int64_t grid = (int64_t) n_seqs * p.n_qt * hkv;
-    if (grid > (int64_t) INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: grid too large");
+    const int64_t n_items = (int64_t) n_seqs * p.n_qt * hkv;
+    if (n_items > (int64_t) INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: too many tiles");
+    p.n_items = (int) n_items;
+    // Persistent: one CTA per SM walks its share of the items (snake order over heaviest-first).
+    const int64_t grid = std::min<int64_t>(n_items, dev->n_sms);
     if (!dev->prefill_attr) {
         const cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    prefill::kSmemBytes);

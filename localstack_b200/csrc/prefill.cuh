@@ -10,12 +10,18 @@
 // (64, G, 128/G) loads exactly that row order. K/V tiles are 128 keys = 4 pages, each page
 // fetched by TMA through the block table (box (64, 1, 32), 128-byte swizzle).
 //
-// Pipeline (one CTA per SM: 163 KiB of shared memory, 512 TMEM columns):
-//   warps 8, 10  TMA producers: Q once and K_j (warp 8), V_j (warp 10), each into a double
-//           buffer; the block table is read a warp at a time, one chunk of 32 pages ahead.
+// Persistent: one CTA per SM (226 KiB of shared memory, 512 TMEM columns) walks its share of the
+// items, rounds of gridDim.x items in snake order over the heaviest-first numbering, so that per-CTA
+// set-up is paid once and the next item's loads and first scores overlap the current item's
+// epilogue. Pipeline:
+//   warps 8, 10  TMA producers: Q (per item, once the item's last QK has read the previous one)
+//           and K_j (warp 8), V_j (warp 10), each into a double buffer, running ahead into the next
+//           item; the block table is read a warp at a time, one chunk of 32 pages ahead.
 //   warp 9  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
 //           waiting for softmax j, so the tensor core computes the next scores while the
-//           softmax warps work; then O += P_j V_j with P_j read from tensor memory (TS form).
+//           softmax warps work; then O += P_j V_j with P_j read from tensor memory (TS form). The
+//           next item's first scores follow this item's last PV; its first PV waits until the
+//           epilogue has read O out.
 //   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and key half w/4 of every
 //           tile (its 64 score columns), so two warps on each SM sub-partition share the tile's
 //           exp work. Each key half keeps its own running max, row sum and O accumulator (O_0,
@@ -25,15 +31,18 @@
 //           The running max only moves (and O_h is rescaled in TMEM) when a tile's max exceeds
 //           it by more than 2^8, so the softmax rarely waits for the previous PV. Epilogue: the
 //           halves swap (m, l) per row through shared memory and merge O = (O_0 2^(m_0-M) +
-//           O_1 2^(m_1-M)) / (l_0 2^(m_0-M) + l_1 2^(m_1-M)); a full tile is staged in the (then
-//           free) K buffers and leaves through TMA stores.
+//           O_1 2^(m_1-M)) / (l_0 2^(m_0-M) + l_1 2^(m_1-M)); a full tile is staged in its own
+//           buffer and leaves through TMA stores that complete while the next item runs (their source reads are awaited before the buffer
+//           is written again). All softmax warps run every item's named barriers and agree on
+//           failure with a barrier reduction, so they stop at the same item.
 // The kernel is launched with programmatic stream serialization: barrier and TMEM set-up overlap
 // the previous kernel, and griddepcontrol.wait precedes every read of earlier work.
 // TMEM: S0 cols [0,128), S1 [128,256), O_0 [256,384), O_1 [384,512) (f32, 128 lanes = 128 rows).
 // P_j occupies S_j's columns [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2}
 // overwrites them only after PV_j, which the tensor core executes first.
 // Every mbarrier wait is on a parity at most one phase from the arrivals: per-buffer barriers
-// (K, V, S, P), and the o_done phases are waited in order.
+// (K, V, S, P) indexed by a running tile count across items, the o_done phases waited in order,
+// and one q_full / q_empty / o_free phase per item.
 // Measured limit: per 128-key tile the tensor core runs 8 SS MMAs (S) and 8 TS MMAs (PV) of
 // 128x128x16; alternating the two forms costs well above the nominal 64 cycles per MMA, and
 // the issuing thread stays blocked on the MMA queue, so the softmax (about half the tile time)
@@ -65,15 +74,16 @@ constexpr int kThreads = 352;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 384;
 
-// Shared memory carve-up (offsets from a 1024-aligned base).
+// Shared memory carve-up (offsets from the 1024-aligned dynamic shared memory base).
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;       // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
-constexpr int kOffBar = kOffV + 2 * kTile;
-constexpr int kSmemBytes = kOffBar + 2304 + 1024;  // + barriers and row statistics + alignment slack
+constexpr int kOffO = kOffV + 2 * kTile;   // output staging: 128 rows x 128 f32 (64 KiB)
+constexpr int kOffBar = kOffO + 2 * kTile;
+constexpr int kSmemBytes = kOffBar + 2304;  // + barriers and row statistics
 
 struct Params {
-    int n_seqs, n_head, n_head_kv, group, n_qt;
+    int n_seqs, n_head, n_head_kv, group, n_qt, n_items;
     const int32_t *q_seq_start;
     const int32_t *q_pos0;
     const int32_t *kv_lens;
@@ -88,6 +98,8 @@ struct Params {
 
 struct Barriers {
     uint64_t q_full;
+    uint64_t q_empty;  // the item's last S MMA has read Q: the next item's Q may load
+    uint64_t o_free;   // the softmax warps have read O out: the next item's first PV may write it
     uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
     uint64_t s_full[2];
     // P_j of key half h: one arrival per softmax warp of that half, on p_full[h][j % 2]. A barrier
@@ -246,6 +258,57 @@ constexpr float kRescaleThreshold = 8.f;
 
 extern __shared__ __align__(1024) uint8_t dyn_smem[];
 
+// One work item: (sequence b, query tile, KV head kvh). Items are numbered heaviest first (latest
+// query positions first); an item past its sequence's end has no keys and no live rows.
+struct Item {
+    int b, kvh, tok0, q_begin, n_q, kv_len, pos0, n_keys, n_tiles;
+};
+
+// An item's sequence metadata as loaded; item_finish derives the rest, so a loop can issue the
+// next item's loads early and use them one item later.
+struct ItemRaw {
+    int b, kvh, tok0, q0, q1, kv_len_raw, pos0;
+};
+
+__device__ __forceinline__ ItemRaw item_load(const Params &p, int x) {
+    ItemRaw r;
+    r.kvh = x % p.n_head_kv;
+    const int rest = x / p.n_head_kv;
+    r.b = rest % p.n_seqs;
+    r.tok0 = (p.n_qt - 1 - rest / p.n_seqs) * (kBM / p.group);
+    r.q0 = p.q_seq_start[r.b];
+    r.q1 = p.q_seq_start[r.b + 1];
+    r.kv_len_raw = p.kv_lens[r.b];
+    r.pos0 = p.q_pos0[r.b];
+    return r;
+}
+
+__device__ __forceinline__ Item item_finish(const Params &p, const ItemRaw &r) {
+    Item it;
+    it.b = r.b;
+    it.kvh = r.kvh;
+    it.tok0 = r.tok0;
+    it.q_begin = r.q0;
+    it.n_q = r.q1 - r.q0;
+    it.kv_len = max(0, min(r.kv_len_raw, p.max_blocks * kPage));
+    it.pos0 = r.pos0;
+    const int last_tok = min(it.tok0 + kBM / p.group, it.n_q) - 1;
+    it.n_keys = it.tok0 < it.n_q ? max(0, min(it.kv_len, it.pos0 + last_tok + 1)) : 0;
+    it.n_tiles = (it.n_keys + kBN - 1) / kBN;
+    return it;
+}
+
+__device__ __forceinline__ Item item_at(const Params &p, int x) { return item_finish(p, item_load(p, x)); }
+
+// The r-th item of this CTA (-1 past the end): rounds of gridDim.x items in "snake" order, forward
+// in even rounds and backward in odd ones, so the CTA that took one of the lightest items of a
+// round takes the heaviest of the next.
+__device__ __forceinline__ int item_index(const Params &p, int r) {
+    const int64_t g = gridDim.x;
+    const int64_t idx = (int64_t) r * g + ((r & 1) ? g - 1 - (int64_t) blockIdx.x : (int64_t) blockIdx.x);
+    return idx < p.n_items ? (int) idx : -1;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
@@ -254,16 +317,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
 
-    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t *base = dyn_smem;
+    if ((smem_u32(base) & 1023u) != 0) {  // the 128-byte swizzle needs 1024-byte aligned tiles
+        if (threadIdx.x == 0) report(p.status, kStatusBadIndex, kSitePrefillSmem, (int) (smem_u32(base) & 1023u));
+        return;
+    }
     Barriers *bars = reinterpret_cast<Barriers *>(base + kOffBar);
     const uint32_t sQ = smem_u32(base + kOffQ);
     const uint32_t sK = smem_u32(base + kOffK);
     const uint32_t sV = smem_u32(base + kOffV);
+    const uint32_t sO = smem_u32(base + kOffO);
     volatile int *abort_flag = &bars->abort;
 
     if (threadIdx.x == 0) {
         bars->abort = 0;
         mbar_init(smem_u32(&bars->q_full), 1);
+        mbar_init(smem_u32(&bars->q_empty), 1);
+        mbar_init(smem_u32(&bars->o_free), kSoftmaxWarps);
         for (int i = 0; i < 2; i++) {
             mbar_init(smem_u32(&bars->k_full[i]), 1);
             mbar_init(smem_u32(&bars->v_full[i]), 1);
@@ -289,42 +359,50 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     // launch); everything below reads what earlier work produced.
     pdl_wait();
     pdl_launch_dependents();
-
-    // Heaviest tiles (latest query positions) are launched first. A tile past its sequence's
-    // end (ragged batches) does nothing: no keys and no live rows.
-    const int x = blockIdx.x;
-    const int kvh = x % p.n_head_kv;
-    const int rest = x / p.n_head_kv;
-    const int b = rest % p.n_seqs;
-    const int qt = p.n_qt - 1 - rest / p.n_seqs;
     const int G = p.group;
-    const int tpt = kBM / G;  // tokens per query tile
-    const int q_begin = p.q_seq_start[b];
-    const int n_q = p.q_seq_start[b + 1] - q_begin;
-    const int tok0 = qt * tpt;
-    const int kv_len = max(0, min(p.kv_lens[b], p.max_blocks * kPage));
-    const int pos0 = p.q_pos0[b];
-    const int last_tok = min(tok0 + tpt, n_q) - 1;
-    const int n_keys = tok0 < n_q ? max(0, min(kv_len, pos0 + last_tok + 1)) : 0;
-    const int n_tiles = (n_keys + kBN - 1) / kBN;
 
+    // Every role walks the same item sequence. Barrier phases come from running counters: g, the
+    // global index of a K/V tile in this CTA (buffer g % 2, parity (g / 2) % 2 for the per-buffer
+    // barriers; parity g % 2 for o_done, one completion per PV), and the count of items that have
+    // tiles (q_full, q_empty, o_free: one completion per item).
     if (warp == kWarpTmaK || warp == kWarpTmaV) {
         // ---- TMA producers: warp 8 streams Q and the K tiles, warp 10 the V tiles, each into
-        // its own double buffer, so a K tile never waits behind the PV that frees a V buffer.
+        // its own double buffer, running ahead into the next item while the current one ends.
         // The block table is read a warp at a time (lane i: page 32c + i, one chunk ahead) and
         // lane 0 issues the copies. ----
         const bool is_k = warp == kWarpTmaK;
-        if (n_tiles > 0) {
-            if (lane == 0) {
-                if (is_k) {
-                    prefetch_tensormap(&qmap);
-                    prefetch_tensormap(&kmap);
-                } else {
-                    prefetch_tensormap(&vmap);
+        if (lane == 0) {
+            if (is_k) {
+                prefetch_tensormap(&qmap);
+                prefetch_tensormap(&kmap);
+            } else {
+                prefetch_tensormap(&vmap);
+            }
+        }
+        const uint32_t dst0 = is_k ? sK : sV;
+        const CUtensorMap *map = is_k ? &kmap : &vmap;
+        int g = 0, n_items_t = 0;
+        bool ok = true;
+        for (int r = 0; ok; r++) {
+            const int x = item_index(p, r);
+            if (x < 0) break;
+            const Item I = item_at(p, x);
+            if (I.n_tiles == 0) continue;
+            if (is_k && lane == 0) {
+                if (n_items_t > 0)
+                    ok = mbar_wait_bounded(smem_u32(&bars->q_empty), (uint32_t) (n_items_t - 1) & 1, abort_flag);
+                if (ok) {
+                    mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
+                    for (int h = 0; h < 2; h++)
+                        tma_load_3d(sQ + h * kSub, &qmap, smem_u32(&bars->q_full), h * 64, I.kvh * G,
+                                    I.q_begin + I.tok0);
                 }
             }
-            const int32_t *bt = p.block_tables + (int64_t) b * p.max_blocks;
-            const int n_pg = (n_keys + kPage - 1) / kPage;  // pages holding visible keys
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            n_items_t++;
+            const int32_t *bt = p.block_tables + (int64_t) I.b * p.max_blocks;
+            const int n_pg = (I.n_keys + kPage - 1) / kPage;  // pages holding visible keys
             auto load_chunk = [&](int chunk) -> int {
                 const int pi = chunk * 32 + lane;
                 int cell = (int) p.n_cells;  // out of bounds: TMA fills zeros
@@ -337,16 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             };
             int cur = load_chunk(0);
             int nxt = n_pg > 32 ? load_chunk(1) : (int) p.n_cells;
-            if (is_k && lane == 0) {
-                mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
-                for (int h = 0; h < 2; h++)
-                    tma_load_3d(sQ + h * kSub, &qmap, smem_u32(&bars->q_full), h * 64, kvh * G, q_begin + tok0);
-            }
-            const uint32_t dst0 = is_k ? sK : sV;
-            const CUtensorMap *map = is_k ? &kmap : &vmap;
-            int n_issued = 0;
-            bool ok = true;
-            for (int j = 0; j < n_tiles; j++) {
+            for (int j = 0; j < I.n_tiles; j++) {
                 if (j > 0 && (j & 7) == 0) {  // next 32 pages: 8 tiles
                     cur = nxt;
                     nxt = (j / 8 + 1) * 32 < n_pg ? load_chunk(j / 8 + 1) : (int) p.n_cells;
@@ -355,8 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                 for (int q = 0; q < 4; q++) cell0[q] = __shfl_sync(0xffffffffu, cur, (j & 7) * 4 + q);
                 if (lane == 0) {
-                    const int buf = j & 1;
-                    const uint32_t use = (uint32_t) (j >> 1);
+                    const int buf = g & 1;
+                    const uint32_t use = (uint32_t) (g >> 1);
                     const uint32_t empty = smem_u32(is_k ? &bars->k_empty[buf] : &bars->v_empty[buf]);
                     const uint32_t full = smem_u32(is_k ? &bars->k_full[buf] : &bars->v_full[buf]);
                     if (use > 0) ok = mbar_wait_bounded(empty, (use - 1) & 1, abort_flag);
@@ -364,37 +433,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         mbar_arrive_expect_tx(full, kTile);
                         for (int q = 0; q < 4; q++)
                             for (int h = 0; h < 2; h++)
-                                tma_load_3d(dst0 + buf * kTile + h * kSub + q * (kPage * 128), map, full, h * 64, kvh,
-                                            cell0[q]);
+                                tma_load_3d(dst0 + buf * kTile + h * kSub + q * (kPage * 128), map, full, h * 64,
+                                            I.kvh, cell0[q]);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
-                n_issued++;
+                g++;
             }
-            if (lane == 0) {
-                if (!ok) {
-                    report(p.status, kStatusTimeout, kSitePrefillWait, warp);
-                    *abort_flag = 1;
-                }
-                if (*abort_flag) {
-                    // Drain: every load still in flight lands before shared memory is released.
-                    if (is_k) mbar_wait_bounded(smem_u32(&bars->q_full), 0, nullptr);
-                    for (int j = max(0, n_issued - 2); j < n_issued; j++)
-                        mbar_wait_bounded(smem_u32(is_k ? &bars->k_full[j & 1] : &bars->v_full[j & 1]),
-                                          (uint32_t) (j >> 1) & 1, nullptr);
-                }
+        }
+        if (lane == 0) {
+            if (!ok) {
+                report(p.status, kStatusTimeout, kSitePrefillWait, warp);
+                *abort_flag = 1;
+            }
+            if (*abort_flag) {
+                // Drain: every load still in flight lands before shared memory is released.
+                if (is_k && n_items_t > 0)
+                    mbar_wait_bounded(smem_u32(&bars->q_full), (uint32_t) (n_items_t - 1) & 1, nullptr);
+                for (int gg = max(0, g - 2); gg < g; gg++)
+                    mbar_wait_bounded(smem_u32(is_k ? &bars->k_full[gg & 1] : &bars->v_full[gg & 1]),
+                                      (uint32_t) (gg >> 1) & 1, nullptr);
             }
         }
     } else if (warp == kWarpMma) {
         // ---- MMA issuer ----
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16(false);
             constexpr uint32_t idesc_pv = idesc_f16(true);
-            bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag);
-            auto issue_qk = [&](int j) -> bool {
-                const int buf = j & 1;
-                if (!mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag))
+            int g = 0, n_items_t = 0;
+            bool ok = true;
+            // S_gg = Q K_gg^T into S buffer gg % 2; after the item's last S, Q may be reloaded.
+            auto issue_qk = [&](int gg, bool last) -> bool {
+                const int buf = gg & 1;
+                if (!mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag))
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem + (buf ? kColS1 : kColS0);
@@ -406,41 +478,64 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
                 mma_commit(smem_u32(&bars->s_full[buf]));
                 mma_commit(smem_u32(&bars->k_empty[buf]));
+                if (last) mma_commit(smem_u32(&bars->q_empty));
                 return true;
             };
-            if (ok) ok = issue_qk(0);
-            for (int j = 0; ok && j < n_tiles; j++) {
-                if (j + 1 < n_tiles && !issue_qk(j + 1)) {
-                    ok = false;
-                    break;
-                }
-                const int buf = j & 1;
-                if (!mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                // P_j sits in TMEM over S_j: keys 0..63 in columns [0, 32), keys 64..127 in
-                // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
-                // Key half h accumulates into its own O_h, as soon as its four warps are done.
-                const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
-                for (int h = 0; h < 2 && ok; h++) {
-                    if (!mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (j >> 1) & 1, abort_flag)) {
+            for (int r = 0; ok; r++) {
+                const int x = item_index(p, r);
+                if (x < 0) break;
+                const int n = item_at(p, x).n_tiles;
+                if (n == 0) continue;
+                // Order: S_0, S_1, then per tile j: PV_j (once its halves have written P_j) and
+                // S_{j+2} into the buffer PV_j has just read (the tensor core runs one thread's
+                // MMAs in order). The next item's S_0 / S_1 follow this item's last PV, so they run
+                // during this item's epilogue.
+                ok = mbar_wait_bounded(smem_u32(&bars->q_full), (uint32_t) n_items_t & 1, abort_flag);
+                if (ok) ok = issue_qk(g, n == 1);
+                if (ok && n > 1) ok = issue_qk(g + 1, n == 2);
+                for (int j = 0; ok && j < n; j++) {
+                    const int gg = g + j;
+                    const int buf = gg & 1;
+                    if (!mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
+                    // The item's first PV overwrites O: the previous item's epilogue must have read it.
+                    if (j == 0 && n_items_t > 0 &&
+                        !mbar_wait_bounded(smem_u32(&bars->o_free), (uint32_t) (n_items_t - 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    // P_gg sits in TMEM over S_gg: keys 0..63 in columns [0, 32), keys 64..127 in
+                    // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
+                    // Key half h accumulates into its own O_h, as soon as its four warps are done.
+                    const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
+                    for (int h = 0; h < 2 && ok; h++) {
+                        if (!mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (gg >> 1) & 1,
+                                               abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
 #pragma unroll
-                    for (int kq = 0; kq < 4; kq++) {
-                        const int kk = 4 * h + kq;
-                        const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
-                        mma_f16_ts(tmem + (h ? kColO1 : kColO0), pcol + (uint32_t) (h * 64 + kq * 8),
-                                   sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
-                                   (j > 0 || kq > 0) ? 1u : 0u);
+                        for (int kq = 0; kq < 4; kq++) {
+                            const int kk = 4 * h + kq;
+                            const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
+                            mma_f16_ts(tmem + (h ? kColO1 : kColO0), pcol + (uint32_t) (h * 64 + kq * 8),
+                                       sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
+                                       (j > 0 || kq > 0) ? 1u : 0u);
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(smem_u32(&bars->o_done));
+                    mma_commit(smem_u32(&bars->v_empty[buf]));
+                    if (j + 2 < n && !issue_qk(gg + 2, j + 2 == n - 1)) {
+                        ok = false;
+                        break;
                     }
                 }
-                if (!ok) break;
-                mma_commit(smem_u32(&bars->o_done));
-                mma_commit(smem_u32(&bars->v_empty[buf]));
+                g += n;
+                n_items_t++;
             }
             if (!ok) {
                 report(p.status, kStatusTimeout, kSitePrefillWait, kWarpMma);
@@ -458,166 +553,195 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const int r = quad * 32 + lane;  // row within the tile
         const uint32_t lane_base = tmem + ((uint32_t) (quad * 32) << 16);
         const uint32_t ocol = lane_base + (hf ? kColO1 : kColO0);
-        const int tq = tok0 + r / G;  // query token index within the sequence
-        const int head = kvh * G + r % G;
-        const int row_keys = min(kv_len, pos0 + tq + 1);  // keys [0, row_keys) are visible
         const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
-        float m = -INFINITY, l = 0.f;  // this key half's running max (log2 domain) and sum
-        bool ok = true;
-        for (int j = 0; j < n_tiles; j++) {
-            const int buf = j & 1;
-            // Warp-uniform outcomes: tcgen05.ld / st below are warp-collective.
-            if (!__all_sync(0xffffffffu,
-                            mbar_wait_bounded(smem_u32(&bars->s_full[buf]), (uint32_t) (j >> 1) & 1, abort_flag))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float sc[64];
-            tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, sc);
-            tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf + 32, sc + 32);
-            tmem_wait_ld();
-            const int kbase = j * kBN + 64 * hf;  // key index of this warp's first column
-            if (kbase + 64 > row_keys) {
-#pragma unroll
-                for (int c = 0; c < 64; c++) sc[c] = (kbase + c < row_keys) ? sc[c] : -INFINITY;
-            }
-            // Row max of the raw scores (the scale is positive): 8 independent max3 chains.
-            float mx[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) mx[i] = fmaxf(sc[i], sc[8 + i]);
-#pragma unroll
-            for (int c = 16; c < 64; c += 16)
-#pragma unroll
-                for (int i = 0; i < 8; i++) mx[i] = max3(mx[i], sc[c + i], sc[c + 8 + i]);
-            const float m_tile =
-                fmaxf(max3(mx[0], mx[1], mx[2]), fmaxf(max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
-                p.scale_log2;
-            const bool move = m_tile > m + kRescaleThreshold;  // always true for the first visible tile
-            const float m_new = move ? m_tile : m;
-            const float alpha = move ? fast_exp2(m - m_new) : 1.f;
-            const float mu = m_new == -INFINITY ? 0.f : m_new;
-            const uint64_t neg_mu2 = pack_f32x2(-mu, -mu);
-            float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial row sums
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < 32; c++)
-                pk[c] = softmax_pair(sc[2 * c], sc[2 * c + 1], scale2, neg_mu2, rsum[2 * (c & 3)], rsum[2 * (c & 3) + 1]);
-            // A moved max rescales O_hf, which PV_{j-1} must have finished updating (PV_{j-2} has:
-            // S_j ready implies it). P_j goes to buffer j%2, last read by PV_{j-2}: no wait.
-            if (j > 0 && __any_sync(0xffffffffu, move)) {
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) (j - 1) & 1, abort_flag))) {
+        bool store_pending = false;  // warp 0 lane 0: a TMA store still reading the staging buffer
+        int g = 0, n_items_t = 0;
+        int x = item_index(p, 0);
+        ItemRaw raw_next = x >= 0 ? item_load(p, x) : ItemRaw{};
+        for (int it = 0; x >= 0; it++) {
+            const Item I = item_finish(p, raw_next);
+            // The next item's metadata loads are issued now and used one item later.
+            const int x_next = item_index(p, it + 1);
+            if (x_next >= 0) raw_next = item_load(p, x_next);
+            x = x_next;
+            const int n_tiles = I.n_tiles;
+            const int tq = I.tok0 + r / G;  // query token index within the sequence
+            const int head = I.kvh * G + r % G;
+            const int row_keys = min(I.kv_len, I.pos0 + tq + 1);  // keys [0, row_keys) are visible
+            const bool live = tq < I.n_q;
+            bool ok = true;
+            float m = -INFINITY, l = 0.f;  // this key half's running max (log2 domain) and sum
+            for (int j = 0; j < n_tiles; j++) {
+                const int gg = g + j;
+                const int buf = gg & 1;
+                // Warp-uniform outcomes: tcgen05.ld / st below are warp-collective.
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->s_full[buf]),
+                                                                (uint32_t) (gg >> 1) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                float sc[64];
+                tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, sc);
+                tmem_ld32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf + 32, sc + 32);
+                tmem_wait_ld();
+                const int kbase = j * kBN + 64 * hf;  // key index of this warp's first column
+                if (kbase + 64 > row_keys) {
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    float o[32];
-                    tmem_ld32(ocol + c * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] *= alpha;
-                    tmem_st32(ocol + c * 32, o);
+                    for (int c = 0; c < 64; c++) sc[c] = (kbase + c < row_keys) ? sc[c] : -INFINITY;
                 }
-            }
-            // P row r, keys 64*hf.., packed f16 pairs, over the first 32 of this warp's own 64
-            // score columns (already read; the other half's columns are untouched), where the
-            // PV MMA reads its A operand from tensor memory.
-            {
-                float pkf[32];
+                // Row max of the raw scores (the scale is positive): 8 independent max3 chains.
+                float mx[8];
 #pragma unroll
-                for (int c = 0; c < 32; c++) pkf[c] = __uint_as_float(pk[c]);
-                tmem_st32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, pkf);
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[hf][buf]));
-            const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-            l = l * alpha + rs;
-            m = m_new;
-        }
-        // Epilogue: after the last PV the halves swap (m, l) per row and merge
-        // O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M));
-        // warp w writes output columns 64*(w/4) .. +63.
-        // o_done phases in order: S_{n-1}, which this warp has seen, was issued before PV_{n-2},
-        // so that phase may still be open, and a parity wait must never skip one.
-        for (int jj = max(0, n_tiles - 2); ok && jj < n_tiles; jj++)
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done), (uint32_t) jj & 1, abort_flag));
-        bars->row_m[hf][r] = m;
-        bars->row_l[hf][r] = l;
-        tc_fence_before();
-        asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
-        tc_fence_after();
-        const float m_o = bars->row_m[hf ^ 1][r], l_o = bars->row_l[hf ^ 1][r];
-        const float mm = fmaxf(m, m_o);
-        const float a_me = l > 0.f ? fast_exp2(m - mm) : 0.f;
-        const float a_ot = l_o > 0.f ? fast_exp2(m_o - mm) : 0.f;
-        const float den = l * a_me + l_o * a_ot;
-        const float inv = den > 0.f ? 1.f / den : 0.f;
-        const float c0 = (hf == 0 ? a_me : a_ot) * inv;  // weight of O_0
-        const float c1 = (hf == 0 ? a_ot : a_me) * inv;  // weight of O_1
-        const bool use0 = c0 > 0.f, use1 = c1 > 0.f;      // an O that never saw a visible key is not read
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) {
-            report(p.status, kStatusTimeout, kSitePrefillWait, warp);
-            *abort_flag = 1;
-        }
-        const bool live = tq < n_q;
-        // Output columns 64*hf + 32c .. +31 of row r: the merged O / l.
-        auto merged = [&](int c, float o[32]) {
-            float a[32], b2[32];
-            tmem_ld32(lane_base + kColO0 + 64 * hf + 32 * c, a);
-            tmem_ld32(lane_base + kColO1 + 64 * hf + 32 * c, b2);
-            tmem_wait_ld();
+                for (int i = 0; i < 8; i++) mx[i] = fmaxf(sc[i], sc[8 + i]);
 #pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = (use0 ? a[i] * c0 : 0.f) + (use1 ? b2[i] * c1 : 0.f);
-        };
-        if (tok0 + kBM / G <= n_q && n_tiles > 0) {
-            // A full tile leaves through TMA stores: O / l is staged in the K buffers (free: the
-            // last QK and PV have completed) as four 32-column boxes of 128 rows x 128 B with the
-            // 128-byte swizzle, whose row order (token, head) is the tile's.
-            if (ok) {
+                for (int c = 16; c < 64; c += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; i++) mx[i] = max3(mx[i], sc[c + i], sc[c + 8 + i]);
+                const float m_tile =
+                    fmaxf(max3(mx[0], mx[1], mx[2]), fmaxf(max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                    p.scale_log2;
+                const bool move = m_tile > m + kRescaleThreshold;  // always true for the first visible tile
+                const float m_new = move ? m_tile : m;
+                const float alpha = move ? fast_exp2(m - m_new) : 1.f;
+                const float mu = m_new == -INFINITY ? 0.f : m_new;
+                const uint64_t neg_mu2 = pack_f32x2(-mu, -mu);
+                float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < 32; c++)
+                    pk[c] = softmax_pair(sc[2 * c], sc[2 * c + 1], scale2, neg_mu2, rsum[2 * (c & 3)],
+                                         rsum[2 * (c & 3) + 1]);
+                // A moved max rescales O_hf, which PV_{gg-1} must have finished updating (PV_{gg-2}
+                // has: S_gg ready implies it). P goes to buffer gg % 2, last read by PV_{gg-2}.
+                if (j > 0 && __any_sync(0xffffffffu, move)) {
+                    if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done),
+                                                                    (uint32_t) (gg - 1) & 1, abort_flag))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        float o[32];
+                        tmem_ld32(ocol + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] *= alpha;
+                        tmem_st32(ocol + c * 32, o);
+                    }
+                }
+                // P row r, keys 64*hf.., packed f16 pairs, over the first 32 of this warp's own
+                // 64 score columns (already read), where the PV MMA reads its A operand.
+                {
+                    float pkf[32];
+#pragma unroll
+                    for (int c = 0; c < 32; c++) pkf[c] = __uint_as_float(pk[c]);
+                    tmem_st32(lane_base + (buf ? kColS1 : kColS0) + 64 * hf, pkf);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[hf][buf]));
+                const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+                l = l * alpha + rs;
+                m = m_new;
+            }
+            // Epilogue. The item's PVs: o_done phases in order (S of the last tile, which this
+            // warp has seen, was issued before the next-to-last PV, so that phase may still be
+            // open, and a parity wait must never skip one).
+            if (n_tiles > 0) {
+                for (int jj = max(0, n_tiles - 2); ok && jj < n_tiles; jj++)
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done),
+                                                                    (uint32_t) (g + jj) & 1, abort_flag));
+                // The halves swap (m, l) per row and merge O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) /
+                // (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)); warp w writes output columns 64*(w/4) .. +63.
+                bars->row_m[hf][r] = m;
+                bars->row_l[hf][r] = l;
+                if (warp == 0 && lane == 0 && store_pending) {  // the staging buffer is free again
+                    tma_store_wait_read();
+                    store_pending = false;
+                }
+                tc_fence_before();
+                asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
+                tc_fence_after();
+                const float m_o = bars->row_m[hf ^ 1][r], l_o = bars->row_l[hf ^ 1][r];
+                const float mm = fmaxf(m, m_o);
+                const float a_me = l > 0.f ? fast_exp2(m - mm) : 0.f;
+                const float a_ot = l_o > 0.f ? fast_exp2(m_o - mm) : 0.f;
+                const float den = l * a_me + l_o * a_ot;
+                const float inv = den > 0.f ? 1.f / den : 0.f;
+                const float c0 = (hf == 0 ? a_me : a_ot) * inv;  // weight of O_0
+                const float c1 = (hf == 0 ? a_ot : a_me) * inv;  // weight of O_1
+                const bool use0 = c0 > 0.f, use1 = c1 > 0.f;      // an O that never saw a visible key is not read
+                ok = __all_sync(0xffffffffu, ok);
+                // This warp's 64 output columns, 32 at a time out of both accumulators: a full tile
+                // is staged for TMA stores (four 32-column boxes of 128 rows x 128 B with the
+                // 128-byte swizzle, whose row order (token, head) is the tile's), a ragged tile's
+                // live rows are stored directly. Then O is released for the next item's PVs.
+                const bool full = I.tok0 + kBM / G <= I.n_q;
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
+                    float a[32], b2[32];
+                    tmem_ld32(lane_base + kColO0 + 64 * hf + 32 * c, a);
+                    tmem_ld32(lane_base + kColO1 + 64 * hf + 32 * c, b2);
+                    tmem_wait_ld();
                     float o[32];
-                    merged(c, o);
-                    const uint32_t box = sK + (uint32_t) (2 * hf + c) * kSub;
 #pragma unroll
-                    for (int ch = 0; ch < 8; ch++)
-                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                         box + sw128_offset((uint32_t) r, (uint32_t) ch)),
-                                     "f"(o[4 * ch]), "f"(o[4 * ch + 1]), "f"(o[4 * ch + 2]), "f"(o[4 * ch + 3])
-                                     : "memory");
+                    for (int i = 0; i < 32; i++) o[i] = (use0 ? a[i] * c0 : 0.f) + (use1 ? b2[i] * c1 : 0.f);
+                    if (full && ok) {
+                        const uint32_t box = sO + (uint32_t) (2 * hf + c) * kSub;
+#pragma unroll
+                        for (int ch = 0; ch < 8; ch++)
+                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                             box + sw128_offset((uint32_t) r, (uint32_t) ch)),
+                                         "f"(o[4 * ch]), "f"(o[4 * ch + 1]), "f"(o[4 * ch + 2]), "f"(o[4 * ch + 3])
+                                         : "memory");
+                    } else if (!full && live && ok) {
+                        float *dst = p.out + ((int64_t) (I.q_begin + tq) * p.n_head + head) * kD + 64 * hf + 32 * c;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                    }
                 }
-                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bars->o_free));
+                if (full) {
+                    if (ok) fence_proxy_async_smem();
+                    asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
+                    if (warp == 0 && lane == 0 && ok && !*abort_flag) {  // completes while the next item runs
+                        for (int bx = 0; bx < 4; bx++)
+                            tma_store_3d(&omap, sO + (uint32_t) bx * kSub, 32 * bx, I.kvh * G, I.q_begin + I.tok0);
+                        tma_store_commit();
+                        store_pending = true;
+                    }
+                }
+                g += n_tiles;
+                n_items_t++;
+            } else if (live) {
+                // no visible keys: the row's output is zero
+                float *dst = p.out + ((int64_t) (I.q_begin + tq) * p.n_head + head) * kD + 64 * hf;
+#pragma unroll
+                for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(kSoftmaxWarps * 32) : "memory");
-            if (warp == 0 && lane == 0 && !*abort_flag) {
-                for (int bx = 0; bx < 4; bx++)
-                    tma_store_3d(&omap, sK + (uint32_t) bx * kSub, 32 * bx, kvh * G, q_begin + tok0);
-                tma_store_commit_wait_read();
-            }
-        } else {
-            float *dst = p.out + ((int64_t) (q_begin + tq) * p.n_head + head) * kD + 64 * hf;
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                float o[32];
-                if (n_tiles > 0 && ok) {
-                    merged(c, o);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = 0.f;
+            // All eight warps stop at the same item if any of them failed (every warp has run this
+            // item's named barriers).
+            int any_fail;
+            asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\t"
+                         "bar.red.or.pred p, 2, %2, p;\n\tselp.s32 %0, 1, 0, p;\n\t}"
+                         : "=r"(any_fail)
+                         : "r"(ok ? 0 : 1), "r"(kSoftmaxWarps * 32)
+                         : "memory");
+            if (any_fail) {
+                if (threadIdx.x == 0) {
+                    report(p.status, kStatusTimeout, kSitePrefillWait, warp);
+                    *abort_flag = 1;
                 }
-                if (live) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4 *>(dst + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-                }
+                break;
             }
         }
+        if (warp == 0 && lane == 0 && store_pending) tma_store_wait_read();
     }
 
     tc_fence_before();
