@@ -41,8 +41,9 @@
 // P_j occupies S_j's columns [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2}
 // overwrites them only after PV_j, which the tensor core executes first.
 // Every mbarrier wait is on a parity at most one phase from the arrivals: per-buffer barriers
-// (K, V, S, P) indexed by a running tile count across items, the o_done phases waited in order,
-// and one q_full / q_empty / o_free phase per item.
+// (K, V, S, P) indexed by a running tile count across items, o_done (one phase per PV) waited
+// only for the PV just before the waiter's own next P, and one q_full / q_empty / o_free /
+// o_final phase per item.
 // Measured limit: per 128-key tile the tensor core runs 8 SS MMAs (S) and 8 TS MMAs (PV) of
 // 128x128x16; alternating the two forms costs well above the nominal 64 cycles per MMA, and
 // the issuing thread stays blocked on the MMA queue, so the softmax (about half the tile time)
@@ -106,7 +107,11 @@ struct Barriers {
     // per S buffer keeps every wait within one phase of the arrivals: P_{j+2} needs S_{j+2},
     // which the MMA issuer creates only after it has seen P_j.
     uint64_t p_full[2][2];
-    uint64_t o_done;
+    uint64_t o_done;   // one completion per PV (read by a softmax warp before it rescales O)
+    // One completion per item, after its last PV: the epilogue's wait. The next item's PVs need
+    // the epilogue's o_free first, so this barrier is never two phases ahead of a waiter (o_done
+    // can be, when a softmax warp is slow to reach its epilogue).
+    uint64_t o_final;
     uint64_t mma_drain;
     uint32_t tmem_base;
     int abort;
@@ -344,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         for (int h = 0; h < 2; h++)
             for (int i = 0; i < 2; i++) mbar_init(smem_u32(&bars->p_full[h][i]), kSoftmaxWarps / 2);
         mbar_init(smem_u32(&bars->o_done), 1);
+        mbar_init(smem_u32(&bars->o_final), 1);
         mbar_init(smem_u32(&bars->mma_drain), 1);
         fence_barrier_init();
     }
@@ -364,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     // Every role walks the same item sequence. Barrier phases come from running counters: g, the
     // global index of a K/V tile in this CTA (buffer g % 2, parity (g / 2) % 2 for the per-buffer
     // barriers; parity g % 2 for o_done, one completion per PV), and the count of items that have
-    // tiles (q_full, q_empty, o_free: one completion per item).
+    // tiles (q_full, q_empty, o_free, o_final: one completion per item).
     if (warp == kWarpTmaK || warp == kWarpTmaV) {
         // ---- TMA producers: warp 8 streams Q and the K tiles, warp 10 the V tiles, each into
         // its own double buffer, running ahead into the next item while the current one ends.
@@ -462,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             constexpr uint32_t idesc_qk = idesc_f16(false);
             constexpr uint32_t idesc_pv = idesc_f16(true);
             int g = 0, n_items_t = 0;
-            bool ok = true;
+            bool ok = true, issued = false;
             // S_gg = Q K_gg^T into S buffer gg % 2; after the item's last S, Q may be reloaded.
             auto issue_qk = [&](int gg, bool last) -> bool {
                 const int buf = gg & 1;
@@ -479,6 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 mma_commit(smem_u32(&bars->s_full[buf]));
                 mma_commit(smem_u32(&bars->k_empty[buf]));
                 if (last) mma_commit(smem_u32(&bars->q_empty));
+                issued = true;
                 return true;
             };
             for (int r = 0; ok; r++) {
@@ -529,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     if (!ok) break;
                     mma_commit(smem_u32(&bars->o_done));
                     mma_commit(smem_u32(&bars->v_empty[buf]));
+                    if (j == n - 1) mma_commit(smem_u32(&bars->o_final));
                     if (j + 2 < n && !issue_qk(gg + 2, j + 2 == n - 1)) {
                         ok = false;
                         break;
@@ -542,8 +550,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 *abort_flag = 1;
             }
             // Every MMA issued so far completes before TMEM can be released.
-            mma_commit(smem_u32(&bars->mma_drain));
-            mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
+            if (issued) {
+                mma_commit(smem_u32(&bars->mma_drain));
+                mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
+            }
         }
     } else {
         // ---- softmax warps 0..7: warp w owns rows 32*(w%4).. and the key half w/4 of every
@@ -647,13 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 l = l * alpha + rs;
                 m = m_new;
             }
-            // Epilogue. The item's PVs: o_done phases in order (S of the last tile, which this
-            // warp has seen, was issued before the next-to-last PV, so that phase may still be
-            // open, and a parity wait must never skip one).
+            // Epilogue: every PV of the item has completed (o_final, one phase per item).
             if (n_tiles > 0) {
-                for (int jj = max(0, n_tiles - 2); ok && jj < n_tiles; jj++)
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done),
-                                                                    (uint32_t) (g + jj) & 1, abort_flag));
+                if (ok)
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_final),
+                                                                    (uint32_t) n_items_t & 1, abort_flag));
                 // The halves swap (m, l) per row and merge O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) /
                 // (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)); warp w writes output columns 64*(w/4) .. +63.
                 bars->row_m[hf][r] = m;
