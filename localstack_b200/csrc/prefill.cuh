@@ -155,6 +155,27 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// The same MMAs with the accumulate flag known at compile time. The tensor core's instruction
+// queue is shallow, so every instruction the issuing thread spends between MMAs can leave it idle.
+template <int ACC>
+__device__ __forceinline__ void mma_f16_ss_k(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "n"(ACC)
+        : "memory");
+}
+template <int ACC>
+__device__ __forceinline__ void mma_f16_ts_k(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "n"(ACC)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -467,6 +488,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16(false);
             constexpr uint32_t idesc_pv = idesc_f16(true);
+            // Shared-memory descriptors as (low, high) words, built once: the high word is fixed,
+            // the low word holds address >> 4 (tiles stay below 256 KiB, so offsets never carry
+            // out of it), so each MMA needs one add for its operand addresses.
+            const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024), dk0 = sdesc_sw128(sK, 16, 1024),
+                           dv0 = sdesc_sw128(sV, kSub, 1024);
+            const uint32_t lq = (uint32_t) dq0, lk = (uint32_t) dk0, lv = (uint32_t) dv0;
+            const uint64_t hq = dq0 & 0xFFFFFFFF00000000ull, hk = dk0 & 0xFFFFFFFF00000000ull,
+                           hv = dv0 & 0xFFFFFFFF00000000ull;
             int g = 0, n_items_t = 0;
             bool ok = true, issued = false;
             // S_gg = Q K_gg^T into S buffer gg % 2; after the item's last S, Q may be reloaded.
@@ -476,11 +505,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem + (buf ? kColS1 : kColS0);
+                const uint32_t lkb = lk + (uint32_t) buf * (kTile >> 4);
+                mma_f16_ss_k<0>(d, hq | lq, hk | lkb, idesc_qk);
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t off = (uint32_t) ((kk >> 2) * kSub + (kk & 3) * 32);
-                    mma_f16_ss(d, sdesc_sw128(sQ + off, 16, 1024), sdesc_sw128(sK + buf * kTile + off, 16, 1024),
-                               idesc_qk, kk > 0 ? 1u : 0u);
+                for (int kk = 1; kk < 8; kk++) {
+                    const uint32_t off = (uint32_t) (((kk >> 2) * kSub + (kk & 3) * 32) >> 4);
+                    mma_f16_ss_k<1>(d, hq | (lq + off), hk | (lkb + off), idesc_qk);
                 }
                 mma_commit(smem_u32(&bars->s_full[buf]));
                 mma_commit(smem_u32(&bars->k_empty[buf]));
@@ -524,14 +554,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                             break;
                         }
                         tc_fence_after();
+                        // V rows of K step kk: 16 keys x 128 B = 128 descriptor units from the tile start.
+                        const uint32_t oc = tmem + (h ? kColO1 : kColO0), pc = pcol + (uint32_t) (h * 64);
+                        const uint32_t lvb = lv + (uint32_t) buf * (kTile >> 4) + (uint32_t) (4 * h) * 128u;
+                        mma_f16_ts(oc, pc, hv | lvb, idesc_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-                        for (int kq = 0; kq < 4; kq++) {
-                            const int kk = 4 * h + kq;
-                            const uint32_t boff = (uint32_t) (kk * 16 * 128);  // 16 keys x 128 B
-                            mma_f16_ts(tmem + (h ? kColO1 : kColO0), pcol + (uint32_t) (h * 64 + kq * 8),
-                                       sdesc_sw128(sV + buf * kTile + boff, kSub, 1024), idesc_pv,
-                                       (j > 0 || kq > 0) ? 1u : 0u);
-                        }
+                        for (int kq = 1; kq < 4; kq++) mma_f16_ts_k<1>(oc, pc + kq * 8, hv | (lvb + kq * 128u), idesc_pv);
                     }
                     if (!ok) break;
                     mma_commit(smem_u32(&bars->o_done));
