@@ -45,9 +45,10 @@
 // only for the PV just before the waiter's own next P, and one q_full / q_empty / o_free /
 // o_final phase per item.
 // Measured limit: per 128-key tile the tensor core runs 8 SS MMAs (S) and 8 TS MMAs (PV) of
-// 128x128x16; alternating the two forms costs well above the nominal 64 cycles per MMA, and
-// the issuing thread stays blocked on the MMA queue, so the softmax (about half the tile time)
-// is hidden and the kernel is bound by the tensor pipe's rate for this mix.
+// 128x128x16, 64 cycles each when fed back to back. Its instruction queue is shallow, so every
+// stall of the one issuing thread (a barrier check, lost issue slots to the busy softmax warps)
+// leaves it idle; with one tile of lookahead (two S buffers) the round trip S_j -> softmax ->
+// PV_j -> S_{j+2} through that thread bounds the kernel at about 2.2 k cycles per tile.
 //
 // Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
 //   Q, K: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
