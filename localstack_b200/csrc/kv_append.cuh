@@ -33,8 +33,8 @@ constexpr int kWarps = 4;
 constexpr int kRowsPerWarp = 32;  // at most; the launch picks 8, 16 or 32 (Params::rows_per_warp)
 // Staged rows keep the input type and layout, 16 bytes of padding after each (16-byte aligned
 // rows for the 16-byte copies): bf16 rows of 68 32-bit words, f32 rows of 132 floats. Lanes
-// reading one row in the write phase hit distinct banks; lane r reading its own row r word by
-// word (the sum) has 4-way conflicts, small next to the sum's dependent double adds.
+// reading one row in the write phase hit distinct banks, and so do lanes reading their own rows
+// 16 bytes at a time for the sum (row starts are 17 or 33 16-byte units apart).
 constexpr int kStrideBf16Words = 68;
 constexpr int kStrideF32 = 132;
 constexpr int kRowBytes = 32 * kStrideBf16Words * 4;  // rows of one group: 32 bf16 rows or 16 f32 rows
@@ -89,6 +89,14 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
+// Shared-memory layouts chosen so that the write loop's 16-byte reads are free of bank conflicts.
+// In the write loop lane c (of eight per row) reads gamma chunks 2c + q + 16h (four floats each)
+// and the (cos, sin) chunks 4c + q of a RoPE row; eight lanes of a quarter-warp then hit the
+// same banks two (gamma) or four (RoPE) at a time in the natural order. Gamma chunk k is stored
+// at slot k ^ ((k >> 3) & 1), RoPE chunk 4c + q at 4c + ((q + (c >> 1)) & 3).
+__device__ __forceinline__ int gamma_slot(int k) { return k ^ ((k >> 3) & 1); }
+__device__ __forceinline__ int rope_slot(int k) { return (k & ~3) | (((k & 3) + ((k >> 3) & 3)) & 3); }
+
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
     extern __shared__ __align__(16) uint8_t stage_smem[];
     float *s_gamma = reinterpret_cast<float *>(stage_smem);  // [2][128]: q_gamma, k_gamma (1 when absent)
@@ -100,8 +108,9 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < kD; i += blockDim.x) {
-        s_gamma[i] = p.q_gamma != nullptr ? p.q_gamma[i] : 1.f;
-        s_gamma[kD + i] = p.k_gamma != nullptr ? p.k_gamma[i] : 1.f;
+        const int at = gamma_slot(i >> 2) * 4 + (i & 3);
+        s_gamma[at] = p.q_gamma != nullptr ? p.q_gamma[i] : 1.f;
+        s_gamma[kD + at] = p.k_gamma != nullptr ? p.k_gamma[i] : 1.f;
     }
     __syncthreads();
     const int R = p.n_head + 2 * p.n_head_kv;
@@ -165,7 +174,7 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
             const int src = (int) (first_row < 0 ? 0 : (first_row > 31 ? 31 : first_row));
             const int pos = __shfl_sync(0xffffffffu, my_pos, src);
             if (first_row < nr && pos >= 0 && pos < p.rope_n_pos)
-                cp_async_16(stage_u32 + (uint32_t) (kRowBytes + u * kD * 4 + lane * 16),
+                cp_async_16(stage_u32 + (uint32_t) (kRowBytes + u * kD * 4 + rope_slot(lane) * 16),
                             p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
         }
         cp_async_wait_all();
@@ -177,17 +186,29 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
             const float *gamma = my_j < p.n_head ? p.q_gamma : p.k_gamma;
             if (gamma != nullptr) {
                 double sum = 0.0;
+                // 16-byte reads (rows start 272 or 528 bytes apart: the eight lanes of a quarter-warp
+                // cover all 32 banks), summed in index order.
                 if (p.in_bf16) {
-                    const uint32_t *row = sw + lane * kStrideBf16Words;
-                    for (int i = 0; i < kD / 2; i++) {
-                        const uint32_t w = row[i];
-                        const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xffff0000u);
-                        sum = __dadd_rn(sum, (double) __fmul_rn(a, a));
-                        sum = __dadd_rn(sum, (double) __fmul_rn(b, b));
+                    const uint4 *row = reinterpret_cast<const uint4 *>(sw + lane * kStrideBf16Words);
+                    for (int i4 = 0; i4 < kD / 8; i4++) {
+                        const uint4 w4 = row[i4];
+                        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float a = __uint_as_float(ws[e] << 16), b = __uint_as_float(ws[e] & 0xffff0000u);
+                            sum = __dadd_rn(sum, (double) __fmul_rn(a, a));
+                            sum = __dadd_rn(sum, (double) __fmul_rn(b, b));
+                        }
                     }
                 } else {
-                    const float *row = sf + lane * kStrideF32;
-                    for (int i = 0; i < kD; i++) sum = __dadd_rn(sum, (double) __fmul_rn(row[i], row[i]));
+                    const float4 *row = reinterpret_cast<const float4 *>(sf + lane * kStrideF32);
+                    for (int i4 = 0; i4 < kD / 4; i4++) {
+                        const float4 v4 = row[i4];
+                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.x, v4.x));
+                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.y, v4.y));
+                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.z, v4.z));
+                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.w, v4.w));
+                    }
                 }
                 const float mean = __double2float_rn(__ddiv_rn(sum, (double) kD));
                 my_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
@@ -220,6 +241,12 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         // owns NEOX pairs [8c, 8c+8) - elements 8c..8c+7 and 64+8c..64+8c+7 - moved as 16-byte
         // vectors. Branch-free arithmetic per element (selects).
         const int sub = lane >> 3, c = lane & 7;
+        int goff[4], coff[4];  // float offsets of this lane's gamma chunks and staged RoPE chunks
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            goff[q] = gamma_slot(2 * c + (q & 1) + 16 * (q >> 1)) * 4;
+            coff[q] = rope_slot(4 * c + q) * 4;
+        }
         for (int r0 = 0; r0 < nr; r0 += 4) {
             const int r = r0 + sub;
             const int from = r < nr ? r : r0;
@@ -260,19 +287,35 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
             const float *g = s_gamma + (is_q ? 0 : kD);
             // (cos, sin) of pairs 8c..8c+7: staged for the group's first tokens, else from the table
             // (Q / K rows have a checked position; V rows use none of it)
+            const bool staged = u < kCsTokens || is_v;
             const float *csr = u < kCsTokens ? s_cs + u * kD
                                              : is_v ? s_cs
                                                     : reinterpret_cast<const float *>(p.rope + (int64_t) pos * (kD / 2));
+            // gamma of elements 8c..8c+7 and 64+8c..64+8c+7; (cos, sin) of pairs 8c..8c+7 (pair
+            // e: elements e and 64 + e of the lane's slice), as 16-byte reads
+            float gm[16], cs[16];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 gv = *reinterpret_cast<const float4 *>(g + goff[q]);
+                gm[4 * q] = gv.x;
+                gm[4 * q + 1] = gv.y;
+                gm[4 * q + 2] = gv.z;
+                gm[4 * q + 3] = gv.w;
+                const float4 cv = *reinterpret_cast<const float4 *>(csr + (staged ? coff[q] : 16 * c + 4 * q));
+                cs[4 * q] = cv.x;
+                cs[4 * q + 1] = cv.y;
+                cs[4 * q + 2] = cv.z;
+                cs[4 * q + 3] = cv.w;
+            }
             float o[16];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                const int i = 8 * c + e;  // pair (i, i + 64)
                 float a = x[e], b = x[8 + e];
-                const float ya = __fmul_rn(__fmul_rn(a, scale), g[i]);
-                const float yb = __fmul_rn(__fmul_rn(b, scale), g[i + 64]);
+                const float ya = __fmul_rn(__fmul_rn(a, scale), gm[e]);
+                const float yb = __fmul_rn(__fmul_rn(b, scale), gm[8 + e]);
                 a = normed ? ya : a;
                 b = normed ? yb : b;
-                const float cx = csr[2 * i], sy = csr[2 * i + 1];
+                const float cx = cs[2 * e], sy = cs[2 * e + 1];
                 const float oa = __fsub_rn(__fmul_rn(a, cx), __fmul_rn(b, sy));
                 const float ob = __fadd_rn(__fmul_rn(a, sy), __fmul_rn(b, cx));
                 o[e] = is_v ? x[e] : oa;  // V rows are stored as read
