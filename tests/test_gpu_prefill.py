@@ -101,6 +101,30 @@ def test_long_prompt_many_key_tiles():
     assert within(got, want), max_err(got, want)
 
 
+def test_mostly_empty_items():
+    """A 200-token and a 1-token prompt: 64 items on 64 CTAs, 24 of which get only items past the
+    short prompt's end (no keys, no MMA). Those CTAs must skip the tensor-core drain rather than
+    wait on it, and every live row must still match: three calls well inside half a second (a
+    wait that ran to its bound would take a second)."""
+    import time
+    out, ex = _prefill_case([200, 1], [0, 0], 16, 8, seed=31)
+    assert within(out, ex), max_err(out, ex)
+    rng = np.random.default_rng(31)
+    bt, n_pages = scattered_block_tables(rng, [200, 1])
+    kc, vc = random_cache(rng, n_pages, 8)
+    q = torch.from_numpy(random_q(rng, 201, 16).astype(np.float16)).to(DEV)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=DEV)
+    args = (_f16(kc), _f16(vc), q, i32(0, 200, 201), i32(0, 0), i32(200, 1), torch.from_numpy(bt).to(DEV), 200, SCALE)
+    L.attn_prefill(*args)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        L.attn_prefill(*args)
+    torch.cuda.synchronize()
+    L.check_status()
+    assert time.perf_counter() - t0 < 0.5
+
+
 def test_f32_query_input():
     out, ex = _prefill_case([129, 64], [5, 0], 16, 8, seed=8, q_dtype=torch.float32)
     assert within(out, ex), max_err(out, ex)
