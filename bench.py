@@ -32,6 +32,12 @@ N_SEQS = 64
 CTX_LO, CTX_HI = 1024, 32768
 SCALE = 1.0 / math.sqrt(D)
 SEED = 0
+# DRAM traffic of decode_split_kernel per algorithmic byte, from one ncu capture of the same
+# workload at 16 sequences (dram__bytes_read.sum + dram__bytes_write.sum = 559.04 + 3.52 MB for
+# 558.81 MB of algorithmic bytes; profiles/decode_split_kernel_config3_16seq.md). The kernel
+# reads every K/V byte once, so its traffic grows in proportion and the 64-sequence launch's
+# traffic is this ratio times its algorithmic bytes.
+DECODE_TRAFFIC_PER_BYTE = (559.04 + 3.52) / 558.81
 
 
 def peaks():
@@ -430,7 +436,9 @@ def run_b200(args):
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": read_bytes, "launch_ms": round(dec_ms, 4),
-                         "traffic": None},
+                         "traffic": round(read_bytes * DECODE_TRAFFIC_PER_BYTE),
+                         "traffic_source": "ncu DRAM bytes of decode_split_kernel on the 16-sequence "
+                                           "capture, scaled by algorithmic bytes"},
             "e2e": {"value": round(all_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "pipeline": "double-buffered pinned staging; H2D and D2H on their own streams overlap the "
