@@ -218,7 +218,10 @@ int lstk_cuda_attn_exchange_merge(void *const *mailboxes, int32_t rank, int32_t 
  * the chunk (lstk_cuda_kv_append first, as attn_block writes set_rows before flash_attn_ext).
  *   q            [total_tokens][n_head][head_dim], f16 (the tensor-core operand type) or f32
  *                (converted into the workspace first)
- *   q_seq_start  [n_seqs + 1] int32 device; max_q_len = host upper bound of any sequence's rows
+ *   q_seq_start  [n_seqs + 1] int32 device; max_q_len = host upper bound of any sequence's rows.
+ *                A sequence whose rows are not inside [0, total_tokens) (or whose start exceeds
+ *                its end) is skipped - nothing is read or written for it - and lstk_cuda_status
+ *                reports LSTK_ERR_DEVICE_INDEX (site 23, detail = the sequence index)
  *   out          [total_tokens][n_head][head_dim] f32
  * Computed with tcgen05 tensor-core MMAs (f16 x f16 -> f32 in tensor memory) on 128-row query
  * tiles and 128-key tiles fed by TMA from the scattered pages. The workspace is sized by

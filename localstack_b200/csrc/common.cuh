@@ -34,6 +34,7 @@ enum : int {
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
     kSitePrefillSmem = 22,
+    kSitePrefillRows = 23,
     kSiteExchangeWait = 30,
     kSitePagesSlot = 40,
     kSitePagesTokens = 41,

@@ -482,6 +482,7 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
     p.n_head_kv = hkv;
     p.group = group;
     p.n_qt = (max_q_len + tpt - 1) / tpt;
+    p.total_tokens = (int) total_tokens;
     p.q_seq_start = q_seq_start;
     p.q_pos0 = q_pos0;
     p.kv_lens = kv_lens;

@@ -86,6 +86,7 @@ constexpr int kSmemBytes = kOffBar + 2304;  // + barriers and row statistics
 
 struct Params {
     int n_seqs, n_head, n_head_kv, group, n_qt, n_items;
+    int total_tokens;  // rows of q and out: every sequence's [q_seq_start[b], q_seq_start[b+1]) must lie inside
     const int32_t *q_seq_start;
     const int32_t *q_pos0;
     const int32_t *kv_lens;
@@ -289,6 +290,7 @@ extern __shared__ __align__(1024) uint8_t dyn_smem[];
 // query positions first); an item past its sequence's end has no keys and no live rows.
 struct Item {
     int b, kvh, tok0, q_begin, n_q, kv_len, pos0, n_keys, n_tiles;
+    bool bad_rows;  // the sequence's query rows are not inside [0, total_tokens): no rows, reported
 };
 
 // An item's sequence metadata as loaded; item_finish derives the rest, so a loop can issue the
@@ -316,7 +318,10 @@ __device__ __forceinline__ Item item_finish(const Params &p, const ItemRaw &r) {
     it.kvh = r.kvh;
     it.tok0 = r.tok0;
     it.q_begin = r.q0;
-    it.n_q = r.q1 - r.q0;
+    // Rows come from device memory: a range outside q / out or a decreasing start gives the
+    // sequence no rows (nothing is read or written for it) and is reported once.
+    it.bad_rows = r.q0 < 0 || r.q1 < r.q0 || r.q1 > p.total_tokens;
+    it.n_q = it.bad_rows ? 0 : r.q1 - r.q0;
     it.kv_len = max(0, min(r.kv_len_raw, p.max_blocks * kPage));
     it.pos0 = r.pos0;
     const int last_tok = min(it.tok0 + kBM / p.group, it.n_q) - 1;
@@ -599,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         ItemRaw raw_next = x >= 0 ? item_load(p, x) : ItemRaw{};
         for (int it = 0; x >= 0; it++) {
             const Item I = item_finish(p, raw_next);
+            if (I.bad_rows && warp == 0 && lane == 0) report(p.status, kStatusBadIndex, kSitePrefillRows, I.b);
             // The next item's metadata loads are issued now and used one item later.
             const int x_next = item_index(p, it + 1);
             if (x_next >= 0) raw_next = item_load(p, x_next);

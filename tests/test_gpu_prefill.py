@@ -151,6 +151,29 @@ def test_chunked_equals_single_prefill():
     assert within(chunked.cpu().numpy(), whole.cpu().numpy(), atol=1e-5, rtol=1e-5)
 
 
+def test_bad_query_rows_report_device_index():
+    """Sequence 1's rows run past total_tokens: it is skipped (its neighbour's rows are still
+    right and nothing past the valid rows is written) and the status reports the sequence."""
+    rng = np.random.default_rng(17)
+    bt, n_pages = scattered_block_tables(rng, [70, 70])
+    kc, vc = random_cache(rng, n_pages, 8)
+    q16 = random_q(rng, 140, 16).astype(np.float16)
+    i32 = lambda *v: torch.tensor(v, dtype=torch.int32, device=DEV)
+    out = torch.full((140, 16, 128), 7.0, device=DEV)
+    L.attn_prefill(_f16(kc), _f16(vc), torch.from_numpy(q16).to(DEV), i32(0, 70, 150), i32(0, 0), i32(70, 70),
+                   torch.from_numpy(bt).to(DEV), 80, SCALE, out=out)
+    with pytest.raises(L.LstkError) as e:
+        L.check_status()
+    assert e.value.code == -6 and "site 23" in str(e.value) and "detail 1" in str(e.value)
+    got = out.cpu().numpy()
+    assert np.all(got[70:] == 7.0)  # the skipped sequence's rows are untouched
+    q_seq = np.zeros(70, np.int32)
+    q_pos = np.arange(70, dtype=np.int32)
+    ex = O.paged_attn(q16[:70].astype(np.float32), q_seq, q_pos, kc, vc, bt[:1], [70], SCALE, causal=True,
+                      mode=O.MODE_EXACT)
+    assert within(got[:70], ex), max_err(got[:70], ex)
+
+
 def test_bad_page_reports_device_index():
     kc = L.alloc_cache(128, 8, DEV)
     vc = L.alloc_cache(128, 8, DEV)
