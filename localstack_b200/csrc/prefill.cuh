@@ -17,11 +17,13 @@
 //   warps 8, 10  TMA producers: Q (per item, once the item's last QK has read the previous one)
 //           and K_j (warp 8), V_j (warp 10), each into a double buffer, running ahead into the next
 //           item; the block table is read a warp at a time, one chunk of 32 pages ahead.
-//   warp 9  MMA issuer (one lane): S_{j+1} = Q K_{j+1}^T into TMEM buffer (j+1)%2 is issued before
-//           waiting for softmax j, so the tensor core computes the next scores while the
-//           softmax warps work; then O += P_j V_j with P_j read from tensor memory (TS form). The
-//           next item's first scores follow this item's last PV; its first PV waits until the
-//           epilogue has read O out.
+//   warp 9  S issuer (one lane): S_j = Q K_j^T into TMEM buffer j%2 once K_j has landed and PV_{j-2}
+//           (which read P_{j-2} from the same columns) has completed, so it runs up to two tiles
+//           ahead of the softmax, into the next item while the current one ends.
+//   warp 11 PV issuer (one lane): O_h += P_j V_j per key half with P_j read from tensor memory
+//           (TS form), as soon as that half's softmax warps have written it; an item's first PV
+//           waits until the previous epilogue has read O out. Two issuing threads keep the
+//           tensor core's shallow queue fed while either of them waits on a barrier.
 //   warps 0-7  softmax: warp w owns the 32 rows of TMEM quadrant w%4 and key half w/4 of every
 //           tile (its 64 score columns), so two warps on each SM sub-partition share the tile's
 //           exp work. Each key half keeps its own running max, row sum and O accumulator (O_0,
@@ -39,16 +41,15 @@
 // the previous kernel, and griddepcontrol.wait precedes every read of earlier work.
 // TMEM: S0 cols [0,128), S1 [128,256), O_0 [256,384), O_1 [384,512) (f32, 128 lanes = 128 rows).
 // P_j occupies S_j's columns [0,32) (keys 0..63) and [64,96) (keys 64..127); QK_{j+2}
-// overwrites them only after PV_j, which the tensor core executes first.
+// overwrites them only after PV_j has completed (o_done).
 // Every mbarrier wait is on a parity at most one phase from the arrivals: per-buffer barriers
-// (K, V, S, P) indexed by a running tile count across items, o_done (one phase per PV) waited
-// only for the PV just before the waiter's own next P, and one q_full / q_empty / o_free /
-// o_final phase per item.
+// (K, V, S, P, o_done) indexed by a running tile count across items, and one q_full / q_empty /
+// o_free / o_final phase per item.
 // Measured limit: per 128-key tile the tensor core runs 8 SS MMAs (S) and 8 TS MMAs (PV) of
-// 128x128x16, 64 cycles each when fed back to back. Its instruction queue is shallow, so every
-// stall of the one issuing thread (a barrier check, lost issue slots to the busy softmax warps)
-// leaves it idle; with one tile of lookahead (two S buffers) the round trip S_j -> softmax ->
-// PV_j -> S_{j+2} through that thread bounds the kernel at about 2.2 k cycles per tile.
+// 128x128x16, 64 cycles each when fed back to back. Its instruction queue is shallow, so stalls
+// of the issuing threads (barrier checks, issue slots lost to the busy softmax warps) leave it
+// idle; with one tile of lookahead (two S buffers) the round trip S_j -> softmax -> PV_j ->
+// S_{j+2} bounds the kernel at about 2.1 k cycles per tile.
 //
 // Operand layouts (UMMA shared-memory descriptors, 128-byte swizzle, atoms of 8 rows x 128 B):
 //   Q, K: K-major (contraction dim contiguous), two 16 KiB sub-tiles of 64 columns.
@@ -70,9 +71,10 @@ constexpr int kTile = kBM * kD * 2;  // 32 KiB
 constexpr int kSub = kTile / 2;      // 16 KiB: 128 rows x 128 B
 constexpr int kSoftmaxWarps = 8;
 constexpr int kWarpTmaK = 8;   // Q and K producer
-constexpr int kWarpMma = 9;
+constexpr int kWarpMma = 9;     // S (QK) MMA issuer; allocates TMEM
 constexpr int kWarpTmaV = 10;  // V producer
-constexpr int kThreads = 352;
+constexpr int kWarpMmaPv = 11; // PV MMA issuer
+constexpr int kThreads = 384;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 384;
 
@@ -103,18 +105,19 @@ struct Barriers {
     uint64_t q_full;
     uint64_t q_empty;  // the item's last S MMA has read Q: the next item's Q may load
     uint64_t o_free;   // the softmax warps have read O out: the next item's first PV may write it
-    uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
+    uint64_t k_full[2], v_full[2];  // K_j / V_j landed; their buffers are freed by s_full / o_done
     uint64_t s_full[2];
     // P_j of key half h: one arrival per softmax warp of that half, on p_full[h][j % 2]. A barrier
     // per S buffer keeps every wait within one phase of the arrivals: P_{j+2} needs S_{j+2},
-    // which the MMA issuer creates only after it has seen P_j.
+    // which the S issuer creates only after PV_j (which needed P_j) has completed.
     uint64_t p_full[2][2];
-    uint64_t o_done;   // one completion per PV (read by a softmax warp before it rescales O)
+    // PV_j done, on o_done[j % 2]: V_j's buffer and P_j's TMEM columns are free, and O may be
+    // rescaled by a softmax warp.
+    uint64_t o_done[2];
     // One completion per item, after its last PV: the epilogue's wait. The next item's PVs need
-    // the epilogue's o_free first, so this barrier is never two phases ahead of a waiter (o_done
-    // can be, when a softmax warp is slow to reach its epilogue).
+    // the epilogue's o_free first, so this barrier is never two phases ahead of a waiter.
     uint64_t o_final;
-    uint64_t mma_drain;
+    uint64_t mma_drain[2];  // per MMA-issuing thread
     uint32_t tmem_base;
     int abort;
     float row_m[2][kBM], row_l[2][kBM];  // per key half: running max (log2 domain) and sum per row
@@ -369,15 +372,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         for (int i = 0; i < 2; i++) {
             mbar_init(smem_u32(&bars->k_full[i]), 1);
             mbar_init(smem_u32(&bars->v_full[i]), 1);
-            mbar_init(smem_u32(&bars->k_empty[i]), 1);
-            mbar_init(smem_u32(&bars->v_empty[i]), 1);
             mbar_init(smem_u32(&bars->s_full[i]), 1);
+            mbar_init(smem_u32(&bars->o_done[i]), 1);
+            mbar_init(smem_u32(&bars->mma_drain[i]), 1);
         }
         for (int h = 0; h < 2; h++)
             for (int i = 0; i < 2; i++) mbar_init(smem_u32(&bars->p_full[h][i]), kSoftmaxWarps / 2);
-        mbar_init(smem_u32(&bars->o_done), 1);
         mbar_init(smem_u32(&bars->o_final), 1);
-        mbar_init(smem_u32(&bars->mma_drain), 1);
         fence_barrier_init();
     }
     if (warp == kWarpMma) {
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 if (lane == 0) {
                     const int buf = g & 1;
                     const uint32_t use = (uint32_t) (g >> 1);
-                    const uint32_t empty = smem_u32(is_k ? &bars->k_empty[buf] : &bars->v_empty[buf]);
+                    const uint32_t empty = smem_u32(is_k ? &bars->s_full[buf] : &bars->o_done[buf]);
                     const uint32_t full = smem_u32(is_k ? &bars->k_full[buf] : &bars->v_full[buf]);
                     if (use > 0) ok = mbar_wait_bounded(empty, (use - 1) & 1, abort_flag);
                     if (ok) {
@@ -490,91 +491,47 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             }
         }
     } else if (warp == kWarpMma) {
-        // ---- MMA issuer ----
+        // ---- S issuer: S_gg = Q K_gg^T into TMEM buffer gg % 2, once K_gg has landed and PV_{gg-2}
+        // (same buffer: it read P_{gg-2} from these columns) has completed. Two issuing threads,
+        // one for S and one for PV, keep the tensor core's shallow queue fed while either waits
+        // on a barrier. A commit tracks only the committing thread's MMAs: s_full[gg % 2] also
+        // frees K buffer gg % 2; after the item's last S, Q may be reloaded. ----
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16(false);
-            constexpr uint32_t idesc_pv = idesc_f16(true);
             // Shared-memory descriptors as (low, high) words, built once: the high word is fixed,
             // the low word holds address >> 4 (tiles stay below 256 KiB, so offsets never carry
             // out of it), so each MMA needs one add for its operand addresses.
-            const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024), dk0 = sdesc_sw128(sK, 16, 1024),
-                           dv0 = sdesc_sw128(sV, kSub, 1024);
-            const uint32_t lq = (uint32_t) dq0, lk = (uint32_t) dk0, lv = (uint32_t) dv0;
-            const uint64_t hq = dq0 & 0xFFFFFFFF00000000ull, hk = dk0 & 0xFFFFFFFF00000000ull,
-                           hv = dv0 & 0xFFFFFFFF00000000ull;
+            const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024), dk0 = sdesc_sw128(sK, 16, 1024);
+            const uint32_t lq = (uint32_t) dq0, lk = (uint32_t) dk0;
+            const uint64_t hq = dq0 & 0xFFFFFFFF00000000ull, hk = dk0 & 0xFFFFFFFF00000000ull;
             int g = 0, n_items_t = 0;
             bool ok = true, issued = false;
-            // S_gg = Q K_gg^T into S buffer gg % 2; after the item's last S, Q may be reloaded.
-            auto issue_qk = [&](int gg, bool last) -> bool {
-                const int buf = gg & 1;
-                if (!mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag))
-                    return false;
-                tc_fence_after();
-                const uint32_t d = tmem + (buf ? kColS1 : kColS0);
-                const uint32_t lkb = lk + (uint32_t) buf * (kTile >> 4);
-                mma_f16_ss_k<0>(d, hq | lq, hk | lkb, idesc_qk);
-#pragma unroll
-                for (int kk = 1; kk < 8; kk++) {
-                    const uint32_t off = (uint32_t) (((kk >> 2) * kSub + (kk & 3) * 32) >> 4);
-                    mma_f16_ss_k<1>(d, hq | (lq + off), hk | (lkb + off), idesc_qk);
-                }
-                mma_commit(smem_u32(&bars->s_full[buf]));
-                mma_commit(smem_u32(&bars->k_empty[buf]));
-                if (last) mma_commit(smem_u32(&bars->q_empty));
-                issued = true;
-                return true;
-            };
             for (int r = 0; ok; r++) {
                 const int x = item_index(p, r);
                 if (x < 0) break;
                 const int n = item_at(p, x).n_tiles;
                 if (n == 0) continue;
-                // Order: S_0, S_1, then per tile j: PV_j (once its halves have written P_j) and
-                // S_{j+2} into the buffer PV_j has just read (the tensor core runs one thread's
-                // MMAs in order). The next item's S_0 / S_1 follow this item's last PV, so they run
-                // during this item's epilogue.
                 ok = mbar_wait_bounded(smem_u32(&bars->q_full), (uint32_t) n_items_t & 1, abort_flag);
-                if (ok) ok = issue_qk(g, n == 1);
-                if (ok && n > 1) ok = issue_qk(g + 1, n == 2);
                 for (int j = 0; ok && j < n; j++) {
                     const int gg = g + j;
                     const int buf = gg & 1;
-                    if (!mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    // The item's first PV overwrites O: the previous item's epilogue must have read it.
-                    if (j == 0 && n_items_t > 0 &&
-                        !mbar_wait_bounded(smem_u32(&bars->o_free), (uint32_t) (n_items_t - 1) & 1, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    // P_gg sits in TMEM over S_gg: keys 0..63 in columns [0, 32), keys 64..127 in
-                    // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
-                    // Key half h accumulates into its own O_h, as soon as its four warps are done.
-                    const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
-                    for (int h = 0; h < 2 && ok; h++) {
-                        if (!mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (gg >> 1) & 1,
-                                               abort_flag)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        // V rows of K step kk: 16 keys x 128 B = 128 descriptor units from the tile start.
-                        const uint32_t oc = tmem + (h ? kColO1 : kColO0), pc = pcol + (uint32_t) (h * 64);
-                        const uint32_t lvb = lv + (uint32_t) buf * (kTile >> 4) + (uint32_t) (4 * h) * 128u;
-                        mma_f16_ts(oc, pc, hv | lvb, idesc_pv, j > 0 ? 1u : 0u);
-#pragma unroll
-                        for (int kq = 1; kq < 4; kq++) mma_f16_ts_k<1>(oc, pc + kq * 8, hv | (lvb + kq * 128u), idesc_pv);
-                    }
+                    ok = mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag);
+                    if (ok && gg >= 2)
+                        ok = mbar_wait_bounded(smem_u32(&bars->o_done[buf]), (uint32_t) ((gg - 2) >> 1) & 1,
+                                               abort_flag);
                     if (!ok) break;
-                    mma_commit(smem_u32(&bars->o_done));
-                    mma_commit(smem_u32(&bars->v_empty[buf]));
-                    if (j == n - 1) mma_commit(smem_u32(&bars->o_final));
-                    if (j + 2 < n && !issue_qk(gg + 2, j + 2 == n - 1)) {
-                        ok = false;
-                        break;
+                    tc_fence_after();
+                    const uint32_t d = tmem + (buf ? kColS1 : kColS0);
+                    const uint32_t lkb = lk + (uint32_t) buf * (kTile >> 4);
+                    mma_f16_ss_k<0>(d, hq | lq, hk | lkb, idesc_qk);
+#pragma unroll
+                    for (int kk = 1; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t) (((kk >> 2) * kSub + (kk & 3) * 32) >> 4);
+                        mma_f16_ss_k<1>(d, hq | (lq + off), hk | (lkb + off), idesc_qk);
                     }
+                    mma_commit(smem_u32(&bars->s_full[buf]));
+                    if (j == n - 1) mma_commit(smem_u32(&bars->q_empty));
+                    issued = true;
                 }
                 g += n;
                 n_items_t++;
@@ -583,10 +540,64 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 report(p.status, kStatusTimeout, kSitePrefillWait, kWarpMma);
                 *abort_flag = 1;
             }
-            // Every MMA issued so far completes before TMEM can be released.
+            // Every MMA this thread issued completes before TMEM can be released.
             if (issued) {
-                mma_commit(smem_u32(&bars->mma_drain));
-                mbar_wait_bounded(smem_u32(&bars->mma_drain), 0, nullptr);
+                mma_commit(smem_u32(&bars->mma_drain[0]));
+                mbar_wait_bounded(smem_u32(&bars->mma_drain[0]), 0, nullptr);
+            }
+        }
+    } else if (warp == kWarpMmaPv) {
+        // ---- PV issuer: O_h += P_gg V_gg for key half h, as soon as that half's four softmax
+        // warps have written P_gg; its commits (o_done, o_final) track only the PV MMAs. ----
+        if (lane == 0) {
+            constexpr uint32_t idesc_pv = idesc_f16(true);
+            const uint64_t dv0 = sdesc_sw128(sV, kSub, 1024);
+            const uint32_t lv = (uint32_t) dv0;
+            const uint64_t hv = dv0 & 0xFFFFFFFF00000000ull;
+            int g = 0, n_items_t = 0;
+            bool ok = true, issued = false;
+            for (int r = 0; ok; r++) {
+                const int x = item_index(p, r);
+                if (x < 0) break;
+                const int n = item_at(p, x).n_tiles;
+                if (n == 0) continue;
+                for (int j = 0; ok && j < n; j++) {
+                    const int gg = g + j;
+                    const int buf = gg & 1;
+                    ok = mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag);
+                    // The item's first PV overwrites O: the previous item's epilogue must have read it.
+                    if (ok && j == 0 && n_items_t > 0)
+                        ok = mbar_wait_bounded(smem_u32(&bars->o_free), (uint32_t) (n_items_t - 1) & 1, abort_flag);
+                    // P_gg sits in TMEM over S_gg: keys 0..63 in columns [0, 32), keys 64..127 in
+                    // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
+                    const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
+                    for (int h = 0; h < 2 && ok; h++) {
+                        ok = mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (gg >> 1) & 1,
+                                               abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        // V rows of K step kk: 16 keys x 128 B = 128 descriptor units from the tile start.
+                        const uint32_t oc = tmem + (h ? kColO1 : kColO0), pc = pcol + (uint32_t) (h * 64);
+                        const uint32_t lvb = lv + (uint32_t) buf * (kTile >> 4) + (uint32_t) (4 * h) * 128u;
+                        mma_f16_ts(oc, pc, hv | lvb, idesc_pv, j > 0 ? 1u : 0u);
+#pragma unroll
+                        for (int kq = 1; kq < 4; kq++) mma_f16_ts_k<1>(oc, pc + kq * 8, hv | (lvb + kq * 128u), idesc_pv);
+                        issued = true;
+                    }
+                    if (!ok) break;
+                    mma_commit(smem_u32(&bars->o_done[buf]));
+                    if (j == n - 1) mma_commit(smem_u32(&bars->o_final));
+                }
+                g += n;
+                n_items_t++;
+            }
+            if (!ok) {
+                report(p.status, kStatusTimeout, kSitePrefillWait, kWarpMmaPv);
+                *abort_flag = 1;
+            }
+            if (issued) {
+                mma_commit(smem_u32(&bars->mma_drain[1]));
+                mbar_wait_bounded(smem_u32(&bars->mma_drain[1]), 0, nullptr);
             }
         }
     } else {
@@ -660,8 +671,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 // A moved max rescales O_hf, which PV_{gg-1} must have finished updating (PV_{gg-2}
                 // has: S_gg ready implies it). P goes to buffer gg % 2, last read by PV_{gg-2}.
                 if (j > 0 && __any_sync(0xffffffffu, move)) {
-                    if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done),
-                                                                    (uint32_t) (gg - 1) & 1, abort_flag))) {
+                    if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done[(gg - 1) & 1]),
+                                                                    (uint32_t) ((gg - 1) >> 1) & 1, abort_flag))) {
                         ok = false;
                         break;
                     }
