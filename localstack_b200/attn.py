@@ -26,9 +26,21 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def _stream(stream=None):
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(stream=None, device=None):
+    """Stream handle to launch on: `stream`, else the current stream of `device` (the tensors'
+    device; the current device when None). The raw handle avoids building a torch Stream object,
+    which costs several microseconds per call."""
+    if stream is not None:
+        return ctypes.c_void_p(stream.cuda_stream)
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None:
+        idx = torch.cuda.current_device()
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(idx))
+    return ctypes.c_void_p(torch.cuda.current_stream(idx).cuda_stream)
 
 
 def layout_of(k_cache: torch.Tensor) -> KvLayout:
@@ -76,7 +88,7 @@ def kv_append(k_cache, v_cache, q, k, v, positions, cells, rope, q_gamma=None, k
     check(lib().lstk_cuda_kv_append(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _p(k), _p(v), _DT[q.dtype],
                                     q.stride(0), k.stride(0), v.stride(0), T, Hq, _p(positions), _p(cells),
                                     _p(q_gamma), _p(k_gamma), eps, _p(rope), rope.shape[0], _p(q_out),
-                                    _DT[q_out.dtype], _stream(stream)))
+                                    _DT[q_out.dtype], _stream(stream, k_cache.device)))
     return q_out
 
 
@@ -115,13 +127,14 @@ def attn_decode(k_cache, v_cache, q, block_tables, seq_lens, scale=None, max_seq
         check(lib().lstk_cuda_attn_decode(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B, Hq,
                                           _p(block_tables), block_tables.shape[1], _p(seq_lens), int(max_seq_len),
                                           float(scale), _p(out), _p(lse_out), _p(workspace.buf),
-                                          workspace.buf.numel(), int(n_ctas), _stream(stream)))
+                                          workspace.buf.numel(), int(n_ctas), _stream(stream, k_cache.device)))
     else:
         check(lib().lstk_cuda_attn_decode_partial(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B,
                                                   Hq, _p(block_tables), block_tables.shape[1], _p(seq_lens),
                                                   int(max_seq_len), int(kv_range[0]), int(kv_range[1]),
                                                   float(scale), _p(out), _p(lse_out), _p(workspace.buf),
-                                                  workspace.buf.numel(), int(n_ctas), _stream(stream)))
+                                                  workspace.buf.numel(), int(n_ctas),
+                                                  _stream(stream, k_cache.device)))
     return (out, lse_out) if want_lse else out
 
 
@@ -139,7 +152,7 @@ def attn_merge(o_parts, lse_parts, out=None, lse_out=None, stream=None):
     if lse_out is None:
         lse_out = torch.empty((rows,), dtype=torch.float32, device=o_parts.device)
     check(lib().lstk_cuda_attn_merge(_p(o_parts), _p(lse_parts), R, rows, D, o_parts.stride(0), lse_parts.stride(0),
-                                     _p(out), _p(lse_out), _stream(stream)))
+                                     _p(out), _p(lse_out), _stream(stream, o_parts.device)))
     return out, lse_out
 
 
@@ -166,14 +179,16 @@ def attn_prefill(k_cache, v_cache, q, q_seq_start, q_pos0, kv_lens, block_tables
         out = torch.empty((total, Hq, HEAD_DIM), dtype=torch.float32, device=q.device)
     elif out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < total * Hq * HEAD_DIM:
         raise ValueError("out must be a contiguous f32 tensor with total_tokens * Hq * 128 elements")
-    need = lib().lstk_cuda_attn_prefill_workspace_size(B, Hq, L.n_head_kv, HEAD_DIM, int(max_q_len),
-                                                       block_tables.shape[1], total, _DT[q.dtype])
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
+    if q.dtype == torch.float32:  # the f16 copy of q lives in the workspace; f16 queries need none
+        need = lib().lstk_cuda_attn_prefill_workspace_size(B, Hq, L.n_head_kv, HEAD_DIM, int(max_q_len),
+                                                           block_tables.shape[1], total, _DT[q.dtype])
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
     check(lib().lstk_cuda_attn_prefill(ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], B, Hq,
                                        _p(q_seq_start), int(max_q_len), total, _p(q_pos0), _p(kv_lens),
                                        _p(block_tables), block_tables.shape[1], float(scale), _p(out),
-                                       _p(workspace), workspace.numel(), _stream(stream)))
+                                       _p(workspace), workspace.numel() if workspace is not None else 0,
+                                       _stream(stream, k_cache.device)))
     return out
 
 

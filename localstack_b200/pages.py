@@ -70,7 +70,7 @@ class DevicePages:
         if cells.numel() < max_tokens or positions.numel() < max_tokens or ok.numel() < n:
             raise ValueError("output tensors are shorter than max_tokens / the slot count")
         check(lib().lstk_cuda_kv_alloc(ctypes.byref(self.state), _p(slots), _p(counts), n, int(max_tokens), _p(cells),
-                                       _p(positions), _p(ok), _stream(stream)))
+                                       _p(positions), _p(ok), _stream(stream, self.device)))
         return cells, positions, ok
 
     def alloc_step(self, slots, cells=None, positions=None, ok=None, stream=None):
@@ -79,7 +79,8 @@ class DevicePages:
 
     def release(self, slot, keep=0, stream=None):
         """KvCache::truncate_seq(slot, keep) for keep > 0, remove_seq(slot) otherwise."""
-        check(lib().lstk_cuda_kv_release(ctypes.byref(self.state), int(slot), int(keep), _stream(stream)))
+        check(lib().lstk_cuda_kv_release(ctypes.byref(self.state), int(slot), int(keep),
+                                         _stream(stream, self.device)))
 
     def free_list(self):
         """The free stack bottom first (KvCache::free_blocks order)."""

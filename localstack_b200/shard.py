@@ -147,7 +147,7 @@ class KvSplitDecode:
         if self.exchange == "p2p":
             check(lib().lstk_cuda_attn_exchange_merge(_p(self.mailboxes), self.rank, self.world, _p(o_loc[0]),
                                                       _p(lse_loc[0]), self.rows, HEAD_DIM, self.wait_ns,
-                                                      _p(self.out), _p(self.lse), _stream()))
+                                                      _p(self.out), _p(self.lse), _stream(None, q.device)))
             return self.out
         all_gather_records(self.gathered, self.local, self.group)
         o_parts, lse_parts = record_views(self.gathered, self.rows)
