@@ -62,6 +62,22 @@ const char *lstk_cuda_last_error(void);
  * LSTK_ERR_DEVICE_INDEX or LSTK_ERR_CUDA. Status is per device and sticky until read. */
 int lstk_cuda_status(void *stream);
 
+/* ---- Bounded waits ----------------------------------------------------------------------------
+ * (no counterpart in the reference, whose ggml ops never wait on other work). Every wait inside
+ * the decode and prefill kernels is bounded: when one runs out, the kernel records LSTK_ERR_TIMEOUT
+ * in the device status, lets its in-flight copies and tensor-core work finish, frees its tensor
+ * memory and returns, so the context stays usable. This sets, for later decode / prefill launches
+ * from the calling host thread (lstk_cuda_attn_decode, _decode_partial, _decode_static,
+ * _prefill):
+ *   pipeline_wait_ns  limit of each wait between the kernels' own warps (0 = the default, 4 s);
+ *                     the waits that drain in-flight work before a kernel exits keep 4 s;
+ *   start_flag        optional device int32: the kernels' loaders wait (bounded by
+ *                     pipeline_wait_ns) until it is non-zero before their first load, to hold a
+ *                     launched kernel until a producer outside its stream (another process or GPU
+ *                     writing the pages) has published its inputs; NULL = no gate.
+ * A CUDA graph captures the policy in force when it is captured. */
+int lstk_cuda_set_wait_policy(uint64_t pipeline_wait_ns, const int32_t *start_flag);
+
 /* ---- RoPE table -----------------------------------------------------------------------------
  * ggml builds the NEOX rotation per step (ggml_rope_cache_init for each position); the backend
  * reads the same values from a persistent table instead. Entry [p][i] = (cosf(t), sinf(t)) with
@@ -199,7 +215,8 @@ int lstk_cuda_kv_release(const lstk_kv_pages *state, int32_t slot, int32_t keep,
  * lse_out, natural log, optional). Set-up per rank: lstk_cuda_mailbox_alloc (on the current
  * device; zeroed; 64-byte IPC handle out), share the handles through any host channel,
  * lstk_cuda_mailbox_open each peer's, and place the R pointers (own at [rank]) in a device
- * array `mailboxes`. Every rank must make the same sequence of calls with the same n_rows; the
+ * array `mailboxes`. At most 128 ranks (LSTK_ERR_UNSUPPORTED beyond). Every rank must make the
+ * same sequence of calls with the same n_rows; the
  * calls advance an epoch kept in the mailbox, so they can be replayed from a CUDA graph. */
 size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim);
 int lstk_cuda_mailbox_alloc(size_t bytes, void **mailbox, void *ipc_handle);

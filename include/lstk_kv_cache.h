@@ -4,8 +4,8 @@
  * device kernels consume: per-sequence block tables.
  *
  * In a drop-in deployment the reference keeps its own KvCache unchanged and only converts
- * KvCache::seq_blocks / seq_len into the int32 tables of lstk_kv_cache_block_tables' format
- * (see INTEGRATION.md). This C ABI lets the backend run standalone with identical bookkeeping.
+ * KvCache::seq_blocks / seq_len into the int32 tables of lstk_kv_cache_block_tables' format.
+ * This C ABI lets the backend run standalone with identical bookkeeping.
  * Not thread-safe, like the reference's Engine (src/engine.h:65).
  */
 #ifndef LSTK_KV_CACHE_H

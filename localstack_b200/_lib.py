@@ -90,6 +90,7 @@ def lib():
     L.lstk_rope_table_bytes.argtypes = [_I32, _I32]
     L.lstk_rope_table_bytes.restype = _SZ
     L.lstk_rope_table_fill.argtypes = [_P, _I32, _I32, _F, _F]
+    L.lstk_cuda_set_wait_policy.argtypes = [ctypes.c_uint64, _P]
     L.lstk_cuda_kv_append.argtypes = [_LP, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I64, _I32, _I32, _P, _P, _P, _P,
                                       _F, _P, _I32, _P, _I32, _P]
     L.lstk_cuda_attn_decode_workspace_size.argtypes = [_I32, _I32, _I32, _I32]

@@ -31,10 +31,12 @@ enum : int {
     kSiteDecodeLen = 11,
     kSiteDecodeWaitFull = 12,
     kSiteDecodeWaitEmpty = 13,
+    kSiteDecodeWaitStart = 14,
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
     kSitePrefillSmem = 22,
     kSitePrefillRows = 23,
+    kSitePrefillWaitStart = 24,
     kSiteExchangeWait = 30,
     kSitePagesSlot = 40,
     kSitePagesTokens = 41,
@@ -47,7 +49,9 @@ __device__ __forceinline__ void report(DeviceStatus *st, int code, int where, in
     }
 }
 
-// Upper bound for any single wait inside a kernel. Normal waits last microseconds.
+// Upper bound for any single wait inside a kernel. Normal waits last microseconds. The pipeline
+// waits of the attention kernels take their limit from the launch (default this value); the drain
+// waits before a kernel exits always use this one, so no CTA leaves with copies in flight.
 constexpr uint64_t kWaitLimitNs = 4ull * 1000 * 1000 * 1000;
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -96,15 +100,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for phase `parity` of the barrier. Gives up (returns false) when *abort becomes
-// non-zero or after kWaitLimitNs; the caller records the timeout and unwinds.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const volatile int *abort) {
+// non-zero or after limit_ns; the caller records the timeout and unwinds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const volatile int *abort,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1; i < (1u << 30); i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (abort != nullptr && *abort) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+            if (global_timer_ns() - t0 > limit_ns) return false;
+        }
+    }
+    return false;
+}
+
+__device__ __forceinline__ int32_t ld_acquire_sys_s32(const int32_t *p) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag != 0 (published by work outside this kernel's stream: another stream, process
+// or GPU), bounded like mbar_wait_bounded. Returns false on abort or when limit_ns runs out.
+__device__ __forceinline__ bool flag_wait_bounded(const int32_t *flag, const volatile int *abort, uint64_t limit_ns) {
+    if (ld_acquire_sys_s32(flag) != 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1; i < (1u << 30); i++) {
+        if (ld_acquire_sys_s32(flag) != 0) return true;
+        if ((i & 63u) == 0) {
+            if (abort != nullptr && *abort) return false;
+            if (global_timer_ns() - t0 > limit_ns) return false;
         }
     }
     return false;

@@ -61,6 +61,8 @@ struct Params {
     float *part_lse;  // [kMaxCtas][2][kPartRows], log2 units
     int32_t *prefix;  // [n_seqs + 1] pages before each sequence
     DeviceStatus *status;
+    uint64_t wait_ns;           // limit of each pipeline wait (drains keep kWaitLimitNs)
+    const int32_t *start_flag;  // optional: the producer waits for it to be non-zero before loading
 };
 
 __host__ __device__ inline int64_t range_lo(int c, int64_t P, int G) { return ((int64_t) c * P) / G; }
@@ -319,10 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             cur.locate(lo, pfx, p.n_seqs, p.n_hg);
             int64_t i = 0;
             bool ok = true;
-            for (int64_t x = lo; x < hi; x++, i++) {
+            if (p.start_flag != nullptr && !flag_wait_bounded(p.start_flag, abort_flag, p.wait_ns)) {
+                report(p.status, kStatusTimeout, kSiteDecodeWaitStart, blockIdx.x);
+                *abort_flag = 1;
+                ok = false;
+            }
+            for (int64_t x = lo; ok && x < hi; x++, i++) {
                 const int s = (int) (i % kStages);
                 const uint32_t k_use = (uint32_t) (i / kStages);
-                if (k_use > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag)) {
+                if (k_use > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag, p.wait_ns)) {
                     report(p.status, kStatusTimeout, kSiteDecodeWaitEmpty, s);
                     *abort_flag = 1;
                     ok = false;
@@ -375,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             const int s = (int) (i % kStages);
             // Warp-uniform outcome: ldmatrix / mma.sync below are warp-collective.
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full[s]), (uint32_t) (i / kStages) & 1,
-                                                             abort_flag))) {
+                                                             abort_flag, p.wait_ns))) {
                 if (lane == 0) {
                     report(p.status, kStatusTimeout, kSiteDecodeWaitFull, s);
                     *abort_flag = 1;

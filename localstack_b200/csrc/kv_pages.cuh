@@ -161,7 +161,10 @@ __global__ void __launch_bounds__(kThreads) alloc_kernel(State st, const int32_t
     int hwm = 0;
     for (int i = warp; i < n; i += kThreads / 32) {
         const int s = slots[i];
-        const int c = counts ? counts[i] : 1;
+        const int c_raw = counts ? counts[i] : 1;
+        // An invalid item (slot out of range, negative count) reserved no output entries in the
+        // token scan above, so it writes none: its s_tok is the next item's start.
+        const int c = (s >= 0 && s < st.n_slots && c_raw >= 0) ? c_raw : 0;
         const bool got = s_pop[i] >= 0;
         const int l0 = s_len[i];
         const int64_t t0 = s_tok[i];

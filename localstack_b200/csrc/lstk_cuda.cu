@@ -30,14 +30,20 @@ struct DeviceInfo {
     bool ready = false;
     int n_sms = 0;
     DeviceStatus *status = nullptr;
+    // Dynamic shared-memory limits raised so far on this device, per kernel (ensure_smem).
     size_t decode_smem = 0;
-    bool prefill_attr = false;
-    bool append_smem_set = false;
+    size_t prefill_smem = 0;
+    size_t append_smem = 0;
 };
 
 DeviceInfo g_devices[kMaxDevices];
 std::mutex g_devices_mu;
 thread_local int t_last_device = -1;
+
+// Bounded-wait policy for the decode and prefill launches of this host thread
+// (lstk_cuda_set_wait_policy).
+thread_local uint64_t t_pipeline_wait_ns = kWaitLimitNs;
+thread_local const int32_t *t_start_flag = nullptr;
 
 std::string cuda_msg(const char *what, cudaError_t e) {
     return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
@@ -70,6 +76,19 @@ int bind_device(const void *ptr, DeviceInfo **info) {
     }
     t_last_device = dev;
     *info = &d;
+    return LSTK_OK;
+}
+
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at least `bytes`, once
+// per device (`*have` is the DeviceInfo field that records it). Serialised with the other
+// first-use set-up, so host threads making their first calls on a device at once do not race.
+template <typename Kernel>
+int ensure_smem(size_t *have, Kernel kernel, size_t bytes, const char *what) {
+    std::lock_guard<std::mutex> lock(g_devices_mu);
+    if (*have >= bytes) return LSTK_OK;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) bytes);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg(what, e));
+    *have = bytes;
     return LSTK_OK;
 }
 
@@ -173,6 +192,14 @@ int lstk_cuda_status(void *stream) {
     return set_error(st.code == kStatusTimeout ? LSTK_ERR_TIMEOUT : LSTK_ERR_DEVICE_INDEX, buf);
 }
 
+int lstk_cuda_set_wait_policy(uint64_t pipeline_wait_ns, const int32_t *start_flag) {
+    if (start_flag != nullptr && !aligned(start_flag, 4))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_set_wait_policy: start_flag must be 4-byte aligned");
+    t_pipeline_wait_ns = pipeline_wait_ns ? pipeline_wait_ns : kWaitLimitNs;
+    t_start_flag = start_flag;
+    return clear_error();
+}
+
 int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
                         const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
                         int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
@@ -240,12 +267,9 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    if (!dev->append_smem_set) {
-        const cudaError_t e = cudaFuncSetAttribute(append::kv_append_kernel,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, append::kSmemBytes);
-        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(kv_append)", e));
-        dev->append_smem_set = true;
-    }
+    if ((rc = ensure_smem(&dev->append_smem, append::kv_append_kernel, append::kSmemBytes,
+                          "cudaFuncSetAttribute(kv_append)")))
+        return rc;
     cfg.gridDim = dim3((unsigned) blocks);
     cfg.blockDim = dim3(append::kWarps * 32);
     cfg.dynamicSmemBytes = append::kSmemBytes;
@@ -364,15 +388,13 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
     p.part_lse = reinterpret_cast<float *>(ws + decode_ws_prefix_bytes(n_seqs));
     p.part_o = reinterpret_cast<float *>(ws + decode_ws_prefix_bytes(n_seqs) + kDecodePartLseBytes);
     p.status = dev->status;
+    p.wait_ns = t_pipeline_wait_ns;
+    p.start_flag = t_start_flag;
 
     const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
                         16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
-    if (dev->decode_smem < smem) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(decode::decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
-        dev->decode_smem = smem;
-    }
+    if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel, smem, "cudaFuncSetAttribute(decode)")))
+        return rc;
     return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
 }
 
@@ -493,17 +515,16 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
     p.status = dev->status;
+    p.wait_ns = t_pipeline_wait_ns;
+    p.start_flag = t_start_flag;
     const int64_t n_items = (int64_t) n_seqs * p.n_qt * hkv;
     if (n_items > (int64_t) INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill: too many tiles");
     p.n_items = (int) n_items;
     // Persistent: one CTA per SM walks its share of the items (snake order over heaviest-first).
     const int64_t grid = std::min<int64_t>(n_items, dev->n_sms);
-    if (!dev->prefill_attr) {
-        const cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   prefill::kSmemBytes);
-        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(prefill)", e));
-        dev->prefill_attr = true;
-    }
+    if ((rc = ensure_smem(&dev->prefill_smem, prefill::prefill_kernel, prefill::kSmemBytes,
+                          "cudaFuncSetAttribute(prefill)")))
+        return rc;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -604,6 +625,9 @@ int lstk_cuda_attn_exchange_merge(void *const *mailboxes, int32_t rank, int32_t 
     if (!mailboxes || !local_o || !local_lse || !out || n_ranks <= 0 || rank < 0 || rank >= n_ranks || n_rows < 0)
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_exchange_merge: bad arguments");
     if (head_dim != exchange::kD) return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_exchange_merge: head_dim must be 128");
+    // One thread per source raises and awaits its flag.
+    if (n_ranks > exchange::kThreads)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_exchange_merge: at most 128 ranks");
     if (n_rows == 0) return clear_error();
     DeviceInfo *dev = nullptr;
     int rc = bind_device(local_o, &dev);
@@ -702,15 +726,20 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     if ((rc = bind_device(k_cache, &dev))) return rc;
 
     // First call on this device (which bind_device made current): resolve the array's device
-    // address once.
+    // address once, under the same lock as the rest of the first-use set-up, so host threads
+    // making their first calls on one device at once do not race on the cached pointer.
     const int dev_id = t_last_device;
-    if (g_decode_scratch_ptr[dev_id] == nullptr) {
-        void *addr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&addr, g_decode_scratch);
-        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaGetSymbolAddress(decode scratch)", e));
-        g_decode_scratch_ptr[dev_id] = static_cast<uint8_t *>(addr);
+    uint8_t *ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_devices_mu);
+        if (g_decode_scratch_ptr[dev_id] == nullptr) {
+            void *addr = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+            if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaGetSymbolAddress(decode scratch)", e));
+            g_decode_scratch_ptr[dev_id] = static_cast<uint8_t *>(addr);
+        }
+        ws = g_decode_scratch_ptr[dev_id];
     }
-    uint8_t *ws = g_decode_scratch_ptr[dev_id];
 
     CUtensorMap kmap, vmap;
     if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
@@ -742,15 +771,13 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     p.part_lse = reinterpret_cast<float *>(ws + kStaticPrefixBytes);
     p.part_o = reinterpret_cast<float *>(ws + kStaticPrefixBytes + kStaticLseBytes);
     p.status = dev->status;
+    p.wait_ns = t_pipeline_wait_ns;
+    p.start_flag = t_start_flag;
 
     const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
                         16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
-    if (dev->decode_smem < smem) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(decode::decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaFuncSetAttribute(decode)", e));
-        dev->decode_smem = smem;
-    }
+    if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel, smem, "cudaFuncSetAttribute(decode)")))
+        return rc;
     return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
 }
 

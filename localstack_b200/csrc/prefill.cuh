@@ -99,6 +99,8 @@ struct Params {
     float scale_log2;
     float *out;
     DeviceStatus *status;
+    uint64_t wait_ns;           // limit of each pipeline wait (drains keep kWaitLimitNs)
+    const int32_t *start_flag;  // optional: the producers wait for it to be non-zero before loading
 };
 
 struct Barriers {
@@ -417,6 +419,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const CUtensorMap *map = is_k ? &kmap : &vmap;
         int g = 0, n_items_t = 0;
         bool ok = true;
+        if (p.start_flag != nullptr) {
+            if (lane == 0 && !(ok = flag_wait_bounded(p.start_flag, abort_flag, p.wait_ns))) {
+                report(p.status, kStatusTimeout, kSitePrefillWaitStart, warp);
+                *abort_flag = 1;
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
         for (int r = 0; ok; r++) {
             const int x = item_index(p, r);
             if (x < 0) break;
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (I.n_tiles == 0) continue;
             if (is_k && lane == 0) {
                 if (n_items_t > 0)
-                    ok = mbar_wait_bounded(smem_u32(&bars->q_empty), (uint32_t) (n_items_t - 1) & 1, abort_flag);
+                    ok = mbar_wait_bounded(smem_u32(&bars->q_empty), (uint32_t) (n_items_t - 1) & 1, abort_flag, p.wait_ns);
                 if (ok) {
                     mbar_arrive_expect_tx(smem_u32(&bars->q_full), kTile);
                     for (int h = 0; h < 2; h++)
@@ -462,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     const uint32_t use = (uint32_t) (g >> 1);
                     const uint32_t empty = smem_u32(is_k ? &bars->s_full[buf] : &bars->o_done[buf]);
                     const uint32_t full = smem_u32(is_k ? &bars->k_full[buf] : &bars->v_full[buf]);
-                    if (use > 0) ok = mbar_wait_bounded(empty, (use - 1) & 1, abort_flag);
+                    if (use > 0) ok = mbar_wait_bounded(empty, (use - 1) & 1, abort_flag, p.wait_ns);
                     if (ok) {
                         mbar_arrive_expect_tx(full, kTile);
                         for (int q = 0; q < 4; q++)
@@ -511,14 +520,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 if (x < 0) break;
                 const int n = item_at(p, x).n_tiles;
                 if (n == 0) continue;
-                ok = mbar_wait_bounded(smem_u32(&bars->q_full), (uint32_t) n_items_t & 1, abort_flag);
+                ok = mbar_wait_bounded(smem_u32(&bars->q_full), (uint32_t) n_items_t & 1, abort_flag, p.wait_ns);
                 for (int j = 0; ok && j < n; j++) {
                     const int gg = g + j;
                     const int buf = gg & 1;
-                    ok = mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag);
+                    ok = mbar_wait_bounded(smem_u32(&bars->k_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag, p.wait_ns);
                     if (ok && gg >= 2)
                         ok = mbar_wait_bounded(smem_u32(&bars->o_done[buf]), (uint32_t) ((gg - 2) >> 1) & 1,
-                                               abort_flag);
+                                               abort_flag, p.wait_ns);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t d = tmem + (buf ? kColS1 : kColS0);
@@ -564,16 +573,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 for (int j = 0; ok && j < n; j++) {
                     const int gg = g + j;
                     const int buf = gg & 1;
-                    ok = mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag);
+                    ok = mbar_wait_bounded(smem_u32(&bars->v_full[buf]), (uint32_t) (gg >> 1) & 1, abort_flag, p.wait_ns);
                     // The item's first PV overwrites O: the previous item's epilogue must have read it.
                     if (ok && j == 0 && n_items_t > 0)
-                        ok = mbar_wait_bounded(smem_u32(&bars->o_free), (uint32_t) (n_items_t - 1) & 1, abort_flag);
+                        ok = mbar_wait_bounded(smem_u32(&bars->o_free), (uint32_t) (n_items_t - 1) & 1, abort_flag, p.wait_ns);
                     // P_gg sits in TMEM over S_gg: keys 0..63 in columns [0, 32), keys 64..127 in
                     // [64, 96) of the S buffer, two f16 per 32-bit column (16 keys per MMA step).
                     const uint32_t pcol = tmem + (buf ? kColS1 : kColS0);
                     for (int h = 0; h < 2 && ok; h++) {
                         ok = mbar_wait_bounded(smem_u32(&bars->p_full[h][buf]), (uint32_t) (gg >> 1) & 1,
-                                               abort_flag);
+                                               abort_flag, p.wait_ns);
                         if (!ok) break;
                         tc_fence_after();
                         // V rows of K step kk: 16 keys x 128 B = 128 descriptor units from the tile start.
@@ -632,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const int buf = gg & 1;
                 // Warp-uniform outcomes: tcgen05.ld / st below are warp-collective.
                 if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->s_full[buf]),
-                                                                (uint32_t) (gg >> 1) & 1, abort_flag))) {
+                                                                (uint32_t) (gg >> 1) & 1, abort_flag, p.wait_ns))) {
                     ok = false;
                     break;
                 }
@@ -672,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 // has: S_gg ready implies it). P goes to buffer gg % 2, last read by PV_{gg-2}.
                 if (j > 0 && __any_sync(0xffffffffu, move)) {
                     if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_done[(gg - 1) & 1]),
-                                                                    (uint32_t) ((gg - 1) >> 1) & 1, abort_flag))) {
+                                                                    (uint32_t) ((gg - 1) >> 1) & 1, abort_flag, p.wait_ns))) {
                         ok = false;
                         break;
                     }
@@ -707,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (n_tiles > 0) {
                 if (ok)
                     ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->o_final),
-                                                                    (uint32_t) n_items_t & 1, abort_flag));
+                                                                    (uint32_t) n_items_t & 1, abort_flag, p.wait_ns));
                 // The halves swap (m, l) per row and merge O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) /
                 // (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)); warp w writes output columns 64*(w/4) .. +63.
                 bars->row_m[hf][r] = m;

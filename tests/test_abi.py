@@ -190,3 +190,11 @@ def test_python_wrappers_validate_before_launch():
         L.attn_decode(kc, kc, q[:1], bt.long(), i32(4))
     with pytest.raises(ValueError):  # strided block tables
         L.attn_decode(kc, kc, q[:1], torch.zeros(1, 4, dtype=torch.int32)[:, ::2], i32(4))
+
+
+def test_wait_policy_validation_without_gpu():
+    lib = L.lib()
+    assert lib.lstk_cuda_set_wait_policy(0, ctypes.c_void_p(0x10002)) == _lib.LSTK_ERR_INVALID_ARG
+    assert "aligned" in _lib.last_error()
+    assert lib.lstk_cuda_set_wait_policy(1000, ctypes.c_void_p(0x10000)) == _lib.LSTK_OK
+    assert lib.lstk_cuda_set_wait_policy(0, None) == _lib.LSTK_OK  # back to the default: 4 s, no gate

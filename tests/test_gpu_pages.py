@@ -96,6 +96,31 @@ def test_failed_request_takes_nothing_and_later_ones_fit():
     assert torch.equal(dp.block_tables, before[2])
 
 
+def test_invalid_items_write_no_outputs():
+    """Items with an out-of-range slot or a negative count reserve no output entries and write
+    none: the valid slots after them keep their cells and positions, the entries past the valid
+    tokens stay untouched, and the device status reports the bad item."""
+    kv = KvCache(1024)
+    dp = DevicePages(1024, 4, 32)
+    dev = "cuda"
+    for slots_l, counts_l in (([7, 1, -3, 2], [5, 3, 4, 2]), ([0, 1, 3], [-2, 40, 1])):
+        slots = torch.tensor(slots_l, dtype=torch.int32, device=dev)
+        counts = torch.tensor(counts_l, dtype=torch.int32, device=dev)
+        cells = torch.full((64,), -7, dtype=torch.int64, device=dev)
+        pos = torch.full((64,), -7, dtype=torch.int32, device=dev)
+        _, _, ok = dp.alloc(slots, counts, 64, cells=cells, positions=pos)
+        with pytest.raises(L.LstkError) as e:
+            L.check_status()
+        assert e.value.code == -6  # LSTK_ERR_DEVICE_INDEX
+        valid = [(s, c) for s, c in zip(slots_l, counts_l) if 0 <= s < 4 and c >= 0]
+        want_c, want_p, _ = _host_alloc(kv, [s for s, _ in valid], [c for _, c in valid])
+        n = want_c.size
+        assert ok.cpu().tolist() == [1 if (0 <= s < 4 and c >= 0) else 0 for s, c in zip(slots_l, counts_l)]
+        assert np.array_equal(cells[:n].cpu().numpy(), want_c) and np.array_equal(pos[:n].cpu().numpy(), want_p)
+        assert bool((cells[n:] == -7).all()) and bool((pos[n:] == -7).all())
+        _compare(kv, dp, 4, 32, "invalid items")
+
+
 def test_full_cache_and_full_table():
     # 4 blocks for 3 slots of at most 2 blocks: the stack runs empty mid-step; a full table row fails
     kv = KvCache(128)

@@ -13,7 +13,8 @@ import torch
 
 import localstack_b200 as L
 from localstack_b200 import _lib
-from tests.helpers import random_cache, random_q, scattered_block_tables, within
+from oracle import oracle as O
+from tests.helpers import max_err, random_cache, random_q, scattered_block_tables, within
 
 pytestmark = pytest.mark.gpu
 SCALE = 1.0 / math.sqrt(128)
@@ -61,6 +62,34 @@ def test_static_scratch_decode_matches_workspace_decode_twice():
         fin = np.isfinite(b)
         assert np.array_equal(np.isfinite(a), fin) and np.all(a[~fin] == b[~fin])  # empty sequence: -inf
         assert within(a[fin], b[fin], atol=1e-4, rtol=1e-5)
+
+
+def test_static_scratch_at_its_limits_against_the_oracle():
+    """The fixed array's two limits at once - 1024 sequences (mixed short lengths, some empty) on a
+    160-CTA split - twice in a row with different data: against the CPU oracle directly, and bit
+    for bit against the workspace entry point on the same grid."""
+    fn = _static_fn()
+    for seed, (Hq, Hkv) in ((41, (32, 4)), (42, (16, 8))):
+        rng = np.random.default_rng(seed)
+        lens = rng.integers(0, 400, 1024)
+        lens[rng.choice(1024, 40, replace=False)] = 0
+        lens = lens.tolist()
+        kc, vc, q, bt, lens_t = _case(seed, lens, Hq, Hkv)
+        out = torch.empty((1024, Hq, 128), device="cuda")
+        lse = torch.empty((1024, Hq), device="cuda")
+        assert _call_static(fn, kc, vc, q, bt, lens_t, out, lse, n_ctas=160) == _lib.LSTK_OK, _lib.last_error()
+        ref, ref_lse = L.attn_decode(kc, vc, q, bt, lens_t, SCALE, want_lse=True, n_ctas=160)
+        L.check_status()
+        assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+        lens_np = np.asarray(lens, np.int32)
+        kh = kc.cpu().view(torch.int16).numpy().view(np.uint16)
+        vh = vc.cpu().view(torch.int16).numpy().view(np.uint16)
+        ex = O.paged_attn(q.cpu().numpy(), np.arange(1024), np.maximum(lens_np - 1, 0), kh, vh, bt.cpu().numpy(),
+                          lens_np, SCALE, mode=O.MODE_EXACT)
+        got = out.cpu().numpy()
+        empty = lens_np == 0
+        assert np.all(got[empty] == 0)
+        assert within(got[~empty], ex[~empty]), max_err(got[~empty], ex[~empty])
 
 
 def test_static_scratch_rejects_oversized_requests():
