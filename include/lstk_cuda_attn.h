@@ -253,6 +253,25 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
                            const int32_t *block_tables, int32_t max_blocks_per_seq, float scale, float *out,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- Projections: replace attn_block's mul_mat nodes and the input RMSNorm ------------------
+ * (src/qwen3.cpp:117-120 proj(), called at :135-138 for Wq / Wk / Wv and at :169 for Wo; the
+ * residual add of :170; rms(x, attn_norm) of :112-114 / :134).
+ * lstk_cuda_proj: out[m][n] = sum_k x[m][k] * w[n][k] (+ residual[m][n]) on the tcgen05 tensor
+ *   cores. x [m][ldx] bf16 activations; w [n][ldw] bf16, a weight in ggml's mul_mat layout (ne0 = k
+ *   contiguous, one output row per row of w: a fused Wq|Wk|Wv is the three weights stacked);
+ *   residual optional [m][ldr] bf16; out [m][ldo] bf16 or f32 (out_dtype). f32 accumulation; the
+ *   residual is added in f32 and the sum rounded once. Row strides are whole 16-byte units and
+ *   pointers 16-byte aligned; k > 0. out must not overlap x or w (it may be the residual itself).
+ * lstk_cuda_rms_norm: y[r][:] = x[r][:] / sqrt(mean(x[r][:]^2) + eps) * gamma (gamma NULL = 1),
+ *   x bf16 or f32, y bf16; f32 sums. cols a multiple of 8 (bf16) or 4 (f32).
+ * lstk_cuda_to_bf16: y = bf16(x) for a [rows][cols] f32 block (the f32 attention output entering the
+ *   bf16 Wo projection). */
+int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                   const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *stream);
+int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,
+                       int64_t ldy, int32_t rows, int32_t cols, void *stream);
+int lstk_cuda_to_bf16(const float *x, int64_t ldx, void *y, int64_t ldy, int32_t rows, int32_t cols, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,3 +17,4 @@ from .attn import (  # noqa: F401
     rope_table_host,
 )
 from .pages import DevicePages  # noqa: F401,E402
+from .proj import proj, rms_norm, to_bf16  # noqa: F401,E402

@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "exchange.cuh"
+#include "gemm.cuh"
 #include "host_util.h"
 #include "kv_append.cuh"
 #include "kv_pages.cuh"
@@ -34,6 +35,7 @@ struct DeviceInfo {
     size_t decode_smem = 0;
     size_t prefill_smem = 0;
     size_t append_smem = 0;
+    size_t gemm_smem = 0;
 };
 
 DeviceInfo g_devices[kMaxDevices];
@@ -123,6 +125,22 @@ static int encode_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dty
     const CUresult r = fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
+    return LSTK_OK;
+}
+
+// 2-D bf16 map over [rows][ld] (k contiguous, `cols` of each row in the tensor) with a
+// (64, box_rows) box and the 128-byte swizzle; out-of-range boxes fill zeros.
+int encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
     return LSTK_OK;
 }
@@ -655,6 +673,109 @@ int lstk_cuda_attn_exchange_merge(void *const *mailboxes, int32_t rank, int32_t 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return launch_pdl_check(cudaLaunchKernelEx(&cfg, exchange::exchange_merge_kernel, p), "exchange_merge_kernel");
+}
+
+// ---- projections (tcgen05 GEMM) and the row kernels around them --------------------------------
+
+static int launch_pdl(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStream_t s) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return LSTK_OK;
+}
+
+int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                   const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *stream) {
+    if (m < 0 || n < 0 || k <= 0) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: bad sizes (k must be > 0)");
+    if (out_dtype != LSTK_DTYPE_BF16 && out_dtype != LSTK_DTYPE_F32)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_proj: out_dtype must be bf16 or f32");
+    if (!x || !w || !out) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: NULL pointer");
+    const int64_t oe = out_dtype == LSTK_DTYPE_F32 ? 4 : 2;
+    if (ldx < k || ldw < k || ldo < n || (residual && ldr < n))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: leading dimension smaller than the row");
+    if (ldx % 8 || ldw % 8 || (ldo * oe) % 16 || (residual && ldr % 8))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: row strides must be multiples of 16 bytes");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || (residual && !aligned(residual, 16)))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: pointers must be 16-byte aligned");
+    if (m == 0 || n == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(out, &dev);
+    if (rc) return rc;
+    CUtensorMap amap, bmap;
+    if ((rc = encode_bf16_2d(&amap, x, (uint64_t) k, (uint64_t) m, (uint64_t) ldx, gemm::kBM))) return rc;
+    if ((rc = encode_bf16_2d(&bmap, w, (uint64_t) k, (uint64_t) n, (uint64_t) ldw, gemm::kBN))) return rc;
+    gemm::Params p;
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.m_tiles = (m + gemm::kBM - 1) / gemm::kBM;
+    p.n_tiles = (n + gemm::kBN - 1) / gemm::kBN;
+    p.k_blocks = (k + gemm::kBK - 1) / gemm::kBK;
+    const int64_t n_work = (int64_t) p.m_tiles * p.n_tiles;
+    if (n_work > INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_proj: too many tiles");
+    p.n_work = (int) n_work;
+    p.out = out;
+    p.ldo = ldo;
+    p.out_f32 = out_dtype == LSTK_DTYPE_F32;
+    p.res = static_cast<const __nv_bfloat16 *>(residual);
+    p.ldr = ldr;
+    p.status = dev->status;
+    p.wait_ns = t_pipeline_wait_ns;
+    if ((rc = ensure_smem(&dev->gemm_smem, gemm::gemm_kernel, gemm::kSmemBytes, "cudaFuncSetAttribute(gemm)")))
+        return rc;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) std::min<int64_t>(n_work, dev->n_sms));
+    cfg.blockDim = dim3(gemm::kThreads);
+    cfg.dynamicSmemBytes = gemm::kSmemBytes;
+    launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, p), "gemm_kernel");
+}
+
+int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,
+                       int64_t ldy, int32_t rows, int32_t cols, void *stream) {
+    if (rows < 0 || cols <= 0 || !x || !y) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_rms_norm: bad arguments");
+    if (x_dtype != LSTK_DTYPE_BF16 && x_dtype != LSTK_DTYPE_F32)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_rms_norm: x_dtype must be bf16 or f32");
+    const int vec = x_dtype == LSTK_DTYPE_BF16 ? 8 : 4;
+    if (cols % vec || ldx < cols || ldy < cols || ldx % vec || ldy % 8 || !aligned(x, 16) || !aligned(y, 16) ||
+        (gamma && !aligned(gamma, 16)))
+        return set_error(LSTK_ERR_INVALID_ARG,
+                         "lstk_cuda_rms_norm: rows must be whole 16-byte vectors (cols and strides) and 16-byte aligned");
+    if (rows == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(y, &dev);
+    if (rc) return rc;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) ((rows + 7) / 8));
+    cfg.blockDim = dim3(256);
+    launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::rms_norm_kernel, x, (int) (x_dtype == LSTK_DTYPE_F32), ldx,
+                                               gamma, eps, static_cast<__nv_bfloat16 *>(y), ldy, (int) rows, (int) cols),
+                            "rms_norm_kernel");
+}
+
+int lstk_cuda_to_bf16(const float *x, int64_t ldx, void *y, int64_t ldy, int32_t rows, int32_t cols, void *stream) {
+    if (rows < 0 || cols < 0 || !x || !y) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_to_bf16: bad arguments");
+    if (cols % 4 || ldx < cols || ldy < cols || ldx % 4 || ldy % 4 || !aligned(x, 16) || !aligned(y, 8))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_to_bf16: cols and strides must be multiples of 4, x 16-byte "
+                                               "and y 8-byte aligned");
+    if (rows == 0 || cols == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(y, &dev);
+    if (rc) return rc;
+    const int64_t total = (int64_t) rows * (cols / 4);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) std::min<int64_t>((total + 255) / 256, (int64_t) dev->n_sms * 8));
+    cfg.blockDim = dim3(256);
+    launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::to_bf16_kernel, x, ldx, static_cast<__nv_bfloat16 *>(y), ldy,
+                                               (int) rows, (int) cols),
+                            "to_bf16_kernel");
 }
 
 }  // extern "C"
