@@ -185,7 +185,18 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t sr
 // shared-memory source (the buffer may then be reused or released). The global writes complete
 // asynchronously; they are part of the grid's work, so stream order and griddepcontrol.wait in a
 // dependent grid see them.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed store groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read_n() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void tma_store_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }

@@ -21,8 +21,11 @@
 //            accumulator buffer (tile % 2), then a commit that frees the stage; after the tile's
 //            last stage a commit to acc_full;
 //   warps 2-5 epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (its quadrant: one
-//            output row per thread), 32 columns at a time, adds the residual, rounds and stores;
-//            then releases the accumulator buffer, which the MMA issuer reuses two tiles later.
+//            output row per thread), 32 columns at a time, adds the residual, rounds, and writes
+//            the 32 x 32 block into one of its two swizzled staging buffers, which a TMA bulk store
+//            copies out while the warp goes on (coalesced, clipped at the matrix edges); the
+//            accumulator buffer is released as soon as its last columns are read, and the MMA
+//            issuer reuses it two tiles later.
 // Two accumulator buffers (2 x 256 columns) let the epilogue of tile i run under the MMAs of
 // tile i + 1. Every wait is bounded (the launch's wait limit); on timeout the kernel records it,
 // drains its copies and MMAs, frees tensor memory and returns.
@@ -44,7 +47,11 @@ constexpr int kStageBytes = kATile + kBTile;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kTmemCols = 2 * kBN;
-constexpr int kOffBar = kStages * kStageBytes;
+// Output staging: per epilogue warp two buffers of one 32 x 32 block (4 KiB: f32 rows of 128 B;
+// bf16 rows of 64 B use half), 1024-byte aligned for the swizzled TMA layout.
+constexpr int kStageBufBytes = 4096;
+constexpr int kOffOut = kStages * kStageBytes;
+constexpr int kOffBar = kOffOut + kEpiWarps * 2 * kStageBufBytes;
 constexpr int kSmemBytes = 1024 + kOffBar + 256;  // + alignment slack, barriers
 static_assert(kSmemBytes <= 232448, "shared memory over the 227 KiB limit");
 
@@ -85,9 +92,8 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// 32 consecutive outputs of one row: v + residual (if any), rounded once, stored as 16-byte
-// vectors (ncol < 32 at the right edge: element by element).
-__device__ __forceinline__ void store_row32(const Params &p, int64_t gm, int gn, int ncol, float v[32]) {
+// Adds the residual to 32 consecutive outputs of one row (ncol < 32 at the right edge).
+__device__ __forceinline__ void add_residual32(const Params &p, int64_t gm, int gn, int ncol, float v[32]) {
     // (Tail loops are unrolled with a predicate so v stays in registers.)
     if (p.res != nullptr) {
         const __nv_bfloat16 *r = p.res + gm * p.ldr + gn;
@@ -106,35 +112,34 @@ __device__ __forceinline__ void store_row32(const Params &p, int64_t gm, int gn,
                 if (i < ncol) v[i] += __bfloat162float(r[i]);
         }
     }
-    if (p.out_f32) {
-        float *o = reinterpret_cast<float *>(p.out) + gm * p.ldo + gn;
-        if (ncol == 32) {
+}
+
+// Row `row` (0..31) of a 32 x 32 staging block, rounded once to the output type and written as
+// 16-byte chunks in the TMA swizzled layout: f32 rows of 128 B (128-byte swizzle: chunk ^ row % 8),
+// bf16 rows of 64 B (64-byte swizzle: chunk ^ (row / 2) % 4). One row per lane is bank-conflict
+// free in both.
+__device__ __forceinline__ void stage_row32(uint32_t buf, int row, bool f32, const float v[32]) {
+    if (f32) {
 #pragma unroll
-            for (int i = 0; i < 8; i++)
-                *reinterpret_cast<float4 *>(o + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (i < ncol) o[i] = v[i];
-        }
+        for (int c = 0; c < 8; c++)
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(buf + (uint32_t) row * 128u +
+                                                                           (uint32_t) ((c ^ (row & 7)) << 4)),
+                         "f"(v[4 * c]), "f"(v[4 * c + 1]), "f"(v[4 * c + 2]), "f"(v[4 * c + 3])
+                         : "memory");
     } else {
-        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out) + gm * p.ldo + gn;
-        if (ncol == 32) {
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                *reinterpret_cast<uint4 *>(o + 8 * i) =
-                    make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
-                               bf16x2_bits(v[8 * i + 4], v[8 * i + 5]), bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (i < ncol) o[i] = __float2bfloat16_rn(v[i]);
-        }
+        for (int c = 0; c < 4; c++)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(buf + (uint32_t) row * 64u +
+                                                                           (uint32_t) ((c ^ ((row >> 1) & 3)) << 4)),
+                         "r"(bf16x2_bits(v[8 * c], v[8 * c + 1])), "r"(bf16x2_bits(v[8 * c + 2], v[8 * c + 3])),
+                         "r"(bf16x2_bits(v[8 * c + 4], v[8 * c + 5])), "r"(bf16x2_bits(v[8 * c + 6], v[8 * c + 7]))
+                         : "memory");
     }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap amap,
-                                                           const __grid_constant__ CUtensorMap bmap, const Params p) {
+                                                           const __grid_constant__ CUtensorMap bmap,
+                                                           const __grid_constant__ CUtensorMap omap, const Params p) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
@@ -241,11 +246,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
         }
     } else {
-        // ---- epilogue: one output row per thread, 32 columns per tensor-memory load ----
+        // ---- epilogue: one output row per thread, 32 columns per tensor-memory load, out through
+        // TMA stores of 32 x 32 blocks staged in this warp's two buffers ----
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t) (quad * 32) << 16);
-        int c = 0;
+        const uint32_t stage0 = s0 + kOffOut + (uint32_t) (warp - 2) * 2 * kStageBufBytes;
+        const bool f32 = p.out_f32 != 0;
+        int c = 0, n_st = 0;  // tiles seen, stores issued by this warp
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, c++) {
             const int buf = c & 1;
@@ -255,20 +263,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 break;
             }
             tc_fence_after();
-            const int64_t gm = (int64_t) (w % p.m_tiles) * kBM + r;
+            const int m0 = (w % p.m_tiles) * kBM;
+            const int64_t gm = (int64_t) m0 + r;
             const int n0 = (w / p.m_tiles) * kBN;
 #pragma unroll 1
             for (int ch = 0; ch < kBN / 32; ch++) {
                 float v[32];
                 tmem_ld32(lane_base + (uint32_t) (buf * kBN + ch * 32), v);
                 tmem_wait_ld();
+                if (ch == kBN / 32 - 1) {  // the accumulator buffer is read out: the MMAs may reuse it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&bars->acc_empty[buf]));
+                }
                 const int gn = n0 + ch * 32;
-                if (gm < p.m && gn < p.n) store_row32(p, gm, gn, min(32, p.n - gn), v);
+                if (gn >= p.n) continue;  // warp-uniform: the block lies right of the matrix
+                if (gm < p.m) add_residual32(p, gm, gn, min(32, p.n - gn), v);
+                const uint32_t sb = stage0 + (uint32_t) (n_st & 1) * kStageBufBytes;
+                if (lane == 0 && n_st >= 2) tma_store_wait_read_n<1>();  // the store two back has read sb
+                __syncwarp();
+                stage_row32(sb, lane, f32, v);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && !*abort_flag) {  // rows / columns past the matrix are clipped by the store
+                    tma_store_2d(&omap, sb, gn, m0 + quad * 32);
+                    tma_store_commit();
+                }
+                n_st++;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars->acc_empty[buf]));
         }
+        if (lane == 0) tma_store_wait_read_n<0>();  // staging buffers are read before the CTA exits
         if (!ok && lane == 0) {
             report(p.status, kStatusTimeout, kSiteGemmWait, warp);
             *abort_flag = 1;

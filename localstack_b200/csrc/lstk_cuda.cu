@@ -145,6 +145,24 @@ int encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t r
     return LSTK_OK;
 }
 
+// 2-D map for the projection's TMA stores: [rows][ld] of bf16 or f32 with a 32 x 32 box in the
+// swizzled staging layout (64-byte swizzle for bf16 rows of 64 B, 128-byte for f32 rows of 128 B).
+int encode_out_2d(CUtensorMap *map, void *base, bool f32, uint64_t cols, uint64_t rows, uint64_t ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const uint64_t es = f32 ? 4 : 2;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * es};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
+    return LSTK_OK;
+}
+
 int encode_f16_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
                   uint32_t box1, uint32_t box2) {
     return encode_3d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dim0, dim1, dim2, box0, box1, box2);
@@ -703,9 +721,11 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
     DeviceInfo *dev = nullptr;
     int rc = bind_device(out, &dev);
     if (rc) return rc;
-    CUtensorMap amap, bmap;
+    CUtensorMap amap, bmap, omap;
     if ((rc = encode_bf16_2d(&amap, x, (uint64_t) k, (uint64_t) m, (uint64_t) ldx, gemm::kBM))) return rc;
     if ((rc = encode_bf16_2d(&bmap, w, (uint64_t) k, (uint64_t) n, (uint64_t) ldw, gemm::kBN))) return rc;
+    if ((rc = encode_out_2d(&omap, out, out_dtype == LSTK_DTYPE_F32, (uint64_t) n, (uint64_t) m, (uint64_t) ldo)))
+        return rc;
     gemm::Params p;
     p.m = m;
     p.n = n;
@@ -731,7 +751,7 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
     cfg.blockDim = dim3(gemm::kThreads);
     cfg.dynamicSmemBytes = gemm::kSmemBytes;
     launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
-    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, p), "gemm_kernel");
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, omap, p), "gemm_kernel");
 }
 
 int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,
