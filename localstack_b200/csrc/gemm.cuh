@@ -47,11 +47,11 @@ constexpr int kStageBytes = kATile + kBTile;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kTmemCols = 2 * kBN;
-// Output staging: per epilogue warp two buffers of one 32 x 32 block (4 KiB: f32 rows of 128 B;
-// bf16 rows of 64 B use half), 1024-byte aligned for the swizzled TMA layout.
-constexpr int kStageBufBytes = 4096;
+// Output staging: 8 KiB per epilogue warp, a ring of 32 x 32 blocks in the swizzled TMA layout:
+// two f32 blocks of 4 KiB (rows of 128 B) or four bf16 blocks of 2 KiB (rows of 64 B).
+constexpr int kWarpStageBytes = 8192;
 constexpr int kOffOut = kStages * kStageBytes;
-constexpr int kOffBar = kOffOut + kEpiWarps * 2 * kStageBufBytes;
+constexpr int kOffBar = kOffOut + kEpiWarps * kWarpStageBytes;
 constexpr int kSmemBytes = 1024 + kOffBar + 256;  // + alignment slack, barriers
 static_assert(kSmemBytes <= 232448, "shared memory over the 227 KiB limit");
 
@@ -71,6 +71,7 @@ struct Barriers {
     uint64_t full[kStages], empty[kStages];
     uint64_t acc_full[2], acc_empty[2];
     uint64_t drain;
+    uint64_t res_full[kEpiWarps][4];  // residual block landed in staging buffer b of epilogue warp w
     uint32_t tmem_base;
     int abort;
 };
@@ -137,9 +138,26 @@ __device__ __forceinline__ void stage_row32(uint32_t buf, int row, bool f32, con
     }
 }
 
+// Adds row `row` of a bf16 32 x 32 block staged with the 64-byte swizzle to v.
+__device__ __forceinline__ void add_staged_bf16_row(uint32_t buf, int row, float v[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint32_t w0, w1, w2, w3;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                     : "r"(buf + (uint32_t) row * 64u + (uint32_t) ((c ^ ((row >> 1) & 3)) << 4))
+                     : "memory");
+        v[8 * c + 0] += bf16_lo(w0), v[8 * c + 1] += bf16_hi(w0), v[8 * c + 2] += bf16_lo(w1);
+        v[8 * c + 3] += bf16_hi(w1), v[8 * c + 4] += bf16_lo(w2), v[8 * c + 5] += bf16_hi(w2);
+        v[8 * c + 6] += bf16_lo(w3), v[8 * c + 7] += bf16_hi(w3);
+    }
+}
+
+// rmap: the residual as bf16 32 x 32 blocks (64-byte swizzle), read by TMA when the output is bf16.
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap amap,
                                                            const __grid_constant__ CUtensorMap bmap,
-                                                           const __grid_constant__ CUtensorMap omap, const Params p) {
+                                                           const __grid_constant__ CUtensorMap omap,
+                                                           const __grid_constant__ CUtensorMap rmap, const Params p) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
@@ -158,6 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(smem_u32(&bars->acc_empty[b]), kEpiWarps);
         }
         mbar_init(smem_u32(&bars->drain), 1);
+        for (int e = 0; e < kEpiWarps; e++)
+            for (int b = 0; b < 4; b++) mbar_init(smem_u32(&bars->res_full[e][b]), 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -247,40 +267,69 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else {
         // ---- epilogue: one output row per thread, 32 columns per tensor-memory load, out through
-        // TMA stores of 32 x 32 blocks staged in this warp's two buffers ----
+        // TMA stores of 32 x 32 blocks staged in this warp's ring of buffers. A bf16 output's
+        // residual block is brought into the same buffer by a TMA load one block ahead. ----
         const int quad = warp & 3;
+        const int ew = warp - 2;
         const int r = quad * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t) (quad * 32) << 16);
-        const uint32_t stage0 = s0 + kOffOut + (uint32_t) (warp - 2) * 2 * kStageBufBytes;
+        const uint32_t stage0 = s0 + kOffOut + (uint32_t) ew * kWarpStageBytes;
         const bool f32 = p.out_f32 != 0;
-        int c = 0, n_st = 0;  // tiles seen, stores issued by this warp
+        const bool res_tma = p.res != nullptr && !f32;
+        const int nbuf = f32 ? 2 : 4;
+        const uint32_t buf_bytes = f32 ? 4096u : 2048u;
+        int c = 0, j = 0, n_res = 0;  // tiles seen; blocks staged; residual loads issued (lane 0)
         bool ok = true;
-        for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, c++) {
+        // Lane 0: residual block of output block jj (columns gn, rows m0 + 32 quad ..) into buffer jj % 4,
+        // once the store that last read that buffer (block jj - 4) is done with it.
+        auto load_res = [&](int jj, int gn, int m0) {
+            tma_store_wait_read_n<2>();
+            const uint32_t bar = smem_u32(&bars->res_full[ew][jj & 3]);
+            mbar_arrive_expect_tx(bar, 2048);
+            tma_load_2d(stage0 + (uint32_t) (jj & 3) * 2048u, &rmap, bar, gn, m0 + quad * 32);
+            n_res++;
+        };
+        for (int w = blockIdx.x; ok && w < p.n_work; w += gridDim.x, c++) {
             const int buf = c & 1;
+            const int m0 = (w % p.m_tiles) * kBM;
+            const int64_t gm = (int64_t) m0 + r;
+            const int n0 = (w / p.m_tiles) * kBN;
+            const int nch = min(kBN / 32, (p.n - n0 + 31) / 32);  // column blocks inside the matrix
+            if (res_tma && lane == 0 && !*abort_flag) load_res(j, n0, m0);
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->acc_full[buf]), (uint32_t) (c >> 1) & 1,
                                                             abort_flag, p.wait_ns))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int m0 = (w % p.m_tiles) * kBM;
-            const int64_t gm = (int64_t) m0 + r;
-            const int n0 = (w / p.m_tiles) * kBN;
 #pragma unroll 1
             for (int ch = 0; ch < kBN / 32; ch++) {
+                if (ch >= nch) break;  // warp-uniform: the rest lies right of the matrix (released below)
+                const int gn = n0 + ch * 32;
+                if (res_tma && lane == 0 && ch + 1 < nch && !*abort_flag) load_res(j + 1, gn + 32, m0);
                 float v[32];
                 tmem_ld32(lane_base + (uint32_t) (buf * kBN + ch * 32), v);
                 tmem_wait_ld();
-                if (ch == kBN / 32 - 1) {  // the accumulator buffer is read out: the MMAs may reuse it
+                if (ch == nch - 1) {  // the accumulator's columns in the matrix are read: the MMAs may reuse it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&bars->acc_empty[buf]));
                 }
-                const int gn = n0 + ch * 32;
-                if (gn >= p.n) continue;  // warp-uniform: the block lies right of the matrix
-                if (gm < p.m) add_residual32(p, gm, gn, min(32, p.n - gn), v);
-                const uint32_t sb = stage0 + (uint32_t) (n_st & 1) * kStageBufBytes;
-                if (lane == 0 && n_st >= 2) tma_store_wait_read_n<1>();  // the store two back has read sb
+                const uint32_t sb = stage0 + (uint32_t) (j % nbuf) * buf_bytes;
+                if (res_tma) {
+                    if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->res_full[ew][j & 3]),
+                                                                    (uint32_t) (j >> 2) & 1, abort_flag, p.wait_ns))) {
+                        ok = false;
+                        break;
+                    }
+                    add_staged_bf16_row(sb, lane, v);
+                } else {
+                    if (gm < p.m) add_residual32(p, gm, gn, min(32, p.n - gn), v);
+                    if (lane == 0) {  // the store that last read sb (nbuf blocks back) is done with it
+                        if (f32) tma_store_wait_read_n<1>();
+                        else tma_store_wait_read_n<3>();
+                    }
+                }
                 __syncwarp();
                 stage_row32(sb, lane, f32, v);
                 fence_proxy_async_smem();
@@ -289,13 +338,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     tma_store_2d(&omap, sb, gn, m0 + quad * 32);
                     tma_store_commit();
                 }
-                n_st++;
+                j++;
             }
         }
-        if (lane == 0) tma_store_wait_read_n<0>();  // staging buffers are read before the CTA exits
-        if (!ok && lane == 0) {
-            report(p.status, kStatusTimeout, kSiteGemmWait, warp);
-            *abort_flag = 1;
+        if (lane == 0) {
+            // residual loads still in flight land before shared memory is released
+            for (int jj = j; jj < n_res; jj++)
+                mbar_wait_bounded(smem_u32(&bars->res_full[ew][jj & 3]), (uint32_t) (jj >> 2) & 1, nullptr);
+            tma_store_wait_read_n<0>();  // staging buffers are read before the CTA exits
+            if (!ok) {
+                report(p.status, kStatusTimeout, kSiteGemmWait, warp);
+                *abort_flag = 1;
+            }
         }
     }
 

@@ -726,6 +726,11 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
     if ((rc = encode_bf16_2d(&bmap, w, (uint64_t) k, (uint64_t) n, (uint64_t) ldw, gemm::kBN))) return rc;
     if ((rc = encode_out_2d(&omap, out, out_dtype == LSTK_DTYPE_F32, (uint64_t) n, (uint64_t) m, (uint64_t) ldo)))
         return rc;
+    // the residual as TMA blocks (read that way for bf16 outputs); without one, any valid map
+    CUtensorMap rmap = omap;
+    if (residual && (rc = encode_out_2d(&rmap, const_cast<void *>(residual), false, (uint64_t) n, (uint64_t) m,
+                                        (uint64_t) ldr)))
+        return rc;
     gemm::Params p;
     p.m = m;
     p.n = n;
@@ -751,7 +756,7 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
     cfg.blockDim = dim3(gemm::kThreads);
     cfg.dynamicSmemBytes = gemm::kSmemBytes;
     launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
-    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, omap, p), "gemm_kernel");
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, omap, rmap, p), "gemm_kernel");
 }
 
 int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,
