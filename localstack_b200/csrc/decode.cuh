@@ -262,12 +262,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
     int32_t *pfx = reinterpret_cast<int32_t *>(empty + kStages) + 4;
 
+    __shared__ int32_t stage_pid[kStages];  // page id of each stage's page-group (producer -> consumers)
     // Inputs (q, seq_lens, tables, pages) may come from the previous kernel in the stream; the
     // combine grid may be scheduled right away (it waits for this grid to complete).
     pdl_wait();
     pdl_launch_dependents();
-    // Prefix over sequences of page counts (every CTA computes it; CTA 0 publishes it).
-    __shared__ int32_t chunk_sum[kThreads];
+    // Prefix over sequences of page counts (every CTA computes it; CTA 0 publishes it): thread t
+    // sums the pages of its run of sequences, a block-wide scan (warp shuffles, then the warps'
+    // totals) gives each run's start.
+    __shared__ int32_t warp_tot[kThreads / 32];
     {
         const int per = (p.n_seqs + kThreads - 1) / kThreads;
         const int b0 = threadIdx.x * per;
@@ -277,18 +280,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             if (len < 0 || len > p.max_blocks * kPage) report(p.status, kStatusBadIndex, kSiteDecodeLen, b);
             local += (range_len(p, len) + kPage - 1) / kPage;
         }
-        chunk_sum[threadIdx.x] = local;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int32_t acc = 0;
-            for (int i = 0; i < kThreads; i++) {
-                const int32_t v = chunk_sum[i];
-                chunk_sum[i] = acc;
-                acc += v;
-            }
+        int32_t incl = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += y;
         }
+        if (lane == 31) warp_tot[warp] = incl;
         __syncthreads();
-        int32_t acc = chunk_sum[threadIdx.x];
+        int32_t acc = incl - local;
+        for (int w = 0; w < warp; w++) acc += warp_tot[w];
         for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
             pfx[b] = acc;
             acc += (range_len(p, p.seq_lens[b]) + kPage - 1) / kPage;
@@ -312,56 +313,88 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     const int64_t hi = range_lo(blockIdx.x + 1, P, gridDim.x);
 
     if (lo < hi && warp == kConsumerWarps) {
-        // Producer: one lane streams the CTA's page-groups through the stage ring.
+        // Producer warp: the whole warp reads the block-table entries of the CTA's page-groups, 32
+        // at a time and one batch ahead (lane i: page-group xb + i), so no copy waits on a table
+        // read; lane 0 streams the page-groups through the stage ring, handing each stage's page id
+        // to the consumers in shared memory.
+        __shared__ int32_t batch_pid[2][32];
+        __shared__ int32_t batch_hg[2][32];
+        uint64_t policy = 0;
+        bool ok = true;
         if (lane == 0) {
             prefetch_tensormap(&kmap);
             prefetch_tensormap(&vmap);
-            const uint64_t policy = l2_policy_evict_first();
-            Cursor cur;
-            cur.locate(lo, pfx, p.n_seqs, p.n_hg);
-            int64_t i = 0;
-            bool ok = true;
+            policy = l2_policy_evict_first();
             if (p.start_flag != nullptr && !flag_wait_bounded(p.start_flag, abort_flag, p.wait_ns)) {
                 report(p.status, kStatusTimeout, kSiteDecodeWaitStart, blockIdx.x);
                 *abort_flag = 1;
                 ok = false;
             }
-            for (int64_t x = lo; ok && x < hi; x++, i++) {
-                const int s = (int) (i % kStages);
-                const uint32_t k_use = (uint32_t) (i / kStages);
-                if (k_use > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag, p.wait_ns)) {
-                    report(p.status, kStatusTimeout, kSiteDecodeWaitEmpty, s);
-                    *abort_flag = 1;
-                    ok = false;
-                    break;
-                }
-                const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + p.kv_page0 + cur.p];
-                const int nh = min(kHeadsPerGroup, p.n_head_kv - cur.hg * kHeadsPerGroup);
-                const uint32_t fb = smem_u32(&full[s]);
-                if (pid < 0 || pid >= p.n_pages) {
-                    report(p.status, kStatusBadIndex, kSiteDecodePage, pid);
-                    mbar_arrive(fb);
-                } else {
-                    mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kHeadPage));
-                    const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
-                    for (int h = 0; h < nh; h++) {
-                        const int kvh = cur.hg * kHeadsPerGroup + h;
-                        for (int half = 0; half < 2; half++) {
-                            const uint32_t off = (uint32_t) (h * kHeadPage + half * kSubTile);
-                            tma_load_3d_hint(sb + off, &kmap, fb, half * 64, kvh, pid * kPage, policy);
-                            tma_load_3d_hint(sb + kHeadsPerGroup * kHeadPage + off, &vmap, fb, half * 64, kvh,
-                                             pid * kPage, policy);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        auto fetch = [&](int64_t xb, int32_t &pid, int &hg) {
+            const int64_t x = xb + lane;
+            pid = -1;
+            hg = 0;
+            if (x < hi) {
+                Cursor c;
+                c.locate(x, pfx, p.n_seqs, p.n_hg);
+                hg = c.hg;
+                pid = p.block_tables[(int64_t) c.b * p.max_blocks + p.kv_page0 + c.p];
+            }
+        };
+        int32_t pid_next;
+        int hg_next;
+        fetch(lo, pid_next, hg_next);
+        int64_t i = 0;  // page-groups issued (lane 0)
+        for (int64_t xb = lo; ok && xb < hi; xb += 32) {
+            const int bb = (int) ((xb - lo) >> 5) & 1;
+            batch_pid[bb][lane] = pid_next;
+            batch_hg[bb][lane] = hg_next;
+            __syncwarp();
+            if (xb + 32 < hi) fetch(xb + 32, pid_next, hg_next);  // in flight while lane 0 issues
+            if (lane == 0) {
+                const int cnt = (int) (hi - xb < 32 ? hi - xb : 32);
+                for (int e = 0; e < cnt; e++, i++) {
+                    const int s = (int) (i % kStages);
+                    const uint32_t k_use = (uint32_t) (i / kStages);
+                    if (k_use > 0 &&
+                        !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag, p.wait_ns)) {
+                        report(p.status, kStatusTimeout, kSiteDecodeWaitEmpty, s);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const int32_t pid = batch_pid[bb][e];
+                    const int hg = batch_hg[bb][e];
+                    stage_pid[s] = pid;  // published to the consumers by the arrival below
+                    const int nh = min(kHeadsPerGroup, p.n_head_kv - hg * kHeadsPerGroup);
+                    const uint32_t fb = smem_u32(&full[s]);
+                    if (pid < 0 || pid >= p.n_pages) {
+                        report(p.status, kStatusBadIndex, kSiteDecodePage, pid);
+                        mbar_arrive(fb);
+                    } else {
+                        mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kHeadPage));
+                        const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                        for (int h = 0; h < nh; h++) {
+                            const int kvh = hg * kHeadsPerGroup + h;
+                            for (int half = 0; half < 2; half++) {
+                                const uint32_t off = (uint32_t) (h * kHeadPage + half * kSubTile);
+                                tma_load_3d_hint(sb + off, &kmap, fb, half * 64, kvh, pid * kPage, policy);
+                                tma_load_3d_hint(sb + kHeadsPerGroup * kHeadPage + off, &vmap, fb, half * 64, kvh,
+                                                 pid * kPage, policy);
+                            }
                         }
                     }
                 }
-                cur.advance(pfx, p.n_seqs, p.n_hg);
             }
-            if (!ok || *abort_flag) {
-                // Let every copy already issued land before the CTA's shared memory goes away.
-                const int64_t n_issued = i;
-                for (int64_t j = n_issued > kStages ? n_issued - kStages : 0; j < n_issued; j++)
-                    mbar_wait_bounded(smem_u32(&full[j % kStages]), (uint32_t) (j / kStages) & 1, nullptr);
-            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        if (lane == 0 && (!ok || *abort_flag)) {
+            // Let every copy already issued land before the CTA's shared memory goes away.
+            const int64_t n_issued = i;
+            for (int64_t j = n_issued > kStages ? n_issued - kStages : 0; j < n_issued; j++)
+                mbar_wait_bounded(smem_u32(&full[j % kStages]), (uint32_t) (j / kStages) & 1, nullptr);
         }
     } else if (lo < hi) {
         // Consumers: warp w owns KV head hg*4 + w of every page-group.
@@ -370,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         cur.locate(lo, pfx, p.n_seqs, p.n_hg);
         int64_t piece_start = lo;
         int64_t i = 0;
+        int len = 0;  // keys of the current segment's sequence inside the call's range
         for (int64_t x = lo; x < hi; x++, i++) {
             const int np = pfx[cur.b + 1] - pfx[cur.b];
             const int kvh = cur.hg * kHeadsPerGroup + warp;
@@ -378,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                 piece_start = x;
                 st.reset();
                 if (active) load_q(st, p, cur.b, kvh, lane);
+                len = range_len(p, p.seq_lens[cur.b]);
             }
             const int s = (int) (i % kStages);
             // Warp-uniform outcome: ldmatrix / mma.sync below are warp-collective.
@@ -389,9 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                 }
                 break;
             }
-            const int32_t pid = p.block_tables[(int64_t) cur.b * p.max_blocks + p.kv_page0 + cur.p];
+            const int32_t pid = stage_pid[s];
             if (active && pid >= 0 && pid < p.n_pages) {
-                const int len = range_len(p, p.seq_lens[cur.b]);
                 const int valid = min(kPage, len - cur.p * kPage);
                 const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
                 process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage, valid,
@@ -516,9 +550,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     den = warp_sum_xor(den, 1);
     if (lane == 0) red_sum[warp] = den;
     __syncthreads();
-    // Pass 3: warp k sums pieces k, k + 8, ..., loading 8 of them at a time before any use, so a
-    // long sequence split over many CTAs costs a few memory round trips, not one per piece.
-    constexpr int kBatch = 8;
+    // Pass 3: warp k sums pieces k, k + 8, ..., loading 24 of them at a time before any use, so a
+    // long sequence split over a whole grid of CTAs (148 pieces) costs one memory round trip here.
+    constexpr int kBatch = 24;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = warp; i0 < n_pc; i0 += kCombineWarps * kBatch) {
         float4 v[kBatch];
