@@ -27,6 +27,7 @@ struct DeviceStatus {
 enum : int {
     kSiteAppendCell = 1,
     kSiteAppendPos = 2,
+    kSiteAppendWait = 3,
     kSiteDecodePage = 10,
     kSiteDecodeLen = 11,
     kSiteDecodeWaitFull = 12,

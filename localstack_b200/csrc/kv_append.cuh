@@ -5,23 +5,26 @@
 // writes 2 Hkv * 128 f16 cache values plus Hq * 128 Q values.
 //
 // Bit-exactness. Every floating-point step uses an explicitly rounded intrinsic so nothing is
-// contracted into an FMA, and the RMS sum of squares is accumulated in double in index order,
-// the order ggml's CPU rms_norm uses. With the same (cos, sin) table the f16 cache bytes equal
-// a CPU evaluation of the ggml op sequence.
+// contracted into an FMA, and the RMS sum of squares equals ggml's CPU rms_norm sum (f32
+// squares added in double in index order): rows whose partial sums cannot round are summed in
+// parallel (any order gives the exact total), every other row sequentially in index order. With
+// the same (cos, sin) table the f16 cache bytes equal a CPU evaluation of the ggml op sequence.
 //
-// Work decomposition. A "row" is one (token, head) vector of 128 values; rows are numbered
-// token-major: for token t, rows [t*R, t*R + R) with R = Hq + 2*Hkv are Hq query heads, Hkv key
-// heads, Hkv value heads. Each warp takes up to 32 consecutive rows (8 or 16 for short appends,
-// whose time is one warp's chain of dependent steps; at most 16 with f32 data). The rows, and
-// the RoPE rows of the group's first four tokens, are staged into shared memory with 16-byte
-// cp.async copies (a bf16 row is 16 chunks, so one warp instruction moves two rows), every copy
-// of the group in flight at once and no registers held. Lane r then sums row r's squares
-// sequentially in double: independent chains across the lanes, where the sequential order
-// leaves no parallelism inside a row; it also prepares row r's kind, destination and RoPE slot.
-// The warp writes four rows per step: lanes 8s..8s+7 take one row, lane c its NEOX pairs
-// [8c, 8c+8) (elements 8c..8c+7 and 64+8c..64+8c+7), loaded and stored as 16-byte vectors with
-// branch-free arithmetic, so the per-row shuffles and address work are shared by four rows.
+// Work decomposition. A "row" is one (token, head) vector of 128 values; token t has R = Hq +
+// 2 Hkv rows: Hq query heads, Hkv key heads, Hkv value heads. A group is G consecutive rows of
+// one token (G a multiple of 4, at most 32 bf16 or 16 f32 rows; the launch picks G so there are
+// enough groups for the grid), and a warp takes a grid-stride sequence of groups on a grid sized
+// to the resident warps. A group's rows are at most three contiguous pieces of the inputs (its
+// Q, K and V rows), copied into shared memory by bulk async copies together with the RoPE row of
+// the token's position, completing on one mbarrier; two stage buffers per warp keep the next
+// group's copies in flight while the current group is processed. Four rows per step: lanes
+// 8s..8s+7 take one row, lane c its NEOX pairs [8c, 8c+8) (elements 8c..8c+7 and 64+8c..64+8c+7)
+// as 16-byte vectors; the row's sum of squares is reduced across its eight lanes by shuffles, the
+// scale of row r is computed by lane r, and lane c keeps the token's cos / sin of its pairs in
+// registers for the whole group.
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -30,19 +33,12 @@ namespace append {
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
-constexpr int kRowsPerWarp = 32;  // at most; the launch picks 8, 16 or 32 (Params::rows_per_warp)
-// Staged rows keep the input type and layout, 16 bytes of padding after each (16-byte aligned
-// rows for the 16-byte copies): bf16 rows of 68 32-bit words, f32 rows of 132 floats. Lanes
-// reading one row in the write phase hit distinct banks, and so do lanes reading their own rows
-// 16 bytes at a time for the sum (row starts are 17 or 33 16-byte units apart).
-constexpr int kStrideBf16Words = 68;
-constexpr int kStrideF32 = 132;
-constexpr int kRowBytes = 32 * kStrideBf16Words * 4;  // rows of one group: 32 bf16 rows or 16 f32 rows
-static_assert(kRowBytes >= 16 * kStrideF32 * 4, "f32 groups hold at most 16 rows");
-constexpr int kCsTokens = 4;                               // RoPE rows staged per group
-constexpr int kWarpStageBytes = kRowBytes + kCsTokens * kD * 4;
+constexpr int kMaxGroupRows = 32;  // bf16 rows; f32 groups hold at most 16
 constexpr int kGammaBytes = 2 * kD * 4;
-constexpr int kSmemBytes = kGammaBytes + kWarps * kWarpStageBytes;
+// One stage buffer: the group's rows back to back in the input type, then the RoPE row (64
+// (cos, sin) pairs). Rows are 256 or 512 bytes, so every piece starts 16-byte aligned.
+__host__ __device__ constexpr int buf_bytes(int group_rows, bool bf16) { return group_rows * kD * (bf16 ? 2 : 4) + kD * 4; }
+constexpr int kSmemBytes = kGammaBytes + kWarps * 2 * (kMaxGroupRows * kD * 2 + kD * 4);  // the largest launch
 
 struct Params {
     const void *q_in;
@@ -63,43 +59,65 @@ struct Params {
     int64_t n_cells;
     void *q_out;
     int q_out_f16;
-    int rows_per_warp;  // 8, 16 or 32
+    int group_rows;        // G: a multiple of 4, at most 32 (bf16) or 16 (f32)
+    int groups_per_token;  // ceil(R / G)
     DeviceStatus *status;
 };
 
-__device__ __forceinline__ __half2 h2(float a, float b) { return __halves2half2(__float2half_rn(a), __float2half_rn(b)); }
-
-// Input row (t, j) as the 32-bit words lane `lane` needs: bf16 -> w[0] = elements (2l, 2l+1),
-// w[1] = (64+2l, 65+2l); f32 -> w[0..3] = elements 2l, 2l+1, 64+2l, 65+2l.
-__device__ __forceinline__ const void *row_ptr(const Params &p, int64_t t, int j) {
-    if (j < p.n_head) return p.in_bf16 ? (const void *) ((const uint16_t *) p.q_in + t * p.q_stride + (int64_t) j * kD)
-                                       : (const void *) ((const float *) p.q_in + t * p.q_stride + (int64_t) j * kD);
-    if (j < p.n_head + p.n_head_kv) {
-        const int64_t o = t * p.k_stride + (int64_t) (j - p.n_head) * kD;
-        return p.in_bf16 ? (const void *) ((const uint16_t *) p.k_in + o) : (const void *) ((const float *) p.k_in + o);
-    }
-    const int64_t o = t * p.v_stride + (int64_t) (j - p.n_head - p.n_head_kv) * kD;
-    return p.in_bf16 ? (const void *) ((const uint16_t *) p.v_in + o) : (const void *) ((const float *) p.v_in + o);
+// Packed f32 pairs (one 64-bit register pair): each lane of mul.rn.f32x2 is an IEEE round-to-
+// nearest multiply on its own, the same as the scalar __fmul_rn.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void uf2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ void uf2u(uint64_t v, uint32_t &lo, uint32_t &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// Two floats as an f16 pair, each rounded to nearest even (lower half = lo).
+__device__ __forceinline__ uint32_t f16x2_bits(float lo, float hi) {
+    uint32_t h;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+    return h;
 }
 
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+
+// One contiguous global -> shared copy by the async proxy, completing on `bar` (addresses and
+// size multiples of 16 bytes).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+// min(|a|, |b|) of each bf16 half (the result's sign bits are not used).
+__device__ __forceinline__ uint32_t min_abs_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
-// Shared-memory layouts chosen so that the write loop's 16-byte reads are free of bank conflicts.
-// In the write loop lane c (of eight per row) reads gamma chunks 2c + q + 16h (four floats each)
-// and the (cos, sin) chunks 4c + q of a RoPE row; eight lanes of a quarter-warp then hit the
-// same banks two (gamma) or four (RoPE) at a time in the natural order. Gamma chunk k is stored
-// at slot k ^ ((k >> 3) & 1), RoPE chunk 4c + q at 4c + ((q + (c >> 1)) & 3).
+// The write loop's 16-byte gamma reads are free of bank conflicts with gamma chunk k stored at
+// slot k ^ ((k >> 3) & 1): lane c (of eight per row) reads chunks 2c + q + 16h, which would hit
+// the same banks two at a time in the natural order.
 __device__ __forceinline__ int gamma_slot(int k) { return k ^ ((k >> 3) & 1); }
-__device__ __forceinline__ int rope_slot(int k) { return (k & ~3) | (((k & 3) + ((k >> 3) & 3)) & 3); }
 
+// kBf16: bf16 inputs (else f32); kQ16: Q written as f16 (else f32). Params::in_bf16 and
+// q_out_f16 match the instantiation.
+template <bool kBf16, bool kQ16>
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
-    extern __shared__ __align__(16) uint8_t stage_smem[];
-    float *s_gamma = reinterpret_cast<float *>(stage_smem);  // [2][128]: q_gamma, k_gamma (1 when absent)
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[kWarps][2];    // per warp, per stage buffer
+    __shared__ double s_part_sum[kWarps][kMaxGroupRows * 8];  // per row, the sums of its eight lanes' squares
+    __shared__ uint32_t s_part_min[kWarps][kMaxGroupRows * 8];  // and their smallest |x|
+    float *s_gamma = reinterpret_cast<float *>(smem);     // [2][128]: q_gamma, k_gamma (1 when absent)
 
     // Inputs may come from the previous kernel in the stream (programmatic dependent launch);
     // the decode launched after this kernel may be staged right away (it waits for completion).
@@ -112,239 +130,348 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         s_gamma[at] = p.q_gamma != nullptr ? p.q_gamma[i] : 1.f;
         s_gamma[kD + at] = p.k_gamma != nullptr ? p.k_gamma[i] : 1.f;
     }
+    if (lane == 0) {
+        mbar_init(smem_u32(&s_bar[warp][0]), 1);
+        mbar_init(smem_u32(&s_bar[warp][1]), 1);
+        fence_barrier_init();
+    }
     __syncthreads();
+
     const int R = p.n_head + 2 * p.n_head_kv;
     const int n_qk = p.n_head + p.n_head_kv;
-    const int64_t n_rows = (int64_t) p.n_tokens * R;
-    const int rpw = p.rows_per_warp;
-    const int64_t n_groups = (n_rows + rpw - 1) / rpw;
-    uint8_t *stage = stage_smem + kGammaBytes + warp * kWarpStageBytes;
-    const uint32_t stage_u32 = smem_u32(stage);
-    const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);  // bf16 pairs
-    const float *sf = reinterpret_cast<const float *>(stage);        // f32
-    const float *s_cs = reinterpret_cast<const float *>(stage + kRowBytes);  // [kCsTokens][64] (cos, sin)
+    const int G = p.group_rows, gpt = p.groups_per_token;
+    const int64_t n_groups = (int64_t) p.n_tokens * gpt;
+    const int es = kBf16 ? 2 : 4;  // input element bytes
+    const int row_bytes = kD * es;
+    const int rope_off = G * row_bytes;
+    const int bbytes = rope_off + kD * 4;
+    uint8_t *bufs = smem + kGammaBytes + warp * 2 * bbytes;
+    const int64_t gstride = (int64_t) gridDim.x * kWarps;
 
-    for (int64_t grp = (int64_t) blockIdx.x * kWarps + warp; grp < n_groups; grp += (int64_t) gridDim.x * kWarps) {
-        const int64_t row0 = grp * rpw;
-        const int nr = (int) (n_rows - row0 < rpw ? n_rows - row0 : rpw);
-        const int64_t t_first = row0 / R;
-        const int j_first = (int) (row0 - t_first * R);
+    struct Group {  // token, its first row, rows, the token's position and cell
+        int64_t t, cell;
+        int j0, nr, pos;
+    };
+    auto locate = [&](int64_t g, Group &m) {
+        m.t = 0, m.cell = -1, m.j0 = 0, m.nr = 0, m.pos = -1;
+        if (g >= n_groups) return;
+        m.t = g / gpt;
+        m.j0 = (int) (g - m.t * gpt) * G;
+        m.nr = min(G, R - m.j0);
+        m.pos = p.positions[m.t];
+        m.cell = p.cells[m.t];
+    };
+    // Lane 0 issues the group's copies into buffer b: its Q, K and V rows (each a contiguous
+    // piece of its input) and the RoPE row of the token's position when the group has Q / K rows
+    // and the position is valid; all complete on the buffer's barrier.
+    auto issue = [&](const Group &m, int b) {
+        if (lane != 0) return;
+        const uint32_t bar = smem_u32(&s_bar[warp][b]);
+        const uint32_t dst = smem_u32(bufs + b * bbytes);
+        const bool rope = m.j0 < n_qk && m.pos >= 0 && m.pos < p.rope_n_pos;
+        fence_proxy_async_smem();  // the buffer's last reads (generic proxy) come before the copies
+        mbar_arrive_expect_tx(bar, (uint32_t) (m.nr * row_bytes + (rope ? kD * 4 : 0)));
+        int j = m.j0;
+        const int end = m.j0 + m.nr;
+        uint32_t d = dst;
+        if (j < p.n_head) {
+            const int n = min(end, p.n_head) - j;
+            bulk_load(d, (const uint8_t *) p.q_in + (m.t * p.q_stride + (int64_t) j * kD) * es, (uint32_t) (n * row_bytes), bar);
+            d += n * row_bytes;
+            j += n;
+        }
+        if (j < end && j < n_qk) {
+            const int n = min(end, n_qk) - j;
+            bulk_load(d, (const uint8_t *) p.k_in + (m.t * p.k_stride + (int64_t) (j - p.n_head) * kD) * es,
+                      (uint32_t) (n * row_bytes), bar);
+            d += n * row_bytes;
+            j += n;
+        }
+        if (j < end)
+            bulk_load(d, (const uint8_t *) p.v_in + (m.t * p.v_stride + (int64_t) (j - n_qk) * kD) * es,
+                      (uint32_t) ((end - j) * row_bytes), bar);
+        if (rope) bulk_load(dst + rope_off, p.rope + (int64_t) m.pos * (kD / 2), kD * 4, bar);
+    };
 
-        // Lane r: metadata of row r (token, head slot, position, cell), loaded in parallel.
-        int64_t my_t = 0, my_cell = 0;
-        int my_j = 0, my_pos = 0;
-        if (lane < nr) {
-            my_t = (row0 + lane) / R;
-            my_j = (int) (row0 + lane - my_t * R);
-            my_pos = p.positions[my_t];
-            if (my_j >= p.n_head) my_cell = p.cells[my_t];
+    const int sub = lane >> 3, c = lane & 7;
+    int goff[4];  // float offsets of this lane's gamma chunks
+#pragma unroll
+    for (int q = 0; q < 4; q++) goff[q] = gamma_slot(2 * c + (q & 1) + 16 * (q >> 1)) * 4;
+    double *part_sum = s_part_sum[warp];
+    uint32_t *part_min = s_part_min[warp];
+    const int sig = kBf16 ? 16 : 24;  // significant bits of a square of an input value
+
+    int64_t g = (int64_t) blockIdx.x * kWarps + warp;
+    Group cur, nxt, nxt2;
+    locate(g, cur);
+    locate(g + gstride, nxt);
+    if (g < n_groups) issue(cur, 0);
+    uint32_t parity = 0;  // bit b: parity of buffer b's next completion
+    for (int b = 0; g < n_groups; g += gstride, b ^= 1) {
+        locate(g + 2 * gstride, nxt2);  // used two groups from now
+        const bool more = g + gstride < n_groups;
+        if (more) issue(nxt, b ^ 1);
+        if (!mbar_wait_bounded(smem_u32(&s_bar[warp][b]), (parity >> b) & 1u, nullptr)) {
+            report(p.status, kStatusTimeout, kSiteAppendWait, (int) g);
+            // leave no copy in flight into this CTA's shared memory
+            mbar_wait_bounded(smem_u32(&s_bar[warp][b]), (parity >> b) & 1u, nullptr);
+            if (more) mbar_wait_bounded(smem_u32(&s_bar[warp][b ^ 1]), (parity >> (b ^ 1)) & 1u, nullptr);
+            return;
+        }
+        parity ^= 1u << b;
+        const uint8_t *buf = bufs + b * bbytes;
+        const bool pos_ok = cur.pos >= 0 && cur.pos < p.rope_n_pos;
+        const bool cell_ok = cur.cell >= 0 && cur.cell < p.n_cells;
+        if (lane == 0 && cur.j0 == 0) {  // once per token
+            if (!pos_ok) report(p.status, kStatusBadIndex, kSiteAppendPos, (int) cur.t);
+            if (!cell_ok) report(p.status, kStatusBadIndex, kSiteAppendCell, (int) cur.t);
         }
 
-        // Stage the rows straight into shared memory with 16-byte cp.async copies (every copy of
-        // the group in flight at once, no registers held): a bf16 row is 16 chunks, so a warp
-        // instruction moves two rows; an f32 row is 32 chunks. (t, j) walk the rows token-major.
-        {
-            const int cpr = p.in_bf16 ? 16 : 32;  // 16-byte chunks per row
-            const int stride_bytes = p.in_bf16 ? kStrideBf16Words * 4 : kStrideF32 * 4;
-            const int sub = lane / cpr;            // which row of the instruction's pair (bf16)
-            const int chunk = lane % cpr;
-            const int step = 32 / cpr;             // rows per instruction
-            int64_t t = t_first;
-            int j = j_first + sub;
-            while (j >= R) {
-                j -= R;
-                t++;
-            }
-            for (int k = sub; k < nr; k += step) {
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(row_ptr(p, t, j)) + chunk * 16;
-                cp_async_16(stage_u32 + (uint32_t) (k * stride_bytes + chunk * 16), src);
-                j += step;
-                while (j >= R) {
-                    j -= R;
-                    t++;
+        // ggml rms_norm sum of each Q / K row's squares (f32 squares added in double in index
+        // order). If no partial sum of a row's squares can round, every order of summation gives
+        // the exact total: each of the row's eight lanes sums its 16 squares (four chains) and
+        // lane r adds row r's eight partials. With |x| >= 2^e for every element, each square is a multiple of
+        // 2^(2e - sig + 1) (sig significant bits: 16 for bf16 inputs, 24 for f32), so a total
+        // below 2^(2e + 53 - sig) - one bit of margin, so a rounded total fails too - is exact;
+        // e >= -63 keeps every square a normal f32 and the total must stay below 2^128. The squares
+        // are added as doubles scaled by 2^-896: the f32 bits shifted into a double's bits (exact
+        // for every finite f32, and an f32 inf or NaN lands at or above 2^128 once unscaled). Rows
+        // failing the test (zeros, tiny or huge values, inf, NaN, a wide spread of magnitudes) are
+        // summed again sequentially by lane r.
+#pragma unroll 2
+        for (int r0 = 0; r0 < cur.nr; r0 += 4) {
+            const int r = r0 + sub;
+            const int j = cur.j0 + r;
+            const bool norm = r < cur.nr && (j < p.n_head ? p.q_gamma != nullptr : (j < n_qk && p.k_gamma != nullptr));
+            double part[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains
+            uint32_t mn = 0x7f7f7f7fu;                 // smallest |x| (bf16 pair or f32 bits)
+            if (norm) {
+                const uint8_t *row = buf + r * row_bytes;
+                if constexpr (kBf16) {
+                    const uint4 a = *reinterpret_cast<const uint4 *>(row + c * 16);
+                    const uint4 bq = *reinterpret_cast<const uint4 *>(row + 128 + c * 16);
+                    const uint32_t w[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+                    uint32_t mn2 = 0x7f7f7f7fu;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        uint32_t s0, s1;
+                        uf2u(mul2(f2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u)),
+                                  f2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u))), s0, s1);
+                        // a normal square of a bf16 value has zero low mantissa bits: the low word is 0
+                        part[(2 * e) & 3] = __dadd_rn(part[(2 * e) & 3], __hiloint2double((int) (s0 >> 3), 0));
+                        part[(2 * e + 1) & 3] = __dadd_rn(part[(2 * e + 1) & 3], __hiloint2double((int) (s1 >> 3), 0));
+                        if (e & 1) mn2 = min_abs_bf16x2(mn2, w[e]);
+                        else mn = min_abs_bf16x2(mn, w[e]);
+                    }
+                    mn = min_abs_bf16x2(mn, mn2);
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            const float4 v = *reinterpret_cast<const float4 *>(row + (h * 64 + c * 8 + q * 4) * 4);
+                            const float vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const uint32_t s0 = __float_as_uint(__fmul_rn(vs[e], vs[e]));
+                                part[e] = __dadd_rn(part[e], __hiloint2double((int) (s0 >> 3), (int) (s0 << 29)));
+                                mn = min(mn, __float_as_uint(vs[e]) & 0x7fffffffu);
+                            }
+                        }
                 }
             }
+            // this lane's partial sum and minimum, combined per row by lane r below
+            part_sum[r * 8 + c] = __dadd_rn(__dadd_rn(part[0], part[1]), __dadd_rn(part[2], part[3]));
+            part_min[r * 8 + c] = mn;
         }
-        // RoPE rows (64 (cos, sin) pairs, 512 B) of the group's first kCsTokens tokens, staged the
-        // same way; the position of token t_first + u comes from the lane holding that token's
-        // first row in the group. Rows of a token with a bad position are never read.
-#pragma unroll
-        for (int u = 0; u < kCsTokens; u++) {
-            const int64_t first_row = (t_first + u) * R - row0;
-            const int src = (int) (first_row < 0 ? 0 : (first_row > 31 ? 31 : first_row));
-            const int pos = __shfl_sync(0xffffffffu, my_pos, src);
-            if (first_row < nr && pos >= 0 && pos < p.rope_n_pos)
-                cp_async_16(stage_u32 + (uint32_t) (kRowBytes + u * kD * 4 + rope_slot(lane) * 16),
-                            p.rope + (int64_t) pos * (kD / 2) + 2 * lane);
-        }
-        cp_async_wait_all();
         __syncwarp();
 
-        // Lane r: ggml rms_norm scale of row r (Q and K rows with a weight), sequential double sum.
+        // Lane r: the scale of row r, 1 / sqrt(mean + eps) with each step rounded as ggml's. The
+        // mean is the total / 128, exact or rounded once either way, so a multiply by the power
+        // of two equals the divide.
         float my_scale = 1.0f;
-        if (lane < nr && my_j < n_qk) {
-            const float *gamma = my_j < p.n_head ? p.q_gamma : p.k_gamma;
-            if (gamma != nullptr) {
-                double sum = 0.0;
-                // 16-byte reads (rows start 272 or 528 bytes apart: the eight lanes of a quarter-warp
-                // cover all 32 banks), summed in index order.
-                if (p.in_bf16) {
-                    const uint4 *row = reinterpret_cast<const uint4 *>(sw + lane * kStrideBf16Words);
-                    for (int i4 = 0; i4 < kD / 8; i4++) {
-                        const uint4 w4 = row[i4];
-                        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+        {
+            const int j = cur.j0 + lane;
+            const bool norm = lane < cur.nr && (j < p.n_head ? p.q_gamma != nullptr : (j < n_qk && p.k_gamma != nullptr));
+            if (norm) {
+                // the row's eight partials, read in a lane-rotated order (conflict-free 16-byte reads)
+                double ps[8];
+                uint32_t ms[8];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int q = (k + (lane >> 1)) & 3;
+                    const double2 d2 = *reinterpret_cast<const double2 *>(part_sum + lane * 8 + 2 * q);
+                    ps[2 * k] = d2.x, ps[2 * k + 1] = d2.y;
+                }
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const int q = (k + (lane >> 2)) & 1;
+                    const uint4 m4 = *reinterpret_cast<const uint4 *>(part_min + lane * 8 + 4 * q);
+                    ms[4 * k] = m4.x, ms[4 * k + 1] = m4.y, ms[4 * k + 2] = m4.z, ms[4 * k + 3] = m4.w;
+                }
+                const double sum = __dadd_rn(__dadd_rn(__dadd_rn(ps[0], ps[1]), __dadd_rn(ps[2], ps[3])),
+                                             __dadd_rn(__dadd_rn(ps[4], ps[5]), __dadd_rn(ps[6], ps[7])));
+                int fx;  // biased exponent field of the smallest |x|
+                if constexpr (kBf16) {
+                    uint32_t m = min_abs_bf16x2(min_abs_bf16x2(min_abs_bf16x2(ms[0], ms[1]), min_abs_bf16x2(ms[2], ms[3])),
+                                                min_abs_bf16x2(min_abs_bf16x2(ms[4], ms[5]), min_abs_bf16x2(ms[6], ms[7])));
+                    m &= 0x7fff7fffu;
+                    fx = (int) (min(m & 0xffffu, m >> 16) >> 7);
+                } else {
+                    fx = (int) (min(min(min(ms[0], ms[1]), min(ms[2], ms[3])), min(min(ms[4], ms[5]), min(ms[6], ms[7]))) >> 23);
+                }
+                const int fs = (int) ((uint32_t) __double2hiint(sum) >> 20);  // biased exponent of sum * 2^-896
+                // unscaled: fs - 127 = floor(log2(total)); the bound 2^(2e + 53 - sig) with e = fx - 127
+                double mean;
+                if (fx >= 64 && fs < 255 && fs < 2 * fx - 74 - sig) {
+                    mean = __dmul_rn(sum, 0x1p889);  // * 2^896 / 128
+                } else {
+                    double seq = 0.0;
+                    const uint8_t *row = buf + lane * row_bytes;
+                    if constexpr (kBf16) {
+                        const uint32_t *w = reinterpret_cast<const uint32_t *>(row);
+                        for (int i = 0; i < kD / 2; i++) {
+                            const float a = __uint_as_float(w[i] << 16), bb = __uint_as_float(w[i] & 0xffff0000u);
+                            seq = __dadd_rn(seq, (double) __fmul_rn(a, a));
+                            seq = __dadd_rn(seq, (double) __fmul_rn(bb, bb));
+                        }
+                    } else {
+                        const float *f = reinterpret_cast<const float *>(row);
+                        for (int i = 0; i < kD; i++) seq = __dadd_rn(seq, (double) __fmul_rn(f[i], f[i]));
+                    }
+                    mean = __dmul_rn(seq, 1.0 / kD);
+                }
+                my_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(mean), p.eps)));
+            }
+        }
+
+        // cos / sin of this lane's pairs 8c..8c+7 at the token's position, for the whole group,
+        // as packed pairs (C, S of pairs 2k, 2k+1)
+        uint64_t Cp[4], Sp[4];
+        if (cur.j0 < n_qk && pos_ok) {
+            const float4 *cs = reinterpret_cast<const float4 *>(buf + rope_off) + 4 * c;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 t = cs[q];
+                Cp[q] = f2(t.x, t.z);
+                Sp[q] = f2(t.y, t.w);
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++) Cp[q] = Sp[q] = 0;
+        }
+
+        // Write out. Q / K rows: RMSNorm scale and weight, then the rotation, on packed f32 pairs
+        // of neighbouring elements (A = (a_e, a_e+1) of the first half, B of the second half):
+        //   A' = A * C - B * S,  B' = A * S + B * C   (C, S: cos / sin of pairs e, e+1)
+        // every multiply and add rounded on its own, as ggml's CPU rope computes them (the
+        // differences and sums are scalar, see below). V rows are converted and stored as read.
+        // One loop per kind over the group's rows of that kind; a row is written only when its
+        // index is valid: Q needs the position, K the position and the cell, V the cell.
+        auto write_rows = [&](auto kind, int lo, int hi, int64_t dst_row0) {
+            constexpr int K = decltype(kind)::value;  // 0 Q, 1 K, 2 V
+            const bool norm = K == 0 ? p.q_gamma != nullptr : K == 1 ? p.k_gamma != nullptr : false;
+            const float *gm = s_gamma + (K == 0 ? 0 : kD);
+            for (int r0 = lo; r0 < hi; r0 += 4) {
+                const int r = r0 + sub;
+                const float scale = __shfl_sync(0xffffffffu, my_scale, r < hi ? r : lo);
+                if (r >= hi) continue;
+                float x[16];
+                const uint8_t *row = buf + r * row_bytes;
+                if constexpr (kBf16) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(row + h * 128 + c * 16);
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
-                            const float a = __uint_as_float(ws[e] << 16), b = __uint_as_float(ws[e] & 0xffff0000u);
-                            sum = __dadd_rn(sum, (double) __fmul_rn(a, a));
-                            sum = __dadd_rn(sum, (double) __fmul_rn(b, b));
+                            x[8 * h + 2 * e] = __uint_as_float(ws[e] << 16);
+                            x[8 * h + 2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
                         }
                     }
                 } else {
-                    const float4 *row = reinterpret_cast<const float4 *>(sf + lane * kStrideF32);
-                    for (int i4 = 0; i4 < kD / 4; i4++) {
-                        const float4 v4 = row[i4];
-                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.x, v4.x));
-                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.y, v4.y));
-                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.z, v4.z));
-                        sum = __dadd_rn(sum, (double) __fmul_rn(v4.w, v4.w));
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            const float4 v = *reinterpret_cast<const float4 *>(row + (h * 64 + c * 8 + q * 4) * 4);
+                            x[8 * h + 4 * q] = v.x;
+                            x[8 * h + 4 * q + 1] = v.y;
+                            x[8 * h + 4 * q + 2] = v.z;
+                            x[8 * h + 4 * q + 3] = v.w;
+                        }
+                }
+                float o[16];
+                if constexpr (K == 2) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] = x[i];
+                } else {
+                    uint64_t A[4], B[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        A[k] = f2(x[2 * k], x[2 * k + 1]);
+                        B[k] = f2(x[8 + 2 * k], x[9 + 2 * k]);
+                    }
+                    if (norm) {
+                        const uint64_t sc = f2(scale, scale);
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            const float4 ga = *reinterpret_cast<const float4 *>(gm + goff[q]);      // first half
+                            const float4 gb = *reinterpret_cast<const float4 *>(gm + goff[2 + q]);  // second half
+                            A[2 * q] = mul2(mul2(A[2 * q], sc), f2(ga.x, ga.y));
+                            A[2 * q + 1] = mul2(mul2(A[2 * q + 1], sc), f2(ga.z, ga.w));
+                            B[2 * q] = mul2(mul2(B[2 * q], sc), f2(gb.x, gb.y));
+                            B[2 * q + 1] = mul2(mul2(B[2 * q + 1], sc), f2(gb.z, gb.w));
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        // packed products, scalar differences and sums: ptxas contracts a packed
+                        // multiply feeding a packed add or subtract into a packed FMA (one rounding
+                        // instead of two), even when the product is written as fma(a, b, -0), but
+                        // not into a scalar one
+                        float ac0, ac1, bs0, bs1, as0, as1, bc0, bc1;
+                        uf2(mul2(A[k], Cp[k]), ac0, ac1);
+                        uf2(mul2(B[k], Sp[k]), bs0, bs1);
+                        uf2(mul2(A[k], Sp[k]), as0, as1);
+                        uf2(mul2(B[k], Cp[k]), bc0, bc1);
+                        o[2 * k] = __fsub_rn(ac0, bs0);
+                        o[2 * k + 1] = __fsub_rn(ac1, bs1);
+                        o[8 + 2 * k] = __fadd_rn(as0, bc0);
+                        o[9 + 2 * k] = __fadd_rn(as1, bc1);
                     }
                 }
-                const float mean = __double2float_rn(__ddiv_rn(sum, (double) kD));
-                my_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-            }
-        }
-
-        // Lane r prepares row r's output: kind (0 Q, 1 K, 2 V, 3 nothing to write: a bad cell or
-        // position, reported here), destination, and which prefetched RoPE row it uses.
-        int my_kind = 3;
-        int64_t my_dst = 0;  // element offset into q_out / k_cache / v_cache
-        if (lane < nr) {
-            if (my_j >= p.n_head && (my_cell < 0 || my_cell >= p.n_cells)) {
-                if (my_j == p.n_head) report(p.status, kStatusBadIndex, kSiteAppendCell, (int) my_t);
-            } else if (my_j >= n_qk) {
-                my_kind = 2;
-                my_dst = (my_cell * p.n_head_kv + (my_j - n_qk)) * kD;
-            } else if (my_pos < 0 || my_pos >= p.rope_n_pos) {
-                if (my_j == 0) report(p.status, kStatusBadIndex, kSiteAppendPos, (int) my_t);
-            } else if (my_j < p.n_head) {
-                my_kind = 0;
-                my_dst = (my_t * p.n_head + my_j) * kD;
-            } else {
-                my_kind = 1;
-                my_dst = (my_cell * p.n_head_kv + (my_j - p.n_head)) * kD;
-            }
-        }
-        const int my_u = (int) (my_t - t_first);  // RoPE slot (>= 4: loaded in the loop)
-
-        // Write out: lanes 8s..8s+7 take row r0 + s, four rows per warp instruction; lane c = lane & 7
-        // owns NEOX pairs [8c, 8c+8) - elements 8c..8c+7 and 64+8c..64+8c+7 - moved as 16-byte
-        // vectors. Branch-free arithmetic per element (selects).
-        const int sub = lane >> 3, c = lane & 7;
-        int goff[4], coff[4];  // float offsets of this lane's gamma chunks and staged RoPE chunks
+                const int64_t at = dst_row0 + r * kD + c * 8;
+                if constexpr (K == 0 && !kQ16) {
+                    float *d = reinterpret_cast<float *>(p.q_out) + at;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            goff[q] = gamma_slot(2 * c + (q & 1) + 16 * (q >> 1)) * 4;
-            coff[q] = rope_slot(4 * c + q) * 4;
-        }
-        for (int r0 = 0; r0 < nr; r0 += 4) {
-            const int r = r0 + sub;
-            const int from = r < nr ? r : r0;
-            const int kind = __shfl_sync(0xffffffffu, my_kind, from);
-            const int64_t dst = __shfl_sync(0xffffffffu, my_dst, from);
-            const float scale = __shfl_sync(0xffffffffu, my_scale, from);
-            const int u = __shfl_sync(0xffffffffu, my_u, from);
-            const int pos = __shfl_sync(0xffffffffu, my_pos, from);
-            if (r >= nr || kind == 3) continue;  // no warp collective below
-            float x[16];
-            if (p.in_bf16) {
-                const uint8_t *row = stage + r * (kStrideBf16Words * 4);
+                    for (int h = 0; h < 2; h++)
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(row + h * 128 + c * 16);
-                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                        for (int q = 0; q < 2; q++)
+                            *reinterpret_cast<float4 *>(d + h * 64 + q * 4) =
+                                make_float4(o[8 * h + 4 * q], o[8 * h + 4 * q + 1], o[8 * h + 4 * q + 2], o[8 * h + 4 * q + 3]);
+                } else {
+                    __half *d = (K == 0 ? reinterpret_cast<__half *>(p.q_out) : K == 1 ? p.k_cache : p.v_cache) + at;
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        x[8 * h + 2 * e] = __uint_as_float(ws[e] << 16);
-                        x[8 * h + 2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
-                    }
-                }
-            } else {
-                const float *row = sf + r * kStrideF32;
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        const float4 v = *reinterpret_cast<const float4 *>(row + h * 64 + c * 8 + q * 4);
-                        x[8 * h + 4 * q] = v.x;
-                        x[8 * h + 4 * q + 1] = v.y;
-                        x[8 * h + 4 * q + 2] = v.z;
-                        x[8 * h + 4 * q + 3] = v.w;
-                    }
-            }
-            const bool is_q = kind == 0, is_v = kind == 2;
-            const bool normed = is_q ? p.q_gamma != nullptr : p.k_gamma != nullptr;
-            const float *g = s_gamma + (is_q ? 0 : kD);
-            // (cos, sin) of pairs 8c..8c+7: staged for the group's first tokens, else from the table
-            // (Q / K rows have a checked position; V rows use none of it)
-            const bool staged = u < kCsTokens || is_v;
-            const float *csr = u < kCsTokens ? s_cs + u * kD
-                                             : is_v ? s_cs
-                                                    : reinterpret_cast<const float *>(p.rope + (int64_t) pos * (kD / 2));
-            // gamma of elements 8c..8c+7 and 64+8c..64+8c+7; (cos, sin) of pairs 8c..8c+7 (pair
-            // e: elements e and 64 + e of the lane's slice), as 16-byte reads
-            float gm[16], cs[16];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const float4 gv = *reinterpret_cast<const float4 *>(g + goff[q]);
-                gm[4 * q] = gv.x;
-                gm[4 * q + 1] = gv.y;
-                gm[4 * q + 2] = gv.z;
-                gm[4 * q + 3] = gv.w;
-                const float4 cv = *reinterpret_cast<const float4 *>(csr + (staged ? coff[q] : 16 * c + 4 * q));
-                cs[4 * q] = cv.x;
-                cs[4 * q + 1] = cv.y;
-                cs[4 * q + 2] = cv.z;
-                cs[4 * q + 3] = cv.w;
-            }
-            float o[16];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                float a = x[e], b = x[8 + e];
-                const float ya = __fmul_rn(__fmul_rn(a, scale), gm[e]);
-                const float yb = __fmul_rn(__fmul_rn(b, scale), gm[8 + e]);
-                a = normed ? ya : a;
-                b = normed ? yb : b;
-                const float cx = cs[2 * e], sy = cs[2 * e + 1];
-                const float oa = __fsub_rn(__fmul_rn(a, cx), __fmul_rn(b, sy));
-                const float ob = __fadd_rn(__fmul_rn(a, sy), __fmul_rn(b, cx));
-                o[e] = is_v ? x[e] : oa;  // V rows are stored as read
-                o[8 + e] = is_v ? x[8 + e] : ob;
-            }
-            if (is_q && !p.q_out_f16) {
-                float *d = reinterpret_cast<float *>(p.q_out) + dst;
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int q = 0; q < 2; q++)
-                        *reinterpret_cast<float4 *>(d + h * 64 + c * 8 + q * 4) =
-                            make_float4(o[8 * h + 4 * q], o[8 * h + 4 * q + 1], o[8 * h + 4 * q + 2], o[8 * h + 4 * q + 3]);
-            } else {
-                __half *d = (is_q ? reinterpret_cast<__half *>(p.q_out) : is_v ? p.v_cache : p.k_cache) + dst;
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    uint4 v;
-                    uint32_t *vw = reinterpret_cast<uint32_t *>(&v);
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const __half2 hh = h2(o[8 * h + 2 * e], o[8 * h + 2 * e + 1]);
-                        vw[e] = *reinterpret_cast<const uint32_t *>(&hh);
-                    }
-                    *reinterpret_cast<uint4 *>(d + h * 64 + c * 8) = v;
+                    for (int h = 0; h < 2; h++)
+                        *reinterpret_cast<uint4 *>(d + h * 64) =
+                            make_uint4(f16x2_bits(o[8 * h], o[8 * h + 1]), f16x2_bits(o[8 * h + 2], o[8 * h + 3]),
+                                       f16x2_bits(o[8 * h + 4], o[8 * h + 5]), f16x2_bits(o[8 * h + 6], o[8 * h + 7]));
                 }
             }
+        };
+        // group rows [0, nq) are Q rows, [nq, nqk) K rows, [nqk, nr) V rows
+        const int nq = max(0, min(p.n_head - cur.j0, cur.nr));
+        const int nqk = max(0, min(n_qk - cur.j0, cur.nr));
+        const int64_t kv_row0 = (cur.cell * p.n_head_kv + cur.j0) * kD;  // + (j - Hq or j - Hq - Hkv) rows
+        if (pos_ok) {
+            write_rows(std::integral_constant<int, 0>(), 0, nq, (cur.t * p.n_head + cur.j0) * kD);
+            if (cell_ok) write_rows(std::integral_constant<int, 1>(), nq, nqk, kv_row0 - (int64_t) p.n_head * kD);
         }
-        __syncwarp();
+        if (cell_ok) write_rows(std::integral_constant<int, 2>(), nqk, cur.nr, kv_row0 - (int64_t) n_qk * kD);
+        __syncwarp();  // buffer b is free for the group two steps ahead
+        cur = nxt;
+        nxt = nxt2;
     }
 }
 

@@ -34,8 +34,10 @@ struct DeviceInfo {
     // Dynamic shared-memory limits raised so far on this device, per kernel (ensure_smem).
     size_t decode_smem = 0;
     size_t prefill_smem = 0;
-    size_t append_smem = 0;
+    size_t append_smem[4] = {};  // per kv_append instantiation (append_kernel)
     size_t gemm_smem = 0;
+    // Resident kv_append CTAs per SM, per [instantiation][rows per group / 4]; 0 = not asked yet.
+    int append_occ[4][append::kMaxGroupRows / 4 + 1] = {};
 };
 
 DeviceInfo g_devices[kMaxDevices];
@@ -236,6 +238,34 @@ int lstk_cuda_set_wait_policy(uint64_t pipeline_wait_ns, const int32_t *start_fl
     return clear_error();
 }
 
+typedef void (*AppendKernel)(append::Params);
+// The kv_append instantiation for bf16 / f32 inputs and an f16 / f32 Q output; index bf16 * 2 + q16.
+static AppendKernel append_kernel(int idx) {
+    static const AppendKernel k[4] = {append::kv_append_kernel<false, false>, append::kv_append_kernel<false, true>,
+                                      append::kv_append_kernel<true, false>, append::kv_append_kernel<true, true>};
+    return k[idx];
+}
+
+// Resident CTAs per SM of kv_append instantiation `idx` for groups of `rows` rows (two stage
+// buffers per warp), asked of the runtime once per device and shape. Returns the count (>= 1) or
+// a negative error code.
+static int append_occupancy(DeviceInfo *dev, int idx, int rows) {
+    int &slot = dev->append_occ[idx][rows / 4];
+    {
+        std::lock_guard<std::mutex> lock(g_devices_mu);
+        if (slot > 0) return slot;
+    }
+    const int smem = append::kGammaBytes + append::kWarps * 2 * append::buf_bytes(rows, idx >= 2);
+    int n = 0;
+    const cudaError_t e =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, append_kernel(idx), append::kWarps * 32, (size_t) smem);
+    if (e != cudaSuccess) return set_error(LSTK_ERR_CUDA, cuda_msg("cudaOccupancyMaxActiveBlocksPerMultiprocessor(kv_append)", e));
+    if (n < 1) return set_error(LSTK_ERR_CUDA, "kv_append_kernel: no CTA fits on an SM");
+    std::lock_guard<std::mutex> lock(g_devices_mu);
+    slot = n;
+    return n;
+}
+
 int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
                         const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
                         int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
@@ -291,28 +321,37 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     p.q_out = q_out;
     p.q_out_f16 = q_out_dtype == LSTK_DTYPE_F16;
     p.status = dev->status;
-    const int64_t rows = (int64_t) n_tokens * (n_head + 2 * layout->n_head_kv);
-    // Rows per warp: 32 when there are enough rows for two full waves of such groups, fewer for
-    // short (decode-step) appends, which are bound by one warp's chain of dependent steps.
-    const int64_t full = (int64_t) dev->n_sms * append::kWarps * 3 * 2;  // 3 CTAs per SM, 2 waves
-    const int max_rpw = (in_dtype == LSTK_DTYPE_F32 || q_out_dtype == LSTK_DTYPE_F32) ? 16 : 32;
-    p.rows_per_warp = std::min(max_rpw, rows >= full * 32 ? 32 : rows >= full * 16 ? 16 : 8);
-    const int64_t groups = (rows + p.rows_per_warp - 1) / p.rows_per_warp;
-    const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * 16);
+    // Rows per group: the largest (fewest steps per row) that still gives the resident warps a
+    // couple of groups each (the next group's copies overlap the current one); short appends
+    // (decode steps), bound by one warp's chain of dependent steps, go down to one step per group.
+    const int kidx = (p.in_bf16 ? 2 : 0) + (p.q_out_f16 ? 1 : 0);
+    if ((rc = ensure_smem(&dev->append_smem[kidx], append_kernel(kidx), append::kSmemBytes,
+                          "cudaFuncSetAttribute(kv_append)")))
+        return rc;
+    const int R = n_head + 2 * layout->n_head_kv;
+    int G = 4, gpt = (R + 3) / 4, per_sm = 0;
+    for (int cand = p.in_bf16 ? append::kMaxGroupRows : append::kMaxGroupRows / 2; cand >= 4; cand /= 2) {
+        gpt = (R + cand - 1) / cand;
+        G = ((R + gpt - 1) / gpt + 3) / 4 * 4;  // the token's rows spread evenly over its groups
+        if ((per_sm = append_occupancy(dev, kidx, G)) < 0) return per_sm;
+        if ((int64_t) n_tokens * gpt >= (int64_t) dev->n_sms * per_sm * append::kWarps * 2) break;
+    }
+    p.group_rows = G;
+    p.groups_per_token = gpt;
+    const int smem_bytes = append::kGammaBytes + append::kWarps * 2 * append::buf_bytes(G, p.in_bf16 != 0);
+    const int64_t groups = (int64_t) n_tokens * gpt;
+    const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * per_sm);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    if ((rc = ensure_smem(&dev->append_smem, append::kv_append_kernel, append::kSmemBytes,
-                          "cudaFuncSetAttribute(kv_append)")))
-        return rc;
     cfg.gridDim = dim3((unsigned) blocks);
     cfg.blockDim = dim3(append::kWarps * 32);
-    cfg.dynamicSmemBytes = append::kSmemBytes;
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return launch_pdl_check(cudaLaunchKernelEx(&cfg, append::kv_append_kernel, p), "kv_append_kernel");
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, append_kernel(kidx), p), "kv_append_kernel");
 }
 
 // Launches the split kernel and the combine kernel with programmatic stream serialization:

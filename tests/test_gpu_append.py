@@ -149,16 +149,18 @@ def test_append_groups_spanning_many_tokens(dtype):
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_append_rms_sum_hard_rows(dtype):
-    """Rows that stress the sequential double sum of squares: values spanning many orders of
-    magnitude (where summation order changes the rounding), denormal squares next to normal ones,
-    a single nonzero, and zeros, in f32 and bf16. Pages and Q must equal the oracle's."""
+    """Rows that stress the double sum of squares: values spanning many orders of magnitude (where
+    summation order changes the rounding, so the kernel must sum in index order), denormal squares
+    next to normal ones, a single nonzero, zeros, squares that overflow f32 (an infinite sum),
+    squares just below that, and a moderate spread near the bound under which any order of
+    summation is exact, in f32 and bf16. Pages and Q must equal the oracle's."""
     rng = np.random.default_rng(11)
     T, Hq, Hkv, D = 64, 16, 8, 128
     R = Hq + 2 * Hkv
 
     def rows(n):
         out = rng.standard_normal((n, D)).astype(np.float32) * 2
-        kinds = rng.integers(0, 5, n)
+        kinds = rng.integers(0, 8, n)
         for r in range(n):
             if kinds[r] == 1:  # magnitudes from 1e-20 to 1e3: the exact bound fails
                 out[r] *= (10.0 ** rng.uniform(-20, 3, D)).astype(np.float32)
@@ -169,6 +171,12 @@ def test_append_rms_sum_hard_rows(dtype):
                 out[r, rng.integers(D)] = 7.5
             elif kinds[r] == 4:  # all zeros
                 out[r] = 0
+            elif kinds[r] == 5:  # squares overflow f32: ggml's sum is inf, the scale 0
+                out[r, rng.integers(D)] = 3e20
+            elif kinds[r] == 6:  # squares up to ~1e36, their sum finite
+                out[r] *= 3e17
+            elif kinds[r] == 7:  # magnitudes over 2^-12..2^0: near the exact-summation bound
+                out[r] *= (2.0 ** rng.uniform(-12, 0, D)).astype(np.float32)
         return out
 
     q_in = rows(T * Hq).reshape(T, Hq, D)
