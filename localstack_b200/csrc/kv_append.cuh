@@ -38,7 +38,15 @@ constexpr int kGammaBytes = 2 * kD * 4;
 // One stage buffer: the group's rows back to back in the input type, then the RoPE row (64
 // (cos, sin) pairs). Rows are 256 or 512 bytes, so every piece starts 16-byte aligned.
 __host__ __device__ constexpr int buf_bytes(int group_rows, bool bf16) { return group_rows * kD * (bf16 ? 2 : 4) + kD * 4; }
-constexpr int kSmemBytes = kGammaBytes + kWarps * 2 * (kMaxGroupRows * kD * 2 + kD * 4);  // the largest launch
+// A warp's shared memory: two stage buffers, then per row the eight partial sums of squares
+// (double) and the eight smallest |x| (32 bits) of its lanes.
+__host__ __device__ constexpr int warp_bytes(int group_rows, bool bf16) {
+    return 2 * buf_bytes(group_rows, bf16) + group_rows * 8 * (8 + 4);
+}
+__host__ __device__ constexpr int smem_bytes(int group_rows, bool bf16) {
+    return kGammaBytes + kWarps * warp_bytes(group_rows, bf16);
+}
+constexpr int kSmemBytes = smem_bytes(kMaxGroupRows, true);  // the largest launch
 
 struct Params {
     const void *q_in;
@@ -115,8 +123,6 @@ template <bool kBf16, bool kQ16>
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t s_bar[kWarps][2];    // per warp, per stage buffer
-    __shared__ double s_part_sum[kWarps][kMaxGroupRows * 8];  // per row, the sums of its eight lanes' squares
-    __shared__ uint32_t s_part_min[kWarps][kMaxGroupRows * 8];  // and their smallest |x|
     float *s_gamma = reinterpret_cast<float *>(smem);     // [2][128]: q_gamma, k_gamma (1 when absent)
 
     // Inputs may come from the previous kernel in the stream (programmatic dependent launch);
@@ -145,7 +151,9 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     const int row_bytes = kD * es;
     const int rope_off = G * row_bytes;
     const int bbytes = rope_off + kD * 4;
-    uint8_t *bufs = smem + kGammaBytes + warp * 2 * bbytes;
+    uint8_t *bufs = smem + kGammaBytes + warp * warp_bytes(G, kBf16);
+    double *part_sum = reinterpret_cast<double *>(bufs + 2 * bbytes);              // [G][8]
+    uint32_t *part_min = reinterpret_cast<uint32_t *>(bufs + 2 * bbytes + G * 64);  // [G][8]
     const int64_t gstride = (int64_t) gridDim.x * kWarps;
 
     struct Group {  // token, its first row, rows, the token's position and cell
@@ -197,8 +205,6 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     int goff[4];  // float offsets of this lane's gamma chunks
 #pragma unroll
     for (int q = 0; q < 4; q++) goff[q] = gamma_slot(2 * c + (q & 1) + 16 * (q >> 1)) * 4;
-    double *part_sum = s_part_sum[warp];
-    uint32_t *part_min = s_part_min[warp];
     const int sig = kBf16 ? 16 : 24;  // significant bits of a square of an input value
 
     int64_t g = (int64_t) blockIdx.x * kWarps + warp;

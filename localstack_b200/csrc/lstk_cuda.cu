@@ -255,7 +255,7 @@ static int append_occupancy(DeviceInfo *dev, int idx, int rows) {
         std::lock_guard<std::mutex> lock(g_devices_mu);
         if (slot > 0) return slot;
     }
-    const int smem = append::kGammaBytes + append::kWarps * 2 * append::buf_bytes(rows, idx >= 2);
+    const int smem = append::smem_bytes(rows, idx >= 2);
     int n = 0;
     const cudaError_t e =
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, append_kernel(idx), append::kWarps * 32, (size_t) smem);
@@ -321,9 +321,10 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     p.q_out = q_out;
     p.q_out_f16 = q_out_dtype == LSTK_DTYPE_F16;
     p.status = dev->status;
-    // Rows per group: the largest (fewest steps per row) that still gives the resident warps a
-    // couple of groups each (the next group's copies overlap the current one); short appends
-    // (decode steps), bound by one warp's chain of dependent steps, go down to one step per group.
+    // Rows per group: the largest (fewest steps and groups per row) that keeps at least four CTAs
+    // (16 warps) resident per SM - the warps hide each other's latencies - and gives every resident
+    // warp a group; short appends (decode steps), bound by one warp's chain of dependent steps, go
+    // down to one step per group.
     const int kidx = (p.in_bf16 ? 2 : 0) + (p.q_out_f16 ? 1 : 0);
     if ((rc = ensure_smem(&dev->append_smem[kidx], append_kernel(kidx), append::kSmemBytes,
                           "cudaFuncSetAttribute(kv_append)")))
@@ -334,11 +335,11 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
         gpt = (R + cand - 1) / cand;
         G = ((R + gpt - 1) / gpt + 3) / 4 * 4;  // the token's rows spread evenly over its groups
         if ((per_sm = append_occupancy(dev, kidx, G)) < 0) return per_sm;
-        if ((int64_t) n_tokens * gpt >= (int64_t) dev->n_sms * per_sm * append::kWarps * 2) break;
+        if (per_sm >= 4 && (int64_t) n_tokens * gpt >= (int64_t) dev->n_sms * per_sm * append::kWarps) break;
     }
     p.group_rows = G;
     p.groups_per_token = gpt;
-    const int smem_bytes = append::kGammaBytes + append::kWarps * 2 * append::buf_bytes(G, p.in_bf16 != 0);
+    const int smem_bytes = append::smem_bytes(G, p.in_bf16 != 0);
     const int64_t groups = (int64_t) n_tokens * gpt;
     const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * per_sm);
     cudaLaunchAttribute attr[1];
