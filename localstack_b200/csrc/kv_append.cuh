@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     const int R = p.n_head + 2 * p.n_head_kv;
     const int n_qk = p.n_head + p.n_head_kv;
     const int G = p.group_rows, gpt = p.groups_per_token;
-    const int64_t n_groups = (int64_t) p.n_tokens * gpt;
+    const int n_groups = p.n_tokens * gpt;  // below 2^31 (checked by the launch)
     const int es = kBf16 ? 2 : 4;  // input element bytes
     const int row_bytes = kD * es;
     const int rope_off = G * row_bytes;
@@ -154,17 +154,27 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     uint8_t *bufs = smem + kGammaBytes + warp * warp_bytes(G, kBf16);
     double *part_sum = reinterpret_cast<double *>(bufs + 2 * bbytes);              // [G][8]
     uint32_t *part_min = reinterpret_cast<uint32_t *>(bufs + 2 * bbytes + G * 64);  // [G][8]
-    const int64_t gstride = (int64_t) gridDim.x * kWarps;
-
-    struct Group {  // token, its first row, rows, the token's position and cell
-        int64_t t, cell;
-        int j0, nr, pos;
+    // Groups g = blockIdx.x * kWarps + warp + k * gs, walked as (token, part) without dividing.
+    const int gs = gridDim.x * kWarps;
+    const int dq = gs / gpt, dr = gs - dq * gpt;
+    struct Cursor {
+        int g, t, part;
     };
-    auto locate = [&](int64_t g, Group &m) {
+    auto advance = [&](Cursor &k) {
+        k.g += gs;
+        k.t += dq;
+        k.part += dr;
+        if (k.part >= gpt) k.part -= gpt, k.t++;
+    };
+    struct Group {  // token, its first row, rows, the token's position and cell
+        int64_t cell;
+        int t, j0, nr, pos;
+    };
+    auto locate = [&](const Cursor &k, Group &m) {
         m.t = 0, m.cell = -1, m.j0 = 0, m.nr = 0, m.pos = -1;
-        if (g >= n_groups) return;
-        m.t = g / gpt;
-        m.j0 = (int) (g - m.t * gpt) * G;
+        if (k.g >= n_groups) return;
+        m.t = k.t;
+        m.j0 = k.part * G;
         m.nr = min(G, R - m.j0);
         m.pos = p.positions[m.t];
         m.cell = p.cells[m.t];
@@ -184,19 +194,19 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         uint32_t d = dst;
         if (j < p.n_head) {
             const int n = min(end, p.n_head) - j;
-            bulk_load(d, (const uint8_t *) p.q_in + (m.t * p.q_stride + (int64_t) j * kD) * es, (uint32_t) (n * row_bytes), bar);
+            bulk_load(d, (const uint8_t *) p.q_in + ((int64_t) m.t * p.q_stride + (int64_t) j * kD) * es, (uint32_t) (n * row_bytes), bar);
             d += n * row_bytes;
             j += n;
         }
         if (j < end && j < n_qk) {
             const int n = min(end, n_qk) - j;
-            bulk_load(d, (const uint8_t *) p.k_in + (m.t * p.k_stride + (int64_t) (j - p.n_head) * kD) * es,
+            bulk_load(d, (const uint8_t *) p.k_in + ((int64_t) m.t * p.k_stride + (int64_t) (j - p.n_head) * kD) * es,
                       (uint32_t) (n * row_bytes), bar);
             d += n * row_bytes;
             j += n;
         }
         if (j < end)
-            bulk_load(d, (const uint8_t *) p.v_in + (m.t * p.v_stride + (int64_t) (j - n_qk) * kD) * es,
+            bulk_load(d, (const uint8_t *) p.v_in + ((int64_t) m.t * p.v_stride + (int64_t) (j - n_qk) * kD) * es,
                       (uint32_t) ((end - j) * row_bytes), bar);
         if (rope) bulk_load(dst + rope_off, p.rope + (int64_t) m.pos * (kD / 2), kD * 4, bar);
     };
@@ -207,18 +217,22 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
     for (int q = 0; q < 4; q++) goff[q] = gamma_slot(2 * c + (q & 1) + 16 * (q >> 1)) * 4;
     const int sig = kBf16 ? 16 : 24;  // significant bits of a square of an input value
 
-    int64_t g = (int64_t) blockIdx.x * kWarps + warp;
+    const int g0 = blockIdx.x * kWarps + warp;
+    Cursor ahead = {g0, g0 / gpt, g0 % gpt};  // two groups ahead of the current one, once started
     Group cur, nxt, nxt2;
-    locate(g, cur);
-    locate(g + gstride, nxt);
-    if (g < n_groups) issue(cur, 0);
+    locate(ahead, cur);
+    advance(ahead);
+    locate(ahead, nxt);
+    advance(ahead);
+    if (g0 < n_groups) issue(cur, 0);
     uint32_t parity = 0;  // bit b: parity of buffer b's next completion
-    for (int b = 0; g < n_groups; g += gstride, b ^= 1) {
-        locate(g + 2 * gstride, nxt2);  // used two groups from now
-        const bool more = g + gstride < n_groups;
+    for (int b = 0, g = g0; g < n_groups; g += gs, b ^= 1) {
+        locate(ahead, nxt2);  // used two groups from now
+        advance(ahead);
+        const bool more = g + gs < n_groups;
         if (more) issue(nxt, b ^ 1);
         if (!mbar_wait_bounded(smem_u32(&s_bar[warp][b]), (parity >> b) & 1u, nullptr)) {
-            report(p.status, kStatusTimeout, kSiteAppendWait, (int) g);
+            report(p.status, kStatusTimeout, kSiteAppendWait, g);
             // leave no copy in flight into this CTA's shared memory
             mbar_wait_bounded(smem_u32(&s_bar[warp][b]), (parity >> b) & 1u, nullptr);
             if (more) mbar_wait_bounded(smem_u32(&s_bar[warp][b ^ 1]), (parity >> (b ^ 1)) & 1u, nullptr);
@@ -229,8 +243,8 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         const bool pos_ok = cur.pos >= 0 && cur.pos < p.rope_n_pos;
         const bool cell_ok = cur.cell >= 0 && cur.cell < p.n_cells;
         if (lane == 0 && cur.j0 == 0) {  // once per token
-            if (!pos_ok) report(p.status, kStatusBadIndex, kSiteAppendPos, (int) cur.t);
-            if (!cell_ok) report(p.status, kStatusBadIndex, kSiteAppendCell, (int) cur.t);
+            if (!pos_ok) report(p.status, kStatusBadIndex, kSiteAppendPos, cur.t);
+            if (!cell_ok) report(p.status, kStatusBadIndex, kSiteAppendCell, cur.t);
         }
 
         // ggml rms_norm sum of each Q / K row's squares (f32 squares added in double in index
@@ -347,7 +361,7 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
                     }
                     mean = __dmul_rn(seq, 1.0 / kD);
                 }
-                my_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(mean), p.eps)));
+                my_scale = __frcp_rn(__fsqrt_rn(__fadd_rn(__double2float_rn(mean), p.eps)));
             }
         }
 
@@ -378,6 +392,7 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
             constexpr int K = decltype(kind)::value;  // 0 Q, 1 K, 2 V
             const bool norm = K == 0 ? p.q_gamma != nullptr : K == 1 ? p.k_gamma != nullptr : false;
             const float *gm = s_gamma + (K == 0 ? 0 : kD);
+#pragma unroll 2
             for (int r0 = lo; r0 < hi; r0 += 4) {
                 const int r = r0 + sub;
                 const float scale = __shfl_sync(0xffffffffu, my_scale, r < hi ? r : lo);
@@ -471,7 +486,7 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
         const int nqk = max(0, min(n_qk - cur.j0, cur.nr));
         const int64_t kv_row0 = (cur.cell * p.n_head_kv + cur.j0) * kD;  // + (j - Hq or j - Hq - Hkv) rows
         if (pos_ok) {
-            write_rows(std::integral_constant<int, 0>(), 0, nq, (cur.t * p.n_head + cur.j0) * kD);
+            write_rows(std::integral_constant<int, 0>(), 0, nq, ((int64_t) cur.t * p.n_head + cur.j0) * kD);
             if (cell_ok) write_rows(std::integral_constant<int, 1>(), nq, nqk, kv_row0 - (int64_t) p.n_head * kD);
         }
         if (cell_ok) write_rows(std::integral_constant<int, 2>(), nqk, cur.nr, kv_row0 - (int64_t) n_qk * kD);

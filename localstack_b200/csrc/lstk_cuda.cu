@@ -342,6 +342,8 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     const int smem_bytes = append::smem_bytes(G, p.in_bf16 != 0);
     const int64_t groups = (int64_t) n_tokens * gpt;
     const int64_t blocks = std::min<int64_t>((groups + append::kWarps - 1) / append::kWarps, (int64_t) dev->n_sms * per_sm);
+    if (groups + 3 * blocks * append::kWarps >= INT32_MAX)  // the kernel walks groups in 32-bit indices
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: too many rows for one call");
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
