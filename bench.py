@@ -824,9 +824,10 @@ def config4_chunk(L, dev, r, world, ctx=131072):
 def config4_split(L, dev, world):
     """Config 4 over all ranks: one 131072-token context whose pages are split into `world`
     contiguous chunks (chunk r on rank r); per step every rank decodes its chunk and the partials
-    are exchanged and merged on every rank. Timed for both exchanges: "p2p" (one kernel: peer
-    stores into every rank's mailbox over NVLink, flag wait, merge) and "collective" (NCCL
-    all-gather of [O | lse] records + merge kernel). One step is captured in a CUDA graph; L2 is
+    are exchanged and merged on every rank. Timed for three exchanges: "fused" (the decode's
+    combine kernel itself stores each finished row into every rank's mailbox over NVLink, waits
+    for the row's flags and merges; the headline), "p2p" (the same protocol in a kernel of its
+    own after the decode) and "collective" (NCCL all-gather of [O | lse] records + merge kernel). One step is captured in a CUDA graph; L2 is
     flushed before each step (a chunk of 268 MB / world can fit in L2); time = max over ranks
     of the mean per-step time. After the timed replays every rank's merged output is checked
     against a one-GPU decode of the whole context (rank 0 rebuilds every chunk from its seed)."""
@@ -868,7 +869,7 @@ def config4_split(L, dev, world):
            "check": "every rank's merged output after the timed replays vs a one-GPU decode of the whole context "
                     "(|d| <= 2e-3 + 1e-2 |ref|), max over ranks"}
     ok_all = True
-    for exchange in ("p2p", "collective", "decode_only"):
+    for exchange in ("fused", "p2p", "collective", "decode_only"):
         dec = KvSplitDecode(1, HQ, HKV, dev, exchange="collective" if exchange == "decode_only" else exchange)
         if exchange == "decode_only":  # this rank's chunk alone: the part of the step that shrinks with R
             o_loc = torch.empty((1, HQ, D), device=dev)
@@ -910,7 +911,7 @@ def config4_split(L, dev, world):
             ok_all = ok_all and entry["within_tolerance"]
         dec.close()
         res[exchange] = entry
-    res["ms"], res["gbs"] = res["p2p"]["ms"], res["p2p"]["gbs"]
+    res["ms"], res["gbs"] = res["fused"]["ms"], res["fused"]["gbs"]
     res["outputs_match"] = ok_all
     if not ok_all and rank == 0:
         print("config4_split: merged output outside the tolerance of the one-GPU decode", file=sys.stderr)

@@ -219,6 +219,21 @@ int lstk_cuda_kv_release(const lstk_kv_pages *state, int32_t slot, int32_t keep,
  * same sequence of calls with the same n_rows; the
  * calls advance an epoch kept in the mailbox, so they can be replayed from a CUDA graph. */
 size_t lstk_cuda_mailbox_bytes(int32_t n_ranks, int64_t n_rows, int32_t head_dim);
+/* The decode of this rank's chunk and the exchange-merge in one call, without the separate merge
+ * launch: lstk_cuda_attn_decode's arguments, plus the mailboxes / rank / n_ranks / wait_ns of
+ * lstk_cuda_attn_exchange_merge (mailboxes sized for n_seqs * n_head rows). The decode's own
+ * combine kernel runs the exchange protocol on each output row as it finishes it, so out and
+ * lse_out receive the rows merged over all ranks. lse_out is required (it also carries the
+ * local lse of rows the split kernel finishes alone). Limits: n_seqs * ceil(n_head_kv / 4) <= 64
+ * (one mailbox epoch counter per combine CTA; LSTK_ERR_CAPACITY beyond) and n_ranks <= 256. A
+ * mailbox set serves either this call or lstk_cuda_attn_exchange_merge, not both (they map rows
+ * to epoch counters differently). */
+int lstk_cuda_attn_decode_exchange(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                   const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                   const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                   int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
+                                   size_t workspace_bytes, int32_t n_ctas, void *const *mailboxes, int32_t rank,
+                                   int32_t n_ranks, uint64_t wait_ns, void *stream);
 int lstk_cuda_mailbox_alloc(size_t bytes, void **mailbox, void *ipc_handle);
 int lstk_cuda_mailbox_free(void *mailbox);
 int lstk_cuda_mailbox_open(const void *ipc_handle, void **peer_mailbox);

@@ -107,6 +107,8 @@ def lib():
     L.lstk_cuda_mailbox_open.argtypes = [_P, _P]
     L.lstk_cuda_mailbox_close.argtypes = [_P]
     L.lstk_cuda_attn_exchange_merge.argtypes = [_P, _I32, _I32, _P, _P, _I64, _I32, ctypes.c_uint64, _P, _P, _P]
+    L.lstk_cuda_attn_decode_exchange.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _P, _I32, _F, _P, _P,
+                                                 _P, _SZ, _I32, _P, _I32, _I32, ctypes.c_uint64, _P]
     L.lstk_cuda_attn_prefill_workspace_size.argtypes = [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32]
     L.lstk_cuda_attn_prefill_workspace_size.restype = _SZ
     L.lstk_cuda_attn_prefill.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _F, _P,

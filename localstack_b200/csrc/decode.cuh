@@ -26,6 +26,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exchange.cuh"
 
 namespace lstk {
 namespace decode {
@@ -482,7 +483,98 @@ struct CombineParams {
     const float *part_lse;
     float *out;
     float *lse_out;
+    // Exchange across ranks (decode_combine_kernel<true>): the mailboxes of the exchange-merge
+    // protocol (exchange.cuh) for n_seqs * n_head rows, this rank, the rank count, the flag-wait
+    // bound and the device status.
+    uint8_t *const *mailboxes;
+    int rank, n_ranks;
+    uint64_t wait_ns;
+    DeviceStatus *status;
 };
+
+// The end of a combine CTA's row: without an exchange, out / lse_out get the local row. With
+// one, the row's local (O, lse) goes through the exchange-merge protocol of exchange.cuh inside
+// this CTA - stored into slot `rank` of every rank's mailbox (plain peer stores), flagged with a
+// system-scope release, the R flags of the row awaited in the own mailbox (bounded by wait_ns;
+// on timeout the status records it and the row is zeros) - and out / lse_out get the merge of the
+// R records. The CTA's epoch counter is the mailbox header entry of its linear index, so the
+// calls replay from a CUDA graph. Every thread of the CTA calls this; o is read from threads
+// tid < kD, lse (natural log) from thread 0.
+template <bool kExchange>
+__device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, float o, float lse) {
+    const int tid = threadIdx.x;
+    if constexpr (!kExchange) {
+        if (tid < kD) p.out[row * kD + tid] = o;
+        if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = lse;
+    } else {
+        __shared__ float o_s[kD + 1];  // the local row, then its lse
+        __shared__ int timed_out;
+        const int R = p.n_ranks;
+        const int64_t n_rows = (int64_t) p.n_seqs * p.n_head;
+        uint8_t *own = p.mailboxes[p.rank];
+        const int cta = (blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z;
+        uint32_t *my_epoch = reinterpret_cast<uint32_t *>(own) + cta;
+        const uint32_t epoch = *my_epoch + 1u;
+        const int bank = (int) (epoch & 1u);
+        const size_t rec_off = exchange::records_offset(R, n_rows);
+        const int64_t slot_stride = n_rows * (kD + 1);  // floats per (bank, source)
+        if (tid < kD) o_s[tid] = o;
+        if (tid == 0) o_s[kD] = lse, timed_out = 0;
+        __syncthreads();
+        for (int i = tid; i < R * (kD + 1); i += blockDim.x) {
+            const int r = i / (kD + 1), d = i - r * (kD + 1);
+            reinterpret_cast<float *>(p.mailboxes[r] + rec_off)[((int64_t) bank * R + p.rank) * slot_stride +
+                                                                 row * (kD + 1) + d] = o_s[d];
+        }
+        __syncthreads();
+        if (tid < R) {
+            exchange::st_release_sys(reinterpret_cast<uint32_t *>(p.mailboxes[tid] + exchange::flags_offset()) +
+                                         ((int64_t) bank * R + p.rank) * n_rows + row,
+                                     epoch);
+            const uint32_t *flag = reinterpret_cast<const uint32_t *>(own + exchange::flags_offset()) +
+                                   ((int64_t) bank * R + tid) * n_rows + row;
+            bool ok = exchange::ld_acquire_sys(flag) == epoch;
+            if (!ok) {
+                const uint64_t t0 = global_timer_ns();
+                for (uint32_t i = 1; i < (1u << 30); i++) {
+                    if (exchange::ld_acquire_sys(flag) == epoch) {
+                        ok = true;
+                        break;
+                    }
+                    if ((i & 63u) == 0 && global_timer_ns() - t0 > p.wait_ns) break;
+                }
+            }
+            if (!ok) {
+                timed_out = 1;
+                report(p.status, kStatusTimeout, kSiteExchangeWait, tid);
+            }
+        }
+        __syncthreads();
+        if (tid < kD) {
+            float v = 0.f, l = -INFINITY;
+            if (!timed_out) {
+                const float *base = reinterpret_cast<const float *>(own + rec_off) + (int64_t) bank * R * slot_stride +
+                                    row * (kD + 1);
+                float M = -INFINITY;
+                for (int r = 0; r < R; r++) M = fmaxf(M, __ldcv(base + r * slot_stride + kD));
+                if (M != -INFINITY) {
+                    float den = 0.f, acc = 0.f;
+                    for (int r = 0; r < R; r++) {
+                        const float wt = __expf(__ldcv(base + r * slot_stride + kD) - M);
+                        den += wt;
+                        acc += wt * __ldcv(base + r * slot_stride + tid);
+                    }
+                    v = acc / den;
+                    l = M + __logf(den);
+                }
+            }
+            p.out[row * kD + tid] = v;
+            if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = l;
+        }
+        __syncthreads();
+        if (tid == 0) *my_epoch = epoch;  // read by this CTA's successor in the next call
+    }
+}
 
 // One CTA per (sequence b, head group hg, KV head w of the group, query head n of its group):
 // the 128 dims of one output row. The row's partial pieces (one per CTA whose range touched the
@@ -493,6 +585,7 @@ struct CombineParams {
 constexpr int kCombineThreads = 256;
 constexpr int kCombineWarps = kCombineThreads / 32;
 
+template <bool kExchange>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const CombineParams p) {
     pdl_wait();  // the split grid's partials and prefix are complete and visible
     const int b = blockIdx.x, hg = blockIdx.y;
@@ -504,21 +597,24 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     const int32_t pb = p.prefix[b];
     const int np = p.prefix[b + 1] - pb;
     if (np == 0) {
-        if (tid < kD) p.out[out_row * kD + tid] = 0.f;
-        if (tid == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
+        finish_row<kExchange>(p, out_row, 0.f, -INFINITY);
         return;
     }
     const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
     const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
     const int c0 = cta_of(x0, P, p.grid);
     const int c1 = cta_of(x0 + np - 1, P, p.grid);
-    if (c0 == c1) return;  // the split kernel wrote this row directly
+    if (c0 == c1) {  // the split kernel wrote this row directly (with an exchange, its local row)
+        if constexpr (kExchange)
+            finish_row<true>(p, out_row, tid < kD ? p.out[out_row * kD + tid] : 0.f, p.lse_out[out_row]);
+        return;
+    }
     const int part_row = w * kMaxGroup + n;
     const int n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
     __shared__ float wt_s[kMaxCtas];
     __shared__ int row_s[kMaxCtas];
     __shared__ float red_max[kCombineWarps], red_sum[kCombineWarps];
-    __shared__ float acc_s[kCombineWarps][kD];
+    __shared__ __align__(16) float acc_s[kCombineWarps][kD];  // written as float4
     // Pass 1: piece i = CTA c0 + i. Its slot is 1 if the CTA's range began in an earlier
     // segment; an empty range (more CTAs than page-groups) contributes nothing.
     float mx = -INFINITY;
@@ -576,16 +672,15 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const C
     }
     reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
     __syncthreads();
+    float total = 0.f, o = 0.f;
     if (tid < kD) {
-        float total = 0.f, o = 0.f;
         for (int i = 0; i < kCombineWarps; i++) {
             total += red_sum[i];
             o += acc_s[i][tid];
         }
-        p.out[out_row * kD + tid] = total > 0.f ? o / total : 0.f;
-        if (tid == 0 && p.lse_out != nullptr)
-            p.lse_out[out_row] = total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY;
     }
+    finish_row<kExchange>(p, out_row, total > 0.f ? o / total : 0.f,
+                          total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY);
 }
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.

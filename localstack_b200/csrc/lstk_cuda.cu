@@ -360,8 +360,15 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
 // Launches the split kernel and the combine kernel with programmatic stream serialization:
 // each grid can be scheduled while its predecessor in the stream finishes, and waits for it
 // (pdl_wait) before reading anything it produced.
+// The cross-rank exchange fused into the combine (lstk_cuda_attn_decode_exchange).
+struct ExchangeSpec {
+    uint8_t *const *mailboxes;
+    int rank, n_ranks;
+    uint64_t wait_ns;
+};
+
 static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const decode::Params &p, int grid,
-                         size_t smem, cudaStream_t s) {
+                         size_t smem, cudaStream_t s, const ExchangeSpec *ex = nullptr) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -387,10 +394,18 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     c.part_lse = p.part_lse;
     c.out = p.out;
     c.lse_out = p.lse_out;
+    c.mailboxes = ex ? ex->mailboxes : nullptr;
+    c.rank = ex ? ex->rank : 0;
+    c.n_ranks = ex ? ex->n_ranks : 1;
+    c.wait_ns = ex ? ex->wait_ns : 0;
+    c.status = p.status;
     cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, decode::kPartRows);
     cfg.blockDim = dim3(decode::kCombineThreads);
     cfg.dynamicSmemBytes = 0;
-    return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_kernel, c), "decode_combine_kernel");
+    if (ex)
+        return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_kernel<true>, c),
+                                "decode_combine_kernel (exchange)");
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_kernel<false>, c), "decode_combine_kernel");
 }
 
 size_t lstk_cuda_attn_decode_workspace_size(int32_t n_seqs, int32_t n_head, int32_t n_head_kv, int32_t head_dim) {
@@ -405,7 +420,7 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
                         int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
                         int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, int32_t kv_begin,
                         int32_t kv_end, float scale, float *out, float *lse_out, void *workspace,
-                        size_t workspace_bytes, int32_t n_ctas, void *stream) {
+                        size_t workspace_bytes, int32_t n_ctas, void *stream, const ExchangeSpec *ex = nullptr) {
     int rc = check_layout(layout, "lstk_cuda_attn_decode");
     if (rc) return rc;
     const int hkv = layout->n_head_kv;
@@ -473,7 +488,7 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
                         16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
     if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel, smem, "cudaFuncSetAttribute(decode)")))
         return rc;
-    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
+    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream), ex);
 }
 
 int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
@@ -495,6 +510,29 @@ int lstk_cuda_attn_decode_partial(const lstk_kv_layout *layout, const void *k_ca
     return decode_range(layout, k_cache, v_cache, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq,
                         seq_lens, max_seq_len, kv_begin, kv_end, scale, out, lse_out, workspace, workspace_bytes,
                         n_ctas, stream);
+}
+
+int lstk_cuda_attn_decode_exchange(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache,
+                                   const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                                   const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                                   int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
+                                   size_t workspace_bytes, int32_t n_ctas, void *const *mailboxes, int32_t rank,
+                                   int32_t n_ranks, uint64_t wait_ns, void *stream) {
+    if (!mailboxes || !lse_out || n_ranks <= 0 || rank < 0 || rank >= n_ranks)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_exchange: bad mailboxes / rank / lse_out");
+    // One thread per source raises and awaits its flag; one mailbox epoch counter per combine CTA.
+    if (n_ranks > decode::kCombineThreads)
+        return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode_exchange: at most 256 ranks");
+    if (layout && layout->n_head_kv > 0 &&
+        (int64_t) n_seqs * ((layout->n_head_kv + decode::kHeadsPerGroup - 1) / decode::kHeadsPerGroup) *
+                decode::kPartRows >
+            exchange::kMaxCtas)
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_decode_exchange: too many sequences x KV heads for the mailbox");
+    const ExchangeSpec ex = {reinterpret_cast<uint8_t *const *>(mailboxes), rank, n_ranks,
+                             wait_ns ? wait_ns : 1000000000ull};
+    return decode_range(layout, k_cache, v_cache, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq,
+                        seq_lens, max_seq_len, 0, INT32_MAX, scale, out, lse_out, workspace, workspace_bytes, n_ctas,
+                        stream, &ex);
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,

@@ -8,23 +8,26 @@ attention node shards in two ways, both built here on the single-GPU C ABI:
   and runs the ordinary decode; nothing crosses GPUs on the data path.
 * One long sequence: its page list is cut into R contiguous chunks, chunk r's pages resident on
   rank r. Each rank decodes its chunk with lse_out, then the partials are exchanged and merged
-  by log-sum-exp, so the merged output is replicated on every rank. Two exchanges:
-  - "p2p" (default on GPUs): lstk_cuda_attn_exchange_merge stores each rank's rows straight into
-    every rank's mailbox over NVLink (CUDA IPC mappings set up once through the process group),
-    waits on per-row flags and merges, all in one kernel;
+  by log-sum-exp, so the merged output is replicated on every rank. Three exchanges:
+  - "fused": lstk_cuda_attn_decode_exchange - the decode's own combine kernel stores each row it
+    finishes straight into every rank's mailbox over NVLink (CUDA IPC mappings set up once
+    through the process group), waits on the row's flags and merges: no launch after the decode;
+  - "p2p": the same protocol in a kernel of its own (lstk_cuda_attn_exchange_merge) after the
+    decode;
   - "collective": one record [O (rows x D) | lse (rows)] per rank, all-gathered through the
     process group (NCCL on GPUs, gloo on CPUs) and merged with lstk_cuda_attn_merge straight
     out of the gathered buffer through the merge's part strides.
 """
 import ctypes
 import heapq
+import math
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
 from ._lib import check, lib
-from .attn import HEAD_DIM, DecodeWorkspace, _p, _stream, attn_decode, attn_merge
+from .attn import _DT, HEAD_DIM, DecodeWorkspace, _p, _stream, attn_decode, attn_merge, layout_of
 
 
 def lpt_partition(lengths, world):
@@ -84,8 +87,8 @@ class KvSplitDecode:
     lse in `self.lse`. Call close() on every rank before the process group goes away."""
 
     def __init__(self, n_seqs, n_head, n_head_kv, device, group=None, exchange="p2p", wait_ns=0):
-        if exchange not in ("p2p", "collective"):
-            raise ValueError("exchange must be 'p2p' or 'collective'")
+        if exchange not in ("fused", "p2p", "collective"):
+            raise ValueError("exchange must be 'fused', 'p2p' or 'collective'")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -140,6 +143,16 @@ class KvSplitDecode:
         self._own = None
 
     def __call__(self, k_cache, v_cache, q, block_tables, chunk_lens, scale=None, max_seq_len=0):
+        if self.exchange == "fused":
+            L = layout_of(k_cache)
+            if scale is None:
+                scale = 1.0 / math.sqrt(HEAD_DIM)
+            check(lib().lstk_cuda_attn_decode_exchange(
+                ctypes.byref(L), _p(k_cache), _p(v_cache), _p(q), _DT[q.dtype], self.n_seqs, self.n_head,
+                _p(block_tables), block_tables.shape[1], _p(chunk_lens), int(max_seq_len), float(scale), _p(self.out),
+                _p(self.lse), _p(self.ws.buf), self.ws.buf.numel(), 0, _p(self.mailboxes), self.rank, self.world,
+                self.wait_ns, _stream(None, q.device)))
+            return self.out
         o_loc, lse_loc = record_views(self.local, self.rows)
         attn_decode(k_cache, v_cache, q, block_tables, chunk_lens, scale, max_seq_len,
                     out=o_loc[0].view(self.n_seqs, self.n_head, HEAD_DIM),

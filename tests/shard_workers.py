@@ -109,14 +109,14 @@ def kv_split_nccl(rank, world, port, result_dir):
         args = (f16(kc), f16(vc), torch.from_numpy(q).to(dev), torch.from_numpy(_chunk_table(bt, s, e)).to(dev),
                 torch.tensor([n], dtype=torch.int32, device=dev), SCALE)
         ex = O.paged_attn(q, [0], [ctx - 1], kc, vc, bt, [ctx], SCALE, mode=O.MODE_EXACT)
-        for exchange in ("p2p", "collective"):
+        for exchange in ("fused", "p2p", "collective"):
             dec = KvSplitDecode(1, hq, hkv, dev, exchange=exchange)
             for _ in range(3):  # repeated calls: epochs / banks alternate
                 out = dec(*args)
             torch.cuda.synchronize()
             L.check_status()
             res[f"split_{exchange}"] = [within(out.cpu().numpy(), ex), max_err(out.cpu().numpy(), ex)]
-            if exchange == "p2p":
+            if exchange in ("fused", "p2p"):
                 # one step captured in a CUDA graph and replayed
                 side = torch.cuda.Stream()
                 side.wait_stream(torch.cuda.current_stream())
@@ -131,7 +131,7 @@ def kv_split_nccl(rank, world, port, result_dir):
                     g.replay()
                 torch.cuda.synchronize()
                 L.check_status()
-                res["split_p2p_graph"] = [within(dec.out.cpu().numpy(), ex), max_err(dec.out.cpu().numpy(), ex)]
+                res[f"split_{exchange}_graph"] = [within(dec.out.cpu().numpy(), ex), max_err(dec.out.cpu().numpy(), ex)]
                 del g
             dec.close()
     finally:

@@ -95,6 +95,97 @@ def test_exchange_merge_single_rank_epochs_and_graph():
         lib.lstk_cuda_mailbox_free(own)
 
 
+def _fused_case(seed, ctx):
+    rng = np.random.default_rng(seed)
+    bt, n_pages = scattered_block_tables(rng, [ctx])
+    kc, vc = random_cache(rng, n_pages, 4)
+    q = random_q(rng, 1, 32)
+    f16 = lambda a: torch.from_numpy(a.view(np.int16)).cuda().view(torch.float16)
+    return (f16(kc), f16(vc), torch.from_numpy(q).cuda(), torch.from_numpy(bt).cuda(),
+            torch.tensor([ctx], dtype=torch.int32, device="cuda"))
+
+
+def _decode_exchange(args, ws, boxes, rank, n_ranks, out, lse, wait_ns=0):
+    import ctypes
+    from localstack_b200.attn import _DT, layout_of
+    kc, vc, q, bt, lens = args
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    return L.lib().lstk_cuda_attn_decode_exchange(
+        ctypes.byref(layout_of(kc)), P(kc), P(vc), P(q), _DT[q.dtype], 1, 32, P(bt), bt.shape[1], P(lens), 0, SCALE,
+        P(out), P(lse), P(ws.buf), ws.buf.numel(), 0, P(boxes), rank, n_ranks, wait_ns,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ctx", [20000, 33, 0])
+def test_decode_exchange_single_rank_equals_decode(ctx):
+    """R = 1: the decode with the exchange fused into its combine gives the plain decode's rows
+    and lse exactly (a merge of one record), for a context split over every CTA, one finished
+    inside one CTA, and an empty one; over repeated calls (epochs advance) and graph replays."""
+    args = _fused_case(5, max(ctx, 1))
+    if ctx == 0:
+        args = args[:4] + (torch.zeros(1, dtype=torch.int32, device="cuda"),)
+    ref, ref_lse = L.attn_decode(*args, SCALE, want_lse=True)
+    rows = 32
+    own = _mailbox(1, rows)
+    try:
+        boxes = torch.tensor([own.value], dtype=torch.int64, device="cuda")
+        ws = L.DecodeWorkspace(1, 32, 4)
+        out = torch.empty((1, 32, 128), device="cuda")
+        lse = torch.empty((1, 32), device="cuda")
+        for _ in range(3):
+            out.fill_(7.0)
+            assert _decode_exchange(args, ws, boxes, 0, 1, out, lse) == 0
+            torch.cuda.synchronize()
+            L.check_status()
+            assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            _decode_exchange(args, ws, boxes, 0, 1, out, lse)
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            _decode_exchange(args, ws, boxes, 0, 1, out, lse)
+        for _ in range(3):
+            out.fill_(7.0)
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+        del g
+        L.check_status()
+    finally:
+        torch.cuda.synchronize()
+        L.lib().lstk_cuda_mailbox_free(own)
+
+
+@pytest.mark.gpu
+def test_decode_exchange_times_out_when_a_peer_never_writes():
+    """Failure detection of the fused path: rank 0 of 2 waits for rank 1's flags, which nothing
+    sets; each combine CTA's bounded wait (20 ms) runs out, LSTK_ERR_TIMEOUT is recorded, the rows
+    are zeros and the context still decodes correctly afterwards."""
+    args = _fused_case(6, 5000)
+    before = L.attn_decode(*args, SCALE)
+    own, other = _mailbox(2, 32), _mailbox(2, 32)
+    try:
+        boxes = torch.tensor([own.value, other.value], dtype=torch.int64, device="cuda")
+        ws = L.DecodeWorkspace(1, 32, 4)
+        out = torch.full((1, 32, 128), 7.0, device="cuda")
+        lse = torch.empty((1, 32), device="cuda")
+        assert _decode_exchange(args, ws, boxes, 0, 2, out, lse, wait_ns=20_000_000) == 0
+        with pytest.raises(L.LstkError) as e:
+            L.check_status()
+        assert e.value.code == -3
+        assert torch.count_nonzero(out).item() == 0
+        after = L.attn_decode(*args, SCALE)
+        L.check_status()
+        assert torch.equal(after, before)
+    finally:
+        torch.cuda.synchronize()
+        L.lib().lstk_cuda_mailbox_free(own)
+        L.lib().lstk_cuda_mailbox_free(other)
+
+
 @pytest.mark.gpu
 def test_exchange_merge_times_out_when_a_peer_never_writes():
     """Failure detection: rank 0 of 2 waits for source 1's flags, which nothing sets; the bounded
@@ -147,6 +238,6 @@ def test_kv_split_nccl_two_ranks(tmp_path):
                 os.environ[k] = v
     for r in range(2):
         res = json.load(open(os.path.join(tmp_path, f"rank{r}.json")))
-        for key in ("split_p2p", "split_collective", "split_p2p_graph"):
+        for key in ("split_fused", "split_fused_graph", "split_p2p", "split_collective", "split_p2p_graph"):
             ok, err = res[key]
             assert ok, (r, key, err)
