@@ -476,6 +476,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     __syncthreads();
 }
 
+constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = kCombineThreads / 32;
+
 struct CombineParams {
     int n_seqs, n_head, n_head_kv, group, n_hg, grid;
     const int32_t *prefix;
@@ -493,13 +496,16 @@ struct CombineParams {
 };
 
 // The end of a combine CTA's row: without an exchange, out / lse_out get the local row. With
-// one, the row's local (O, lse) goes through the exchange-merge protocol of exchange.cuh inside
-// this CTA - stored into slot `rank` of every rank's mailbox (plain peer stores), flagged with a
-// system-scope release, the R flags of the row awaited in the own mailbox (bounded by wait_ns;
-// on timeout the status records it and the row is zeros) - and out / lse_out get the merge of the
-// R records. The CTA's epoch counter is the mailbox header entry of its linear index, so the
-// calls replay from a CUDA graph. Every thread of the CTA calls this; o is read from threads
-// tid < kD, lse (natural log) from thread 0.
+// one, the row's local (O, lse) goes to every rank (exchange.cuh's mailboxes) and out / lse_out
+// get the log-sum-exp merge of the R ranks' rows. The row travels as 129 words of 8 bytes - a
+// value's f32 bits and the call's epoch - stored straight into slot `rank` of every rank's
+// mailbox (plain peer stores); a reader polls the words of its own mailbox until each carries
+// the epoch, and an 8-byte word is written and read whole, so no flag and no system-scope fence
+// is needed. Waits are bounded by wait_ns (on timeout the status records it and the row is
+// zeros). The CTA's epoch counter is the mailbox header entry of its linear index, so calls
+// replay from a CUDA graph; words alternate between two banks by epoch parity (a rank is at most
+// one call ahead of a peer: it needs the peer's row of the current call to finish it). Every
+// thread of the CTA calls this; o is read from threads tid < kD, lse (natural log) from thread 0.
 template <bool kExchange>
 __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, float o, float lse) {
     const int tid = threadIdx.x;
@@ -507,7 +513,9 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         if (tid < kD) p.out[row * kD + tid] = o;
         if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = lse;
     } else {
-        __shared__ float o_s[kD + 1];  // the local row, then its lse
+        constexpr int kMaxRanks = kCombineThreads;
+        __shared__ float o_s[kD + 1];     // the local row, then its lse
+        __shared__ float lse_s[kMaxRanks];  // every rank's lse of the row
         __shared__ int timed_out;
         const int R = p.n_ranks;
         const int64_t n_rows = (int64_t) p.n_seqs * p.n_head;
@@ -516,63 +524,69 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         uint32_t *my_epoch = reinterpret_cast<uint32_t *>(own) + cta;
         const uint32_t epoch = *my_epoch + 1u;
         const int bank = (int) (epoch & 1u);
-        const size_t rec_off = exchange::records_offset(R, n_rows);
-        const int64_t slot_stride = n_rows * (kD + 1);  // floats per (bank, source)
+        const size_t w_off = exchange::words_offset(R, n_rows);
+        const int64_t slot = n_rows * (kD + 1);  // words per (bank, source)
         if (tid < kD) o_s[tid] = o;
         if (tid == 0) o_s[kD] = lse, timed_out = 0;
         __syncthreads();
+        const uint64_t tag = (uint64_t) epoch << 32;
         for (int i = tid; i < R * (kD + 1); i += blockDim.x) {
             const int r = i / (kD + 1), d = i - r * (kD + 1);
-            reinterpret_cast<float *>(p.mailboxes[r] + rec_off)[((int64_t) bank * R + p.rank) * slot_stride +
-                                                                 row * (kD + 1) + d] = o_s[d];
+            uint64_t *w = reinterpret_cast<uint64_t *>(p.mailboxes[r] + w_off) + ((int64_t) bank * R + p.rank) * slot +
+                          row * (kD + 1) + d;
+            exchange::st_relaxed_sys_u64(w, tag | __float_as_uint(o_s[d]));
         }
-        __syncthreads();
-        if (tid < R) {
-            exchange::st_release_sys(reinterpret_cast<uint32_t *>(p.mailboxes[tid] + exchange::flags_offset()) +
-                                         ((int64_t) bank * R + p.rank) * n_rows + row,
-                                     epoch);
-            const uint32_t *flag = reinterpret_cast<const uint32_t *>(own + exchange::flags_offset()) +
-                                   ((int64_t) bank * R + tid) * n_rows + row;
-            bool ok = exchange::ld_acquire_sys(flag) == epoch;
-            if (!ok) {
+        // Poll the own mailbox: thread r < R the lse word of source r, thread d < kD the value
+        // words of element d from every source (its own values; the lse comes through shared
+        // memory after the barrier).
+        const uint64_t *base = reinterpret_cast<const uint64_t *>(own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
+        volatile int *const abort = &timed_out;
+        auto await = [&](const uint64_t *w, float &v, int src) {
+            uint64_t x = exchange::ld_relaxed_sys_u64(w);
+            if ((uint32_t) (x >> 32) != epoch) {
                 const uint64_t t0 = global_timer_ns();
-                for (uint32_t i = 1; i < (1u << 30); i++) {
-                    if (exchange::ld_acquire_sys(flag) == epoch) {
-                        ok = true;
-                        break;
+                for (uint32_t i = 1;; i++) {
+                    x = exchange::ld_relaxed_sys_u64(w);
+                    if ((uint32_t) (x >> 32) == epoch) break;
+                    if ((i & 63u) == 0 && (global_timer_ns() - t0 > p.wait_ns || *abort)) {
+                        *abort = 1;
+                        report(p.status, kStatusTimeout, kSiteExchangeWait, src);
+                        v = 0.f;
+                        return;
                     }
-                    if ((i & 63u) == 0 && global_timer_ns() - t0 > p.wait_ns) break;
                 }
             }
-            if (!ok) {
-                timed_out = 1;
-                report(p.status, kStatusTimeout, kSiteExchangeWait, tid);
-            }
-        }
+            v = __uint_as_float((uint32_t) x);
+        };
+        if (tid < R) await(base + (int64_t) tid * slot + kD, lse_s[tid], tid);
         __syncthreads();
         if (tid < kD) {
             float v = 0.f, l = -INFINITY;
-            if (!timed_out) {
-                const float *base = reinterpret_cast<const float *>(own + rec_off) + (int64_t) bank * R * slot_stride +
-                                    row * (kD + 1);
-                float M = -INFINITY;
-                for (int r = 0; r < R; r++) M = fmaxf(M, __ldcv(base + r * slot_stride + kD));
+            float M = -INFINITY;
+            for (int r = 0; r < R; r++) M = fmaxf(M, lse_s[r]);
+            float den = 0.f, acc = 0.f;
+            for (int r = 0; r < R; r++) {
+                float x;
+                await(base + (int64_t) r * slot + tid, x, r);
                 if (M != -INFINITY) {
-                    float den = 0.f, acc = 0.f;
-                    for (int r = 0; r < R; r++) {
-                        const float wt = __expf(__ldcv(base + r * slot_stride + kD) - M);
-                        den += wt;
-                        acc += wt * __ldcv(base + r * slot_stride + tid);
-                    }
-                    v = acc / den;
-                    l = M + __logf(den);
+                    const float wt = __expf(lse_s[r] - M);
+                    den += wt;
+                    acc += wt * x;
                 }
+            }
+            if (M != -INFINITY && !timed_out) {
+                v = acc / den;
+                l = M + __logf(den);
             }
             p.out[row * kD + tid] = v;
             if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = l;
         }
         __syncthreads();
-        if (tid == 0) *my_epoch = epoch;  // read by this CTA's successor in the next call
+        if (timed_out && tid < kD) p.out[row * kD + tid] = 0.f;  // every thread's result is void
+        if (tid == 0) {
+            if (timed_out && p.lse_out != nullptr) p.lse_out[row] = -INFINITY;
+            *my_epoch = epoch;  // read by this CTA's successor in the next call
+        }
     }
 }
 
@@ -582,8 +596,6 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
 // passes: one thread per piece finds its partial row and lse (the only place the range
 // arithmetic runs), then the weights exp2(lse - M), then the 8 warps sum weighted rows with the
 // loads of several pieces in flight per warp (lanes own 4 dims each).
-constexpr int kCombineThreads = 256;
-constexpr int kCombineWarps = kCombineThreads / 32;
 
 template <bool kExchange>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const CombineParams p) {

@@ -37,8 +37,15 @@ __host__ __device__ inline size_t flags_offset() { return kHeaderBytes; }
 __host__ __device__ inline size_t records_offset(int n_ranks, int64_t n_rows) {
     return (flags_offset() + sizeof(uint32_t) * 2 * (size_t) n_ranks * (size_t) n_rows + 255) / 256 * 256;
 }
+// Words of the fused decode exchange (decode_combine_kernel<true>): uint64 [2 banks][R sources]
+// [n_rows][kD + 1], each the f32 bits of one value (low half) and the epoch that wrote it (high
+// half), so a reader that sees its epoch in a word has the word's value - no flag, no fence.
+__host__ __device__ inline size_t words_offset(int n_ranks, int64_t n_rows) {
+    return (records_offset(n_ranks, n_rows) + sizeof(float) * 2 * (size_t) n_ranks * (size_t) n_rows * (kD + 1) + 255) /
+           256 * 256;
+}
 __host__ __device__ inline size_t mailbox_bytes(int n_ranks, int64_t n_rows) {
-    return records_offset(n_ranks, n_rows) + sizeof(float) * 2 * (size_t) n_ranks * (size_t) n_rows * (kD + 1);
+    return words_offset(n_ranks, n_rows) + sizeof(uint64_t) * 2 * (size_t) n_ranks * (size_t) n_rows * (kD + 1);
 }
 
 struct Params {
@@ -62,6 +69,15 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Single 8-byte accesses (naturally aligned: single-copy atomic) for the value+epoch words.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
