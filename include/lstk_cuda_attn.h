@@ -205,6 +205,32 @@ int lstk_cuda_kv_alloc(const lstk_kv_pages *state, const int32_t *slots, const i
                        int32_t max_tokens, int64_t *cells, int32_t *positions, int32_t *ok, void *stream);
 int lstk_cuda_kv_release(const lstk_kv_pages *state, int32_t slot, int32_t keep, void *stream);
 
+/* ---- q8_0 KV cache (the reference's planned option, docs/plan.md:389-395; not built there) ----
+ * The values of ggml's block_q8_0 (per 32 consecutive values of a row: d = amax / 127 kept as
+ * f16, q = round-to-nearest-even(x / d) as int8 - quantize_row_q8_0's ARM form) in two planes per
+ * cache, so every 128-byte row stays 16-byte aligned for TMA: qs int8 [n_cells][n_head_kv][128]
+ * and d f16 [n_cells][n_head_kv][4]. layout describes the cache as for f16 (head_dim 128,
+ * block_size 32); n_head_kv must be even for the decode (16-byte scale rows). Planes 16-byte
+ * aligned.
+ *
+ * lstk_cuda_kv_append_q8: lstk_cuda_kv_append with the K and V rows quantised into the planes
+ * (bit-identical to quantising the f16 path's f32 rows). lstk_cuda_attn_decode_q8:
+ * lstk_cuda_attn_decode over q8_0 planes with ggml's CPU semantics for a q8_0 cache - the query
+ * row quantised to q8_0, each score sum_b (d_k,b * d_q,b) * (integer dot of block b), f32
+ * accumulation of the dequantised V (the softmax as in lstk_cuda_attn_decode). Same workspace
+ * (lstk_cuda_attn_decode_workspace_size). */
+int lstk_cuda_kv_append_q8(const lstk_kv_layout *layout, int8_t *k_qs, void *k_d, int8_t *v_qs, void *v_d,
+                           const void *q_in, const void *k_in, const void *v_in, int32_t in_dtype,
+                           int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens,
+                           int32_t n_head, const int32_t *positions, const int64_t *cells, const float *q_gamma,
+                           const float *k_gamma, float eps, const float *rope_table, int32_t rope_n_pos, void *q_out,
+                           int32_t q_out_dtype, void *stream);
+int lstk_cuda_attn_decode_q8(const lstk_kv_layout *layout, const int8_t *k_qs, const void *k_d, const int8_t *v_qs,
+                             const void *v_d, const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                             const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                             int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
+                             size_t workspace_bytes, int32_t n_ctas, void *stream);
+
 /* ---- One context over several processes / GPUs: peer-memory exchange and merge -------------
  * (no counterpart in the reference, which runs in one process). Rank r of R decodes its
  * contiguous chunk of a sequence's pages with lstk_cuda_attn_decode(..., lse_out) and then calls

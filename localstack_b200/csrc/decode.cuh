@@ -25,6 +25,8 @@
 // because they take the FLOPs off the issue slots; the kernel is bound by HBM bytes.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "exchange.cuh"
 
@@ -62,6 +64,7 @@ struct Params {
     float *part_lse;  // [kMaxCtas][2][kPartRows], log2 units
     int32_t *prefix;  // [n_seqs + 1] pages before each sequence
     DeviceStatus *status;
+    int q8_dpitch;              // q8_0 cache: bytes per cell row of a stage's scale tile (16 or 32)
     uint64_t wait_ns;           // limit of each pipeline wait (drains keep kWaitLimitNs)
     const int32_t *start_flag;  // optional: the producer waits for it to be non-zero before loading
 };
@@ -248,10 +251,220 @@ __device__ __forceinline__ void process_page(HeadState &st, uint32_t kbase, uint
     }
 }
 
+// ---- q8_0 cache ------------------------------------------------------------------------------
+// Planes: qs int8 [n_cells][n_head_kv][128] (a head's page: 32 rows of 128 bytes, loaded with the
+// 128-byte swizzle like an f16 half-page) and d f16 [n_cells][n_head_kv][4] (one scale per 32
+// values). Stage layout: K qs of the group's 4 heads (4 x 4 KiB), V qs (4 x 4 KiB), then the K and
+// V scale tiles: 32 rows (cells) of the group's heads' scales, `dpitch` bytes per row.
+constexpr int kQ8HeadPage = kPage * 128;                 // 4 KiB
+constexpr int kQ8VOff = kHeadsPerGroup * kQ8HeadPage;    // 16 KiB
+constexpr int kQ8KdOff = 2 * kHeadsPerGroup * kQ8HeadPage;
+constexpr int kQ8VdOff = kQ8KdOff + kPage * 32;          // scale rows of up to 32 bytes
+
+__device__ __forceinline__ void mma_16832_s8(int c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Per-warp running state over a q8_0 cache: as HeadState, with the query quantised to q8_0.
+struct HeadStateQ8 {
+    float o[8][4];    // O^T fragments: m-tile mt covers dims 16mt + {2g, 2g + 1} (rows g, g + 8)
+    float m[2];
+    float l[2];
+    uint32_t qq[4][2];  // B fragments of the quantised Q^T, one pair per 32-dim block
+    float dq[2][4];     // f16-rounded Q block scales of query heads 2t, 2t + 1
+    __device__ void reset() {
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+    }
+};
+
+// Quantises query head g's row to q8_0 as ggml does for a q8_0 K (quantize_row_q8_0 of the f32
+// row: per 32 values d = amax / 127, q = round-to-nearest-even(x / d)), lane (g, t) keeping the
+// bytes its B fragments need (dims 32b + 4t.. and 32b + 16 + 4t..) and the four lanes of a head
+// reducing the block's amax; then gathers the scales of heads 2t, 2t + 1 (the S layout).
+__device__ __forceinline__ void load_q_q8(HeadStateQ8 &st, const Params &p, int b, int kvh, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const bool live = g < p.group;
+    const int64_t row = ((int64_t) b * p.n_head + (int64_t) kvh * p.group + (live ? g : 0)) * kD;
+    float dqb[4];
+#pragma unroll
+    for (int blk = 0; blk < 4; blk++) {
+        float x[8];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int d0 = blk * 32 + h * 16 + 4 * t;
+            if (!live) {
+                x[4 * h] = x[4 * h + 1] = x[4 * h + 2] = x[4 * h + 3] = 0.f;
+            } else if (p.q_f16) {
+                const __half *q = reinterpret_cast<const __half *>(p.q) + row + d0;
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(q));
+                const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(q + 2));
+                x[4 * h] = a.x, x[4 * h + 1] = a.y, x[4 * h + 2] = c.x, x[4 * h + 3] = c.y;
+            } else {
+                const float4 v = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.q) + row + d0);
+                x[4 * h] = v.x, x[4 * h + 1] = v.y, x[4 * h + 2] = v.z, x[4 * h + 3] = v.w;
+            }
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.f ? __frcp_rn(d) : 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) w |= (uint32_t) (__float2int_rn(__fmul_rn(x[4 * h + e], id)) & 0xff) << (8 * e);
+            st.qq[blk][h] = w;
+        }
+        dqb[blk] = __half2float(__float2half_rn(d));
+    }
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int blk = 0; blk < 4; blk++) st.dq[h][blk] = __shfl_sync(0xffffffffu, dqb[blk], (2 * t + h) * 4);
+}
+
+// Two f16 pairs from four int8 values r = (x0, x1, x2, x3): (x0, x2) and (x1, x3), exactly
+// (bytes offset by 128 under the exponent of 1024, then 1152 subtracted).
+__device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t r, uint32_t &even, uint32_t &odd) {
+    const uint32_t u = r ^ 0x80808080u;
+    uint32_t lo, hi;
+    asm("prmt.b32 %0, %1, %2, 0x4240;" : "=r"(lo) : "r"(u), "r"(0x64646464u));
+    asm("prmt.b32 %0, %1, %2, 0x4341;" : "=r"(hi) : "r"(u), "r"(0x64646464u));
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const __half2 e = __hsub2(*reinterpret_cast<const __half2 *>(&lo), bias);
+    const __half2 o = __hsub2(*reinterpret_cast<const __half2 *>(&hi), bias);
+    even = *reinterpret_cast<const uint32_t *>(&e);
+    odd = *reinterpret_cast<const uint32_t *>(&o);
+}
+
+// One page (32 tokens, `valid` visible) of one KV head over the q8_0 planes. S: per 32-dim block
+// an int8 MMA (m16n8k32) gives the exact integer dot of the K and Q blocks; the score is
+// sum_b (d_k,b * d_q,b) * dot_b in block order, as ggml's q8_0 x q8_0 dot. PV: V's int8 values
+// become f16 exactly and each block's scale d_v multiplies P instead (P' = P * d_v per key and
+// block, rounded to f16 like P itself), so O^T += V^T . P'^T per 16-dim m-tile; the tile's rows
+// are dims 2g, 2g + 1 of its 16 (the pairs ldmatrix.trans delivers).
+__device__ __forceinline__ void process_page_q8(HeadStateQ8 &st, uint32_t kbase, uint32_t vbase, const uint8_t *kd,
+                                                const uint8_t *vd, int dpitch, int valid, float scale_log2,
+                                                int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int li = lane >> 3, lr = lane & 7;
+#pragma unroll
+    for (int slab = 0; slab < 2; slab++) {
+        if (slab * 16 >= valid) break;
+        const int tok0 = slab * 16 + g;
+        int sb[4][4];
+#pragma unroll
+        for (int blk = 0; blk < 4; blk++) {
+            uint32_t a[4];
+            ldsm_x4(kbase + sw128_offset((uint32_t) (slab * 16 + lr + 8 * (li & 1)), (uint32_t) (2 * blk + (li >> 1))),
+                    a);
+            sb[blk][0] = sb[blk][1] = sb[blk][2] = sb[blk][3] = 0;
+            mma_16832_s8(sb[blk], a, st.qq[blk][0], st.qq[blk][1]);
+        }
+        // scales of tokens tok0 and tok0 + 8 (4 f16 each)
+        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + tok0 * dpitch);
+        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + (tok0 + 8) * dpitch);
+        float dk[2][4];
+        {
+            const float2 a0 = __half22float2(*reinterpret_cast<const __half2 *>(&k0.x));
+            const float2 a1 = __half22float2(*reinterpret_cast<const __half2 *>(&k0.y));
+            const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&k1.x));
+            const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&k1.y));
+            dk[0][0] = a0.x, dk[0][1] = a0.y, dk[0][2] = a1.x, dk[0][3] = a1.y;
+            dk[1][0] = c0.x, dk[1][1] = c0.y, dk[1][2] = c1.x, dk[1][3] = c1.y;
+        }
+        float s[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {  // i: (token tok0 + 8 (i >> 1), head 2t + (i & 1))
+            float acc = 0.f;
+#pragma unroll
+            for (int blk = 0; blk < 4; blk++)
+                acc = __fadd_rn(acc, __fmul_rn((float) sb[blk][i], __fmul_rn(dk[i >> 1][blk], st.dq[i & 1][blk])));
+            s[i] = acc;
+        }
+        const bool v0 = tok0 < valid, v1 = tok0 + 8 < valid;
+        float x[4];
+        x[0] = v0 ? s[0] * scale_log2 : -INFINITY;
+        x[1] = v0 ? s[1] * scale_log2 : -INFINITY;
+        x[2] = v1 ? s[2] * scale_log2 : -INFINITY;
+        x[3] = v1 ? s[3] * scale_log2 : -INFINITY;
+        float alpha[2], mu[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float tm = fmaxf(x[h], x[h + 2]);
+            tm = warp_max_xor(tm, 4);
+            const float mn = fmaxf(st.m[h], tm);
+            mu[h] = mn == -INFINITY ? 0.f : mn;
+            alpha[h] = fast_exp2(st.m[h] - mu[h]);
+            st.m[h] = mn;
+        }
+        const float p0 = fast_exp2(x[0] - mu[0]);
+        const float p1 = fast_exp2(x[1] - mu[1]);
+        const float p2 = fast_exp2(x[2] - mu[0]);
+        const float p3 = fast_exp2(x[3] - mu[1]);
+        st.l[0] = st.l[0] * alpha[0] + (p0 + p2);
+        st.l[1] = st.l[1] * alpha[1] + (p1 + p3);
+#pragma unroll
+        for (int mt = 0; mt < 8; mt++) {
+            st.o[mt][0] *= alpha[0];
+            st.o[mt][1] *= alpha[1];
+            st.o[mt][2] *= alpha[0];
+            st.o[mt][3] *= alpha[1];
+        }
+        // V scales of tokens tok0, tok0 + 8; a key that is not visible gets P' = 0 outright (its
+        // stale scale could be non-finite)
+        const uint2 w0 = *reinterpret_cast<const uint2 *>(vd + tok0 * dpitch);
+        const uint2 w1 = *reinterpret_cast<const uint2 *>(vd + (tok0 + 8) * dpitch);
+        float dv[2][4];
+        {
+            const float2 a0 = __half22float2(*reinterpret_cast<const __half2 *>(&w0.x));
+            const float2 a1 = __half22float2(*reinterpret_cast<const __half2 *>(&w0.y));
+            const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&w1.x));
+            const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&w1.y));
+            dv[0][0] = a0.x, dv[0][1] = a0.y, dv[0][2] = a1.x, dv[0][3] = a1.y;
+            dv[1][0] = c0.x, dv[1][1] = c0.y, dv[1][2] = c1.x, dv[1][3] = c1.y;
+        }
+#pragma unroll
+        for (int blk = 0; blk < 4; blk++) {
+            const float s0 = v0 ? dv[0][blk] : 0.f, s1 = v1 ? dv[1][blk] : 0.f;
+            const uint32_t pb0 = movmatrix_trans(pack_half2(v0 ? p0 * s0 : 0.f, v0 ? p1 * s0 : 0.f));
+            const uint32_t pb1 = movmatrix_trans(pack_half2(v1 ? p2 * s1 : 0.f, v1 ? p3 * s1 : 0.f));
+            uint32_t r[4];
+            ldsm_x4_trans(vbase + sw128_offset((uint32_t) (slab * 16 + lr + 8 * (li & 1)), (uint32_t) (2 * blk + (li >> 1))),
+                          r);
+            // r[0] / r[1]: chunk 2 blk, tokens 0-7 / 8-15 of the slab; r[2] / r[3]: chunk 2 blk + 1
+#pragma unroll
+            for (int hc = 0; hc < 2; hc++) {
+                uint32_t a[4];
+                i8x4_to_f16x2x2(r[2 * hc], a[0], a[1]);
+                i8x4_to_f16x2x2(r[2 * hc + 1], a[2], a[3]);
+                mma_16816(st.o[2 * blk + hc], a, pb0, pb1);
+            }
+        }
+    }
+}
+
 extern __shared__ __align__(1024) uint8_t dyn_smem[];
 
+// kQ8: the cache is q8_0 planes (kmap / vmap over the qs planes, kdmap / vdmap over the scale
+// planes); else f16 rows (kmap / vmap; the scale maps are unused).
+template <bool kQ8>
 __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
+                                                                    const __grid_constant__ CUtensorMap kdmap,
+                                                                    const __grid_constant__ CUtensorMap vdmap,
                                                                     const Params p) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -325,6 +538,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         if (lane == 0) {
             prefetch_tensormap(&kmap);
             prefetch_tensormap(&vmap);
+            if constexpr (kQ8) {
+                prefetch_tensormap(&kdmap);
+                prefetch_tensormap(&vdmap);
+            }
             policy = l2_policy_evict_first();
             if (p.start_flag != nullptr && !flag_wait_bounded(p.start_flag, abort_flag, p.wait_ns)) {
                 report(p.status, kStatusTimeout, kSiteDecodeWaitStart, blockIdx.x);
@@ -374,6 +591,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                     if (pid < 0 || pid >= p.n_pages) {
                         report(p.status, kStatusBadIndex, kSiteDecodePage, pid);
                         mbar_arrive(fb);
+                    } else if constexpr (kQ8) {
+                        mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kQ8HeadPage + 2 * kPage * p.q8_dpitch));
+                        const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                        for (int h = 0; h < nh; h++) {
+                            const int kvh = hg * kHeadsPerGroup + h;
+                            tma_load_3d_hint(sb + h * kQ8HeadPage, &kmap, fb, 0, kvh, pid * kPage, policy);
+                            tma_load_3d_hint(sb + kQ8VOff + h * kQ8HeadPage, &vmap, fb, 0, kvh, pid * kPage, policy);
+                        }
+                        // scale rows of the group's heads: x = 16 halves (32 bytes) per group
+                        tma_load_2d(sb + kQ8KdOff, &kdmap, fb, hg * 16, pid * kPage);
+                        tma_load_2d(sb + kQ8VdOff, &vdmap, fb, hg * 16, pid * kPage);
                     } else {
                         mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kHeadPage));
                         const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
@@ -399,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         }
     } else if (lo < hi) {
         // Consumers: warp w owns KV head hg*4 + w of every page-group.
-        HeadState st;
+        typename std::conditional<kQ8, HeadStateQ8, HeadState>::type st;
         Cursor cur;
         cur.locate(lo, pfx, p.n_seqs, p.n_hg);
         int64_t piece_start = lo;
@@ -412,7 +640,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             if (x == lo || cur.p == 0) {
                 piece_start = x;
                 st.reset();
-                if (active) load_q(st, p, cur.b, kvh, lane);
+                if (active) {
+                    if constexpr (kQ8) load_q_q8(st, p, cur.b, kvh, lane);
+                    else load_q(st, p, cur.b, kvh, lane);
+                }
                 len = range_len(p, p.seq_lens[cur.b]);
             }
             const int s = (int) (i % kStages);
@@ -429,8 +660,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             if (active && pid >= 0 && pid < p.n_pages) {
                 const int valid = min(kPage, len - cur.p * kPage);
                 const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
-                process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage, valid,
-                             p.scale_log2, lane);
+                if constexpr (kQ8) {
+                    const uint8_t *st_base = stages + (size_t) s * kStageBytes;
+                    process_page_q8(st, sb + warp * kQ8HeadPage, sb + kQ8VOff + warp * kQ8HeadPage,
+                                    st_base + kQ8KdOff + warp * 8, st_base + kQ8VdOff + warp * 8, p.q8_dpitch, valid,
+                                    p.scale_log2, lane);
+                } else {
+                    process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage,
+                                 valid, p.scale_log2, lane);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
@@ -464,8 +702,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                         }
 #pragma unroll
                         for (int mt = 0; mt < 8; mt++) {
-                            dst[mt * 16 + g] = st.o[mt][h] * inv;
-                            dst[mt * 16 + g + 8] = st.o[mt][h + 2] * inv;
+                            if constexpr (kQ8) {  // m-tile rows g, g + 8 are dims 2g, 2g + 1
+                                *reinterpret_cast<float2 *>(dst + mt * 16 + 2 * g) =
+                                    make_float2(st.o[mt][h] * inv, st.o[mt][h + 2] * inv);
+                            } else {
+                                dst[mt * 16 + g] = st.o[mt][h] * inv;
+                                dst[mt * 16 + g + 8] = st.o[mt][h + 2] * inv;
+                            }
                         }
                     }
                 }

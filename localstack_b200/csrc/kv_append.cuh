@@ -67,6 +67,10 @@ struct Params {
     int64_t n_cells;
     void *q_out;
     int q_out_f16;
+    // q8_0 cache (kv_append_kernel<.., .., true>): K / V rows quantised into planes qs int8
+    // [n_cells][n_head_kv][128] and d f16 [n_cells][n_head_kv][4] instead of k_cache / v_cache.
+    int8_t *k_qs, *v_qs;
+    __half *k_d, *v_d;
     int group_rows;        // G: a multiple of 4, at most 32 (bf16) or 16 (f32)
     int groups_per_token;  // ceil(R / G)
     DeviceStatus *status;
@@ -117,9 +121,9 @@ __device__ __forceinline__ uint32_t min_abs_bf16x2(uint32_t a, uint32_t b) {
 // the same banks two at a time in the natural order.
 __device__ __forceinline__ int gamma_slot(int k) { return k ^ ((k >> 3) & 1); }
 
-// kBf16: bf16 inputs (else f32); kQ16: Q written as f16 (else f32). Params::in_bf16 and
-// q_out_f16 match the instantiation.
-template <bool kBf16, bool kQ16>
+// kBf16: bf16 inputs (else f32); kQ16: Q written as f16 (else f32); kQ8: K and V stored as
+// q8_0 planes (else f16 rows). Params::in_bf16 and q_out_f16 match the instantiation.
+template <bool kBf16, bool kQ16, bool kQ8>
 __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t s_bar[kWarps][2];    // per warp, per stage buffer
@@ -471,6 +475,41 @@ __global__ void __launch_bounds__(kWarps * 32) kv_append_kernel(const Params p) 
                         for (int q = 0; q < 2; q++)
                             *reinterpret_cast<float4 *>(d + h * 64 + q * 4) =
                                 make_float4(o[8 * h + 4 * q], o[8 * h + 4 * q + 1], o[8 * h + 4 * q + 2], o[8 * h + 4 * q + 3]);
+                } else if constexpr (K != 0 && kQ8) {
+                    // ggml's q8_0 of the row (quantize_row_q8_0, ARM form): per 32 values amax, d =
+                    // amax / 127, q = round-to-nearest-even(x * (1 / d)), d kept as f16. Lane c's
+                    // first half lies in block c / 4, its second half in block 2 + c / 4; the four
+                    // lanes of a block reduce its amax.
+                    float amax[2] = {0.f, 0.f};
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        amax[0] = fmaxf(amax[0], fabsf(o[i]));
+                        amax[1] = fmaxf(amax[1], fabsf(o[8 + i]));
+                    }
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        amax[hh] = fmaxf(amax[hh], __shfl_xor_sync(0x000000ffu << (8 * sub), amax[hh], 1));
+                        amax[hh] = fmaxf(amax[hh], __shfl_xor_sync(0x000000ffu << (8 * sub), amax[hh], 2));
+                    }
+                    const int64_t row_i = at - c * 8;  // element offset of the row: (cell * Hkv + head) * 128
+                    int8_t *qs = (K == 1 ? p.k_qs : p.v_qs) + row_i;
+                    __half *dp = (K == 1 ? p.k_d : p.v_d) + row_i / 32;
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        const float dd = __fdiv_rn(amax[hh], 127.0f);
+                        const float id = dd != 0.f ? __frcp_rn(dd) : 0.f;
+                        uint32_t w[2];
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            uint32_t v = 0;
+#pragma unroll
+                            for (int e = 0; e < 4; e++)
+                                v |= (uint32_t) (__float2int_rn(__fmul_rn(o[8 * hh + 4 * k + e], id)) & 0xff) << (8 * e);
+                            w[k] = v;
+                        }
+                        *reinterpret_cast<uint2 *>(qs + hh * 64 + c * 8) = make_uint2(w[0], w[1]);
+                        if ((c & 3) == 0) dp[2 * hh + (c >> 2)] = __float2half_rn(dd);
+                    }
                 } else {
                     __half *d = (K == 0 ? reinterpret_cast<__half *>(p.q_out) : K == 1 ? p.k_cache : p.v_cache) + at;
 #pragma unroll

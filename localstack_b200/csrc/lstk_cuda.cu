@@ -33,11 +33,12 @@ struct DeviceInfo {
     DeviceStatus *status = nullptr;
     // Dynamic shared-memory limits raised so far on this device, per kernel (ensure_smem).
     size_t decode_smem = 0;
+    size_t decode_q8_smem = 0;
     size_t prefill_smem = 0;
-    size_t append_smem[4] = {};  // per kv_append instantiation (append_kernel)
+    size_t append_smem[8] = {};  // per kv_append instantiation (append_kernel)
     size_t gemm_smem = 0;
     // Resident kv_append CTAs per SM, per [instantiation][rows per group / 4]; 0 = not asked yet.
-    int append_occ[4][append::kMaxGroupRows / 4 + 1] = {};
+    int append_occ[8][append::kMaxGroupRows / 4 + 1] = {};
 };
 
 DeviceInfo g_devices[kMaxDevices];
@@ -175,6 +176,22 @@ int encode_f32_3d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t di
     return encode_3d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dim0, dim1, dim2, box0, box1, box2);
 }
 
+// 2-D map over a q8_0 scale plane [rows][cols] f16 (cols = n_head_kv * 4 scales per cell), box
+// (box_cols, 32), no swizzle; out-of-range columns fill zeros.
+int encode_scales_2d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {box_cols, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
+    return LSTK_OK;
+}
+
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 int check_layout(const lstk_kv_layout *L, const char *fn) {
@@ -239,10 +256,14 @@ int lstk_cuda_set_wait_policy(uint64_t pipeline_wait_ns, const int32_t *start_fl
 }
 
 typedef void (*AppendKernel)(append::Params);
-// The kv_append instantiation for bf16 / f32 inputs and an f16 / f32 Q output; index bf16 * 2 + q16.
+// The kv_append instantiation for bf16 / f32 inputs, an f16 / f32 Q output and a q8_0 / f16
+// cache; index bf16 * 4 + q16 * 2 + q8.
 static AppendKernel append_kernel(int idx) {
-    static const AppendKernel k[4] = {append::kv_append_kernel<false, false>, append::kv_append_kernel<false, true>,
-                                      append::kv_append_kernel<true, false>, append::kv_append_kernel<true, true>};
+    using namespace append;
+    static const AppendKernel k[8] = {kv_append_kernel<false, false, false>, kv_append_kernel<false, false, true>,
+                                      kv_append_kernel<false, true, false>,  kv_append_kernel<false, true, true>,
+                                      kv_append_kernel<true, false, false>,  kv_append_kernel<true, false, true>,
+                                      kv_append_kernel<true, true, false>,   kv_append_kernel<true, true, true>};
     return k[idx];
 }
 
@@ -255,7 +276,7 @@ static int append_occupancy(DeviceInfo *dev, int idx, int rows) {
         std::lock_guard<std::mutex> lock(g_devices_mu);
         if (slot > 0) return slot;
     }
-    const int smem = append::smem_bytes(rows, idx >= 2);
+    const int smem = append::smem_bytes(rows, idx >= 4);
     int n = 0;
     const cudaError_t e =
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, append_kernel(idx), append::kWarps * 32, (size_t) smem);
@@ -266,12 +287,17 @@ static int append_occupancy(DeviceInfo *dev, int idx, int rows) {
     return n;
 }
 
-int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
-                        const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
-                        int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
-                        const int32_t *positions, const int64_t *cells, const float *q_gamma, const float *k_gamma,
-                        float eps, const float *rope_table, int32_t rope_n_pos, void *q_out, int32_t q_out_dtype,
-                        void *stream) {
+// The q8_0 planes of a K / V cache pair (lstk_cuda_kv_append_q8, lstk_cuda_attn_decode_q8).
+struct Q8Planes {
+    void *k_qs, *k_d, *v_qs, *v_d;
+};
+
+static int kv_append_impl(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const Q8Planes *q8,
+                          const void *q_in, const void *k_in, const void *v_in, int32_t in_dtype,
+                          int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens,
+                          int32_t n_head, const int32_t *positions, const int64_t *cells, const float *q_gamma,
+                          const float *k_gamma, float eps, const float *rope_table, int32_t rope_n_pos, void *q_out,
+                          int32_t q_out_dtype, void *stream) {
     int rc = check_layout(layout, "lstk_cuda_kv_append");
     if (rc) return rc;
     if (n_tokens < 0 || n_head <= 0 || n_head % layout->n_head_kv != 0)
@@ -294,6 +320,8 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     if (!aligned(q_in, 16) || !aligned(k_in, 16) || !aligned(v_in, 16) || !aligned(q_out, 16) ||
         !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(rope_table, 16))
         return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append: pointers must be 16-byte aligned");
+    if (q8 && (!aligned(q8->k_d, 8) || !aligned(q8->v_d, 8)))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append_q8: scale planes must be 8-byte aligned");
     if (n_tokens == 0) return clear_error();
     DeviceInfo *dev = nullptr;
     if ((rc = bind_device(k_cache, &dev))) return rc;
@@ -320,12 +348,16 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     p.n_cells = layout->n_cells;
     p.q_out = q_out;
     p.q_out_f16 = q_out_dtype == LSTK_DTYPE_F16;
+    p.k_qs = q8 ? static_cast<int8_t *>(q8->k_qs) : nullptr;
+    p.v_qs = q8 ? static_cast<int8_t *>(q8->v_qs) : nullptr;
+    p.k_d = q8 ? static_cast<__half *>(q8->k_d) : nullptr;
+    p.v_d = q8 ? static_cast<__half *>(q8->v_d) : nullptr;
     p.status = dev->status;
     // Rows per group: the largest (fewest steps and groups per row) that keeps at least four CTAs
     // (16 warps) resident per SM - the warps hide each other's latencies - and gives every resident
     // warp a group; short appends (decode steps), bound by one warp's chain of dependent steps, go
     // down to one step per group.
-    const int kidx = (p.in_bf16 ? 2 : 0) + (p.q_out_f16 ? 1 : 0);
+    const int kidx = (p.in_bf16 ? 4 : 0) + (p.q_out_f16 ? 2 : 0) + (q8 ? 1 : 0);
     if ((rc = ensure_smem(&dev->append_smem[kidx], append_kernel(kidx), append::kSmemBytes,
                           "cudaFuncSetAttribute(kv_append)")))
         return rc;
@@ -357,6 +389,30 @@ int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cac
     return launch_pdl_check(cudaLaunchKernelEx(&cfg, append_kernel(kidx), p), "kv_append_kernel");
 }
 
+int lstk_cuda_kv_append(const lstk_kv_layout *layout, void *k_cache, void *v_cache, const void *q_in,
+                        const void *k_in, const void *v_in, int32_t in_dtype, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens, int32_t n_head,
+                        const int32_t *positions, const int64_t *cells, const float *q_gamma, const float *k_gamma,
+                        float eps, const float *rope_table, int32_t rope_n_pos, void *q_out, int32_t q_out_dtype,
+                        void *stream) {
+    return kv_append_impl(layout, k_cache, v_cache, nullptr, q_in, k_in, v_in, in_dtype, q_row_stride, k_row_stride,
+                          v_row_stride, n_tokens, n_head, positions, cells, q_gamma, k_gamma, eps, rope_table,
+                          rope_n_pos, q_out, q_out_dtype, stream);
+}
+
+int lstk_cuda_kv_append_q8(const lstk_kv_layout *layout, int8_t *k_qs, void *k_d, int8_t *v_qs, void *v_d,
+                           const void *q_in, const void *k_in, const void *v_in, int32_t in_dtype,
+                           int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride, int32_t n_tokens,
+                           int32_t n_head, const int32_t *positions, const int64_t *cells, const float *q_gamma,
+                           const float *k_gamma, float eps, const float *rope_table, int32_t rope_n_pos, void *q_out,
+                           int32_t q_out_dtype, void *stream) {
+    if (!k_qs || !k_d || !v_qs || !v_d) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_kv_append_q8: NULL plane");
+    const Q8Planes q8 = {k_qs, k_d, v_qs, v_d};
+    return kv_append_impl(layout, k_qs, v_qs, &q8, q_in, k_in, v_in, in_dtype, q_row_stride, k_row_stride,
+                          v_row_stride, n_tokens, n_head, positions, cells, q_gamma, k_gamma, eps, rope_table,
+                          rope_n_pos, q_out, q_out_dtype, stream);
+}
+
 // Launches the split kernel and the combine kernel with programmatic stream serialization:
 // each grid can be scheduled while its predecessor in the stream finishes, and waits for it
 // (pdl_wait) before reading anything it produced.
@@ -367,8 +423,10 @@ struct ExchangeSpec {
     uint64_t wait_ns;
 };
 
-static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const decode::Params &p, int grid,
-                         size_t smem, cudaStream_t s, const ExchangeSpec *ex = nullptr) {
+// kdmap / vdmap: the scale-plane maps of a q8_0 cache (q8 true), else ignored.
+static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &kdmap,
+                         const CUtensorMap &vdmap, bool q8, const decode::Params &p, int grid, size_t smem,
+                         cudaStream_t s, const ExchangeSpec *ex = nullptr) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -379,8 +437,12 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int rc = launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_split_kernel, kmap, vmap, p),
-                              "decode_split_kernel");
+    int rc = q8 ? launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_split_kernel<true>, kmap, vmap, kdmap,
+                                                      vdmap, p),
+                                   "decode_split_kernel (q8_0)")
+                : launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_split_kernel<false>, kmap, vmap, kdmap,
+                                                      vdmap, p),
+                                   "decode_split_kernel");
     if (rc) return rc;
     decode::CombineParams c;
     c.n_seqs = p.n_seqs;
@@ -420,7 +482,8 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
                         int32_t q_dtype, int32_t n_seqs, int32_t n_head, const int32_t *block_tables,
                         int32_t max_blocks_per_seq, const int32_t *seq_lens, int32_t max_seq_len, int32_t kv_begin,
                         int32_t kv_end, float scale, float *out, float *lse_out, void *workspace,
-                        size_t workspace_bytes, int32_t n_ctas, void *stream, const ExchangeSpec *ex = nullptr) {
+                        size_t workspace_bytes, int32_t n_ctas, void *stream, const ExchangeSpec *ex = nullptr,
+                        const Q8Planes *q8 = nullptr) {
     int rc = check_layout(layout, "lstk_cuda_attn_decode");
     if (rc) return rc;
     const int hkv = layout->n_head_kv;
@@ -450,9 +513,28 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
     DeviceInfo *dev = nullptr;
     if ((rc = bind_device(k_cache, &dev))) return rc;
 
-    CUtensorMap kmap, vmap;
-    if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
-    if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+    CUtensorMap kmap, vmap, kdmap, vdmap;
+    int dpitch = 0;
+    if (q8) {
+        if (hkv % 2 != 0)
+            return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_attn_decode_q8: n_head_kv must be even (16-byte scale rows)");
+        if (!aligned(q8->k_qs, 16) || !aligned(q8->v_qs, 16) || !aligned(q8->k_d, 16) || !aligned(q8->v_d, 16))
+            return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_q8: planes must be 16-byte aligned");
+        dpitch = std::min(hkv, decode::kHeadsPerGroup) * 8;  // the scale tile's row: 4 f16 per head
+        if ((rc = encode_3d(&kmap, q8->k_qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, hkv, layout->n_cells, 128, 1, 32)))
+            return rc;
+        if ((rc = encode_3d(&vmap, q8->v_qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, hkv, layout->n_cells, 128, 1, 32)))
+            return rc;
+        if ((rc = encode_scales_2d(&kdmap, q8->k_d, (uint64_t) hkv * 4, layout->n_cells, (uint32_t) dpitch / 2)))
+            return rc;
+        if ((rc = encode_scales_2d(&vdmap, q8->v_d, (uint64_t) hkv * 4, layout->n_cells, (uint32_t) dpitch / 2)))
+            return rc;
+    } else {
+        if ((rc = encode_f16_3d(&kmap, k_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+        if ((rc = encode_f16_3d(&vmap, v_cache, 128, hkv, layout->n_cells, 64, 1, 32))) return rc;
+        kdmap = kmap;
+        vdmap = vmap;
+    }
 
     const int n_hg = (hkv + decode::kHeadsPerGroup - 1) / decode::kHeadsPerGroup;
     const int64_t max_groups = (int64_t) n_seqs * n_hg * ((max_seq_len + decode::kPage - 1) / decode::kPage);
@@ -483,12 +565,20 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
     p.status = dev->status;
     p.wait_ns = t_pipeline_wait_ns;
     p.start_flag = t_start_flag;
+    p.q8_dpitch = dpitch;
 
     const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
                         16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
-    if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel, smem, "cudaFuncSetAttribute(decode)")))
+    if (q8) {
+        if ((rc = ensure_smem(&dev->decode_q8_smem, decode::decode_split_kernel<true>, smem,
+                              "cudaFuncSetAttribute(decode q8_0)")))
+            return rc;
+    } else if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel<false>, smem,
+                                 "cudaFuncSetAttribute(decode)"))) {
         return rc;
-    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream), ex);
+    }
+    return launch_decode(kmap, vmap, kdmap, vdmap, q8 != nullptr, p, (int) grid, smem,
+                         static_cast<cudaStream_t>(stream), ex);
 }
 
 int lstk_cuda_attn_decode(const lstk_kv_layout *layout, const void *k_cache, const void *v_cache, const void *q,
@@ -533,6 +623,19 @@ int lstk_cuda_attn_decode_exchange(const lstk_kv_layout *layout, const void *k_c
     return decode_range(layout, k_cache, v_cache, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq,
                         seq_lens, max_seq_len, 0, INT32_MAX, scale, out, lse_out, workspace, workspace_bytes, n_ctas,
                         stream, &ex);
+}
+
+int lstk_cuda_attn_decode_q8(const lstk_kv_layout *layout, const int8_t *k_qs, const void *k_d, const int8_t *v_qs,
+                             const void *v_d, const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                             const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
+                             int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
+                             size_t workspace_bytes, int32_t n_ctas, void *stream) {
+    if (!k_qs || !k_d || !v_qs || !v_d) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_decode_q8: NULL plane");
+    const Q8Planes q8 = {const_cast<int8_t *>(k_qs), const_cast<void *>(k_d), const_cast<int8_t *>(v_qs),
+                         const_cast<void *>(v_d)};
+    return decode_range(layout, k_qs, v_qs, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq, seq_lens,
+                        max_seq_len, 0, INT32_MAX, scale, out, lse_out, workspace, workspace_bytes, n_ctas, stream,
+                        nullptr, &q8);
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,
@@ -999,12 +1102,13 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     p.status = dev->status;
     p.wait_ns = t_pipeline_wait_ns;
     p.start_flag = t_start_flag;
+    p.q8_dpitch = 0;
 
     const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
                         16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
-    if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel, smem, "cudaFuncSetAttribute(decode)")))
+    if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel<false>, smem, "cudaFuncSetAttribute(decode)")))
         return rc;
-    return launch_decode(kmap, vmap, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
+    return launch_decode(kmap, vmap, kmap, vmap, false, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

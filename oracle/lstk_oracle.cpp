@@ -420,6 +420,155 @@ void orc_paged_decode_ggml_fast(const float *q, int n_seqs, int n_head, const ui
     });
 }
 
+// ---- q8_0 KV cache (the reference's planned option, docs/plan.md:389-395) ----------------------
+// Quantisation of ggml's block_q8_0 (ggml-quants quantize_row_q8_0): per 32 consecutive values
+// amax = max |x|, d = amax / 127, id = d ? 1 / d : 0, q = round(x * id) as int8 and the f16 of d
+// kept as the block's scale. The rounding is to nearest with ties to even, as the ARM NEON form
+// (vcvtnq_s32_f32) computes it on the reference's platform (the generic C form rounds ties away
+// from zero). The cache keeps ggml's values in two planes: qs int8 [n_cells][n_head_kv][D] and
+// d f16 bits [n_cells][n_head_kv][D / 32].
+static void quantize_q8_0_row(const float *x, int n, int8_t *qs, uint16_t *d) {
+    for (int b = 0; b < n / 32; b++) {
+        float amax = 0.0f;
+        for (int j = 0; j < 32; j++) amax = std::max(amax, std::fabs(x[b * 32 + j]));
+        const float dd = amax / 127.0f;
+        const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+        d[b] = f32_to_f16_bits(dd);
+        for (int j = 0; j < 32; j++) qs[b * 32 + j] = (int8_t) std::lrintf(x[b * 32 + j] * id);
+    }
+}
+
+int orc_quantize_q8_0(const float *x, int64_t n_rows, int row_elems, int8_t *qs, uint16_t *d) {
+    if (row_elems % 32) return -1;
+    for (int64_t r = 0; r < n_rows; r++)
+        quantize_q8_0_row(x + r * row_elems, row_elems, qs + r * row_elems, d + r * (row_elems / 32));
+    return 0;
+}
+
+// orc_kv_append with the K and V rows stored as q8_0 planes instead of f16 rows.
+int orc_kv_append_q8(const void *q_in, const void *k_in, const void *v_in, int in_dtype, int64_t q_stride,
+                     int64_t k_stride, int64_t v_stride, int n_tokens, int n_head, int n_head_kv, int head_dim,
+                     const int32_t *positions, const int64_t *cells, const float *q_gamma, const float *k_gamma,
+                     float eps, float freq_base, float freq_scale, int8_t *k_qs, uint16_t *k_d, int8_t *v_qs,
+                     uint16_t *v_d, int64_t n_cells, float *q_out) {
+    auto load = [&](const void *base, int64_t off) -> float {
+        if (in_dtype == ORC_BF16) return bf16_bits_to_f32(((const uint16_t *) base)[off]);
+        return ((const float *) base)[off];
+    };
+    if (head_dim % 32) return -1;
+    std::vector<float> row(head_dim), normed(head_dim), cs(head_dim);
+    for (int t = 0; t < n_tokens; t++) {
+        if (cells[t] < 0 || cells[t] >= n_cells) return -1;
+        rope_cache(positions[t], head_dim, freq_base, freq_scale, cs.data());
+        for (int h = 0; h < n_head; h++) {
+            for (int i = 0; i < head_dim; i++) row[i] = load(q_in, t * q_stride + (int64_t) h * head_dim + i);
+            if (q_gamma) rms_norm_mul_row(row.data(), normed.data(), head_dim, q_gamma, eps);
+            else normed = row;
+            rope_neox_row(normed.data(), head_dim, cs.data());
+            std::memcpy(q_out + ((int64_t) t * n_head + h) * head_dim, normed.data(), sizeof(float) * head_dim);
+        }
+        for (int h = 0; h < n_head_kv; h++) {
+            const int64_t r = cells[t] * n_head_kv + h;
+            for (int i = 0; i < head_dim; i++) row[i] = load(k_in, t * k_stride + (int64_t) h * head_dim + i);
+            if (k_gamma) rms_norm_mul_row(row.data(), normed.data(), head_dim, k_gamma, eps);
+            else normed = row;
+            rope_neox_row(normed.data(), head_dim, cs.data());
+            quantize_q8_0_row(normed.data(), head_dim, k_qs + r * head_dim, k_d + r * (head_dim / 32));
+            for (int i = 0; i < head_dim; i++) row[i] = load(v_in, t * v_stride + (int64_t) h * head_dim + i);
+            quantize_q8_0_row(row.data(), head_dim, v_qs + r * head_dim, v_d + r * (head_dim / 32));
+        }
+    }
+    return 0;
+}
+
+// Page-table attention over a q8_0 cache (orc_paged_attn's visibility and arguments otherwise).
+// ORC_MODE_GGML follows ggml's CPU flash_attn_ext for a q8_0 K / V cache: the query row is itself
+// quantised to q8_0 (K's vec_dot type), a score is sum over blocks of the block's integer dot
+// product times (d_k * d_q) in block order, scaled; softmax online with expf; V rows dequantised
+// to f32 (d * q) and accumulated in f32 (the non-f16 V path). ORC_MODE_EXACT: f32 query, the
+// dequantised K and V, softmax and accumulation in double.
+void orc_paged_attn_q8(const float *q, int n_q, const int32_t *q_seq, const int32_t *q_pos, int n_head,
+                       const int8_t *k_qs, const uint16_t *k_d, const int8_t *v_qs, const uint16_t *v_d,
+                       int n_head_kv, int head_dim, int block_size, const int32_t *block_tables, int max_blocks,
+                       const int32_t *kv_lens, int causal, float scale, int mode, float *out, float *lse_out,
+                       int n_threads) {
+    const int group = n_head / n_head_kv;
+    const int nb = head_dim / 32;
+    parallel_for((int64_t) n_q * n_head, n_threads, [&](int64_t task) {
+        const int r = (int) (task / n_head);
+        const int h = (int) (task % n_head);
+        const int kvh = h / group;
+        const int b = q_seq[r];
+        int64_t n_keys = kv_lens[b];
+        if (causal) n_keys = std::min<int64_t>(n_keys, (int64_t) q_pos[r] + 1);
+        if (n_keys < 0) n_keys = 0;
+        const int32_t *bt = block_tables + (int64_t) b * max_blocks;
+        const float *qr = q + ((int64_t) r * n_head + h) * head_dim;
+        float *o = out + ((int64_t) r * n_head + h) * head_dim;
+        auto cell_row = [&](int64_t p) {
+            return ((int64_t) bt[p / block_size] * block_size + p % block_size) * n_head_kv + kvh;
+        };
+        if (mode == ORC_MODE_GGML) {
+            std::vector<int8_t> qq(head_dim);
+            std::vector<uint16_t> qd(nb);
+            quantize_q8_0_row(qr, head_dim, qq.data(), qd.data());
+            std::vector<float> acc(head_dim, 0.0f), v32(head_dim);
+            float S = 0.0f, M = -INFINITY;
+            for (int64_t p = 0; p < n_keys; p++) {
+                const int64_t row = cell_row(p);
+                const int8_t *kq = k_qs + row * head_dim;
+                const uint16_t *kd = k_d + row * nb;
+                float s = 0.0f;
+                for (int blk = 0; blk < nb; blk++) {
+                    int sumi = 0;
+                    for (int j = 0; j < 32; j++) sumi += (int) kq[blk * 32 + j] * (int) qq[blk * 32 + j];
+                    s += (float) sumi * (f16_bits_to_f32(kd[blk]) * f16_bits_to_f32(qd[blk]));
+                }
+                s = s * scale;
+                const float Mold = M;
+                float ms = 1.0f, vs = 1.0f;
+                if (s > M) {
+                    M = s;
+                    ms = expf(Mold - M);
+                    for (int d = 0; d < head_dim; d++) acc[d] *= ms;
+                } else {
+                    vs = expf(s - M);
+                }
+                const int8_t *vq = v_qs + row * head_dim;
+                const uint16_t *vd = v_d + row * nb;
+                for (int d = 0; d < head_dim; d++) v32[d] = f16_bits_to_f32(vd[d / 32]) * (float) vq[d];
+                for (int d = 0; d < head_dim; d++) acc[d] = fmaf(v32[d], vs, acc[d]);
+                S = S * ms + vs;
+            }
+            const float S_inv = S == 0.0f ? 0.0f : 1.0f / S;
+            for (int d = 0; d < head_dim; d++) o[d] = acc[d] * S_inv;
+            if (lse_out) lse_out[(int64_t) r * n_head + h] = S == 0.0f ? -INFINITY : (float) ((double) M + std::log((double) S));
+            return;
+        }
+        std::vector<double> s(n_keys);
+        double m = -INFINITY;
+        for (int64_t p = 0; p < n_keys; p++) {
+            const int64_t row = cell_row(p);
+            double dot = 0.0;
+            for (int d = 0; d < head_dim; d++)
+                dot += (double) f16_bits_to_f32(k_d[row * nb + d / 32]) * (double) k_qs[row * head_dim + d] * (double) qr[d];
+            s[p] = dot * (double) scale;
+            m = std::max(m, s[p]);
+        }
+        std::vector<double> acc(head_dim, 0.0);
+        double l = 0.0;
+        for (int64_t p = 0; p < n_keys; p++) {
+            const int64_t row = cell_row(p);
+            const double w = std::exp(s[p] - m);
+            l += w;
+            for (int d = 0; d < head_dim; d++)
+                acc[d] += w * (double) f16_bits_to_f32(v_d[row * nb + d / 32]) * (double) v_qs[row * head_dim + d];
+        }
+        for (int d = 0; d < head_dim; d++) o[d] = l > 0.0 ? (float) (acc[d] / l) : 0.0f;
+        if (lse_out) lse_out[(int64_t) r * n_head + h] = l > 0.0 ? (float) (m + std::log(l)) : -INFINITY;
+    });
+}
+
 int orc_hardware_threads(void) { return (int) std::thread::hardware_concurrency(); }
 
 }  // extern "C"

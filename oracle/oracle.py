@@ -58,6 +58,13 @@ def lib():
         L.orc_lse_merge.argtypes = [_P, _P, _I, _I64, _I, _P, _P]
         L.orc_paged_decode_ggml_fast.argtypes = [_P, _I, _I, _P, _P, _I, _I, _I, _P, _I, _P, _F, _P, _I]
         L.orc_hardware_threads.restype = _I
+        L.orc_quantize_q8_0.argtypes = [_P, _I64, _I, _P, _P]
+        L.orc_quantize_q8_0.restype = _I
+        L.orc_kv_append_q8.argtypes = [_P, _P, _P, _I, _I64, _I64, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _F, _F, _F,
+                                       _P, _P, _P, _P, _I64, _P]
+        L.orc_kv_append_q8.restype = _I
+        L.orc_paged_attn_q8.argtypes = [_P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P, _I, _F, _I, _P,
+                                        _P, _I]
         _lib = L
     return _lib
 
@@ -128,6 +135,69 @@ def kv_append(q_in, k_in, v_in, positions, cells, k_cache, v_cache, q_gamma=None
     if rc != 0:
         raise ValueError("oracle kv_append: cell index out of range")
     return q_out
+
+
+def quantize_q8_0(x):
+    """ggml q8_0 of each row of x [..., D] f32 (D a multiple of 32): (qs int8 [..., D],
+    d uint16 f16 bits [..., D // 32]); ties round to even (the ARM NEON form)."""
+    x = _c(x, np.float32)
+    D = x.shape[-1]
+    n_rows = x.size // D
+    qs = np.empty(x.shape, np.int8)
+    d = np.empty(x.shape[:-1] + (D // 32,), np.uint16)
+    if lib().orc_quantize_q8_0(_ptr(x), n_rows, D, _ptr(qs), _ptr(d)) != 0:
+        raise ValueError("row length must be a multiple of 32")
+    return qs, d
+
+
+def dequantize_q8_0(qs, d):
+    """f32 values d * q of q8_0 planes (qs [..., D] int8, d [..., D // 32] f16 bits)."""
+    scale = f16_bits_to_f32(np.asarray(d, np.uint16))
+    return (np.repeat(scale, 32, axis=-1) * qs.astype(np.float32)).astype(np.float32)
+
+
+def kv_append_q8(q_in, k_in, v_in, positions, cells, k_qs, k_d, v_qs, v_d, q_gamma=None, k_gamma=None, eps=1e-6,
+                 freq_base=1e6, freq_scale=1.0, in_dtype="f32"):
+    """kv_append with K and V stored as q8_0 planes: k_qs / v_qs int8 [n_cells][Hkv][D] and
+    k_d / v_d uint16 f16 bits [n_cells][Hkv][D // 32], updated in place. Returns q_out f32."""
+    dt = np.uint16 if in_dtype == "bf16" else np.float32
+    q_in, k_in, v_in = _c(q_in, dt), _c(k_in, dt), _c(v_in, dt)
+    T, Hq, D = q_in.shape
+    Hkv = k_in.shape[1]
+    positions, cells = _c(positions, np.int32), _c(cells, np.int64)
+    for a, t in ((k_qs, np.int8), (v_qs, np.int8), (k_d, np.uint16), (v_d, np.uint16)):
+        assert a.dtype == t and a.flags.c_contiguous
+    qg = _c(q_gamma, np.float32) if q_gamma is not None else None
+    kg = _c(k_gamma, np.float32) if k_gamma is not None else None
+    q_out = np.empty((T, Hq, D), np.float32)
+    rc = lib().orc_kv_append_q8(_ptr(q_in), _ptr(k_in), _ptr(v_in), 2 if in_dtype == "bf16" else 0, Hq * D,
+                                Hkv * D, Hkv * D, T, Hq, Hkv, D, _ptr(positions), _ptr(cells), _ptr(qg), _ptr(kg), eps,
+                                freq_base, freq_scale, _ptr(k_qs), _ptr(k_d), _ptr(v_qs), _ptr(v_d), k_qs.shape[0],
+                                _ptr(q_out))
+    if rc != 0:
+        raise ValueError("oracle kv_append_q8: cell index out of range")
+    return q_out
+
+
+def paged_attn_q8(q, q_seq, q_pos, k_qs, k_d, v_qs, v_d, block_tables, kv_lens, scale, causal=True, mode=MODE_GGML,
+                  block_size=32, n_threads=0, want_lse=False):
+    """paged_attn over a q8_0 cache (planes as in kv_append_q8). MODE_GGML: ggml's CPU semantics
+    for a q8_0 cache (query quantised to q8_0, integer block dots, f32 V accumulation);
+    MODE_EXACT: f32 query against the dequantised cache, in double."""
+    q = _c(q, np.float32)
+    n_q, Hq, D = q.shape
+    Hkv = k_qs.shape[1]
+    q_seq, q_pos = _c(q_seq, np.int32), _c(q_pos, np.int32)
+    bt = _c(block_tables, np.int32)
+    kv_lens = _c(kv_lens, np.int32)
+    k_qs, v_qs = _c(k_qs, np.int8), _c(v_qs, np.int8)
+    k_d, v_d = _c(k_d, np.uint16), _c(v_d, np.uint16)
+    out = np.empty_like(q)
+    lse = np.empty((n_q, Hq), np.float32) if want_lse else None
+    lib().orc_paged_attn_q8(_ptr(q), n_q, _ptr(q_seq), _ptr(q_pos), Hq, _ptr(k_qs), _ptr(k_d), _ptr(v_qs), _ptr(v_d),
+                            Hkv, D, block_size, _ptr(bt), bt.shape[1], _ptr(kv_lens), 1 if causal else 0, scale, mode,
+                            _ptr(out), _ptr(lse), n_threads)
+    return (out, lse) if want_lse else out
 
 
 def flash_attn_ext(q, k_cache, v_cache, n_kv, mask, scale, mode=MODE_EXACT, n_threads=0):
