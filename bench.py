@@ -188,6 +188,68 @@ def decode_step(L, w, q_in=None, k_in=None, v_in=None, pos=None, cells=None, bt=
                   out=out if out is not None else w["out"], workspace=w["ws"])
 
 
+def config3_q8(L, w, steps, warmup, dev, world):
+    """Config 3's decode step over a q8_0 KV cache (the reference's planned option): the same
+    sequences, block tables and queries, K / V as q8_0 planes (random int8 values and scales; the
+    kernels' speed does not depend on them); per step the append quantises the new rows and the
+    decode reads the planes. Same timing as the headline (eager steps, events, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    n_cells = w["kc"].shape[0]
+    g = torch.Generator(device=dev).manual_seed(33)
+    kq, vq = L.Q8Cache(n_cells, HKV, dev), L.Q8Cache(n_cells, HKV, dev)
+    for c in (kq, vq):
+        c.qs.copy_(torch.randint(-127, 128, c.qs.shape, generator=g, device=dev, dtype=torch.int8))
+        c.d.copy_((torch.rand(c.d.shape, generator=g, device=dev) * 0.02 + 0.005).half())
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        L.kv_append_q8(kq, vq, w["q_in"], w["k_in"], w["v_in"], w["pos"], w["cells"], w["rope"], w["gamma"],
+                       w["gamma"], 1e-6, q_out=w["q_out"])
+        if ev is not None:
+            ev[0].record(stream)
+        L.attn_decode_q8(kq, vq, w["q_out"], w["bt"], w["lens"], SCALE, max_seq_len=w["max_len"], out=w["out"],
+                         workspace=w["ws"])
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(warmup):
+        step()
+    L.check_status()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(steps):
+        step(evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    L.check_status()
+    ms = t0.elapsed_time(t1) / steps
+    dec_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    keys = float(np.asarray(w["lens_host"], np.float64).sum())
+    q8_bytes = keys * HKV * (D + 8) * 2  # int8 values + four f16 scales per row, K and V
+    t = torch.tensor([ms, dec_ms, q8_bytes, float(len(w["lens_host"]))], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t[:2].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t[2:].clone()
+        dist.all_reduce(sm)
+        t = torch.cat([mx, sm])
+    ms, dec_ms, all_bytes, n_seqs = (float(x) for x in t)
+    del kq, vq
+    torch.cuda.empty_cache()
+    return {"ms_per_step": round(ms, 4), "tokens_per_s": round(n_seqs / (ms / 1e3), 1),
+            "gbs": round(all_bytes / (ms / 1e3) / 1e9, 1), "decode_ms": round(dec_ms, 4),
+            "decode_gbs_per_gpu": round(all_bytes / world / (dec_ms / 1e3) / 1e9, 1),
+            "kv_bytes_vs_f16": round((D + 8) / (2 * D), 4),
+            "note": "q8_0 planes (ggml block_q8_0 values): 136 bytes per 128-value row against 256 for f16; "
+                    "gbs counts the q8_0 bytes read"}
+
+
 def cpu_baseline_sample(w, budget_s=12.0):
     """The oracle's page-table decode (ggml CPU precision model, all host threads) on the first
     sequences of the same batch, sized to roughly `budget_s` of CPU work."""
@@ -433,6 +495,8 @@ def run_b200(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t[0])
 
+    q8 = None if args.no_secondary else config3_q8(L, w, max(20, args.steps // 4), args.warmup, dev, world)
+
     weak = None
     if world > 1 and not args.no_secondary:
         # weak scaling beside the headline: 64 sequences per GPU (64 x world drawn, split by LPT)
@@ -492,6 +556,9 @@ def run_b200(args):
             line["secondary"] = secondary(L, dev, tc_peak, hbm_peak)
             if weak is not None:
                 line["secondary"]["config3_weak"] = weak
+            if q8 is not None:
+                q8["tokens_per_s_vs_f16_cache"] = round(q8["tokens_per_s"] / line["tokens_per_s"], 3)
+                line["secondary"]["config3_q8_kv"] = q8
             if c4_split is not None:
                 line["secondary"]["config4_kv_split"] = c4_split
             if c5 is not None:

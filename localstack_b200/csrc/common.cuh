@@ -33,6 +33,7 @@ enum : int {
     kSiteDecodeWaitFull = 12,
     kSiteDecodeWaitEmpty = 13,
     kSiteDecodeWaitStart = 14,
+    kSiteDecodeWaitMerge = 15,
     kSitePrefillPage = 20,
     kSitePrefillWait = 21,
     kSitePrefillSmem = 22,

@@ -261,6 +261,27 @@ constexpr int kQ8VOff = kHeadsPerGroup * kQ8HeadPage;    // 16 KiB
 constexpr int kQ8KdOff = 2 * kHeadsPerGroup * kQ8HeadPage;
 constexpr int kQ8VdOff = kQ8KdOff + kPage * 32;          // scale rows of up to 32 bytes
 
+// Split-kernel shapes. f16: 4 consumer warps (one per KV head of the group, both 16-token slabs of
+// a page), 3 stages of 64 KiB. q8_0: a page costs half the bytes and more instructions per byte,
+// so 8 consumer warps - warp w takes KV head w % 4 and slab w / 4 of every page - and 4 stages of
+// 35 KiB; the two warps of a head merge their softmax states through shared memory at the end of
+// each piece (kMergeBytes: per head, 32 lanes x (2 maxima, 2 sums, 32 accumulators)).
+template <bool kQ8>
+struct SplitCfg {
+    static constexpr int kConsumers = kQ8 ? 8 : kConsumerWarps;
+    static constexpr int kThreads = (kConsumers + 1) * 32;
+    static constexpr int kStages = kQ8 ? 4 : decode::kStages;
+    static constexpr int kStageBytes = kQ8 ? 35 * 1024 : decode::kStageBytes;
+    static constexpr int kMergeBytes = kQ8 ? kHeadsPerGroup * 32 * 36 * 4 : 0;
+    static constexpr int kBarriers = 2 * kStages + (kQ8 ? 2 * kHeadsPerGroup : 0);
+};
+// Dynamic shared memory of the split kernel for n_seqs sequences.
+template <bool kQ8>
+__host__ __device__ constexpr size_t split_smem_bytes(int n_seqs) {
+    return 1024 + (size_t) SplitCfg<kQ8>::kStages * SplitCfg<kQ8>::kStageBytes + SplitCfg<kQ8>::kMergeBytes +
+           sizeof(uint64_t) * SplitCfg<kQ8>::kBarriers + 16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
+}
+
 __device__ __forceinline__ void mma_16832_s8(int c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
@@ -356,12 +377,11 @@ __device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t r, uint32_t &even, uint
 // block, rounded to f16 like P itself), so O^T += V^T . P'^T per 16-dim m-tile; the tile's rows
 // are dims 2g, 2g + 1 of its 16 (the pairs ldmatrix.trans delivers).
 __device__ __forceinline__ void process_page_q8(HeadStateQ8 &st, uint32_t kbase, uint32_t vbase, const uint8_t *kd,
-                                                const uint8_t *vd, int dpitch, int valid, float scale_log2,
-                                                int lane) {
+                                                const uint8_t *vd, int dpitch, int valid, float scale_log2, int lane,
+                                                int slab_lo, int slab_hi) {
     const int g = lane >> 2, t = lane & 3;
     const int li = lane >> 3, lr = lane & 7;
-#pragma unroll
-    for (int slab = 0; slab < 2; slab++) {
+    for (int slab = slab_lo; slab < slab_hi; slab++) {
         if (slab * 16 >= valid) break;
         const int tok0 = slab * 16 + g;
         int sb[4][4];
@@ -461,7 +481,7 @@ extern __shared__ __align__(1024) uint8_t dyn_smem[];
 // kQ8: the cache is q8_0 planes (kmap / vmap over the qs planes, kdmap / vdmap over the scale
 // planes); else f16 rows (kmap / vmap; the scale maps are unused).
 template <bool kQ8>
-__global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
                                                                     const __grid_constant__ CUtensorMap kdmap,
                                                                     const __grid_constant__ CUtensorMap vdmap,
@@ -470,13 +490,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     const int warp = threadIdx.x >> 5;
 
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+    constexpr int kConsumers = SplitCfg<kQ8>::kConsumers;
+    constexpr int kNThreads = SplitCfg<kQ8>::kThreads;
+    constexpr int kNStages = SplitCfg<kQ8>::kStages;
+    constexpr int kSBytes = SplitCfg<kQ8>::kStageBytes;
     uint8_t *stages = base;
-    uint64_t *full = reinterpret_cast<uint64_t *>(base + kStages * kStageBytes);
-    uint64_t *empty = full + kStages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
-    int32_t *pfx = reinterpret_cast<int32_t *>(empty + kStages) + 4;
+    float *merge_buf = reinterpret_cast<float *>(base + kNStages * kSBytes);  // q8_0: the second warps' states
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + kNStages * kSBytes + SplitCfg<kQ8>::kMergeBytes);
+    uint64_t *empty = full + kNStages;
+    uint64_t *merge_ready = empty + kNStages;  // q8_0, per head: the slab-1 warp's state is in merge_buf
+    uint64_t *merge_taken = merge_ready + kHeadsPerGroup;  // q8_0, per head: the slab-0 warp has read it
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(full + SplitCfg<kQ8>::kBarriers);
+    int32_t *pfx = reinterpret_cast<int32_t *>(full + SplitCfg<kQ8>::kBarriers) + 4;
 
-    __shared__ int32_t stage_pid[kStages];  // page id of each stage's page-group (producer -> consumers)
+    __shared__ int32_t stage_pid[kNStages];  // page id of each stage's page-group (producer -> consumers)
     // Inputs (q, seq_lens, tables, pages) may come from the previous kernel in the stream; the
     // combine grid may be scheduled right away (it waits for this grid to complete).
     pdl_wait();
@@ -484,9 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
     // Prefix over sequences of page counts (every CTA computes it; CTA 0 publishes it): thread t
     // sums the pages of its run of sequences, a block-wide scan (warp shuffles, then the warps'
     // totals) gives each run's start.
-    __shared__ int32_t warp_tot[kThreads / 32];
+    __shared__ int32_t warp_tot[kNThreads / 32];
     {
-        const int per = (p.n_seqs + kThreads - 1) / kThreads;
+        const int per = (p.n_seqs + kNThreads - 1) / kNThreads;
         const int b0 = threadIdx.x * per;
         int32_t local = 0;
         for (int b = b0; b < min(b0 + per, p.n_seqs); b++) {
@@ -508,25 +535,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             pfx[b] = acc;
             acc += (range_len(p, p.seq_lens[b]) + kPage - 1) / kPage;
         }
-        if (threadIdx.x == kThreads - 1) pfx[p.n_seqs] = acc;
+        if (threadIdx.x == kNThreads - 1) pfx[p.n_seqs] = acc;
         if (threadIdx.x == 0) {
             *abort_flag = 0;
-            for (int s = 0; s < kStages; s++) {
+            for (int s = 0; s < kNStages; s++) {
                 mbar_init(smem_u32(&full[s]), 1);
-                mbar_init(smem_u32(&empty[s]), kConsumerWarps);
+                mbar_init(smem_u32(&empty[s]), kConsumers);
             }
+            if constexpr (kQ8)
+                for (int h = 0; h < kHeadsPerGroup; h++) {
+                    mbar_init(smem_u32(&merge_ready[h]), 1);
+                    mbar_init(smem_u32(&merge_taken[h]), 1);
+                }
             fence_barrier_init();
         }
         __syncthreads();
         if (blockIdx.x == 0)
-            for (int b = threadIdx.x; b <= p.n_seqs; b += kThreads) p.prefix[b] = pfx[b];
+            for (int b = threadIdx.x; b <= p.n_seqs; b += kNThreads) p.prefix[b] = pfx[b];
     }
 
     const int64_t P = (int64_t) p.n_hg * pfx[p.n_seqs];
     const int64_t lo = range_lo(blockIdx.x, P, gridDim.x);
     const int64_t hi = range_lo(blockIdx.x + 1, P, gridDim.x);
 
-    if (lo < hi && warp == kConsumerWarps) {
+    if (lo < hi && warp == kConsumers) {
         // Producer warp: the whole warp reads the block-table entries of the CTA's page-groups, 32
         // at a time and one batch ahead (lane i: page-group xb + i), so no copy waits on a table
         // read; lane 0 streams the page-groups through the stage ring, handing each stage's page id
@@ -574,8 +606,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             if (lane == 0) {
                 const int cnt = (int) (hi - xb < 32 ? hi - xb : 32);
                 for (int e = 0; e < cnt; e++, i++) {
-                    const int s = (int) (i % kStages);
-                    const uint32_t k_use = (uint32_t) (i / kStages);
+                    const int s = (int) (i % kNStages);
+                    const uint32_t k_use = (uint32_t) (i / kNStages);
                     if (k_use > 0 &&
                         !mbar_wait_bounded(smem_u32(&empty[s]), (k_use - 1) & 1, abort_flag, p.wait_ns)) {
                         report(p.status, kStatusTimeout, kSiteDecodeWaitEmpty, s);
@@ -593,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                         mbar_arrive(fb);
                     } else if constexpr (kQ8) {
                         mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kQ8HeadPage + 2 * kPage * p.q8_dpitch));
-                        const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                        const uint32_t sb = smem_u32(stages + (size_t) s * kSBytes);
                         for (int h = 0; h < nh; h++) {
                             const int kvh = hg * kHeadsPerGroup + h;
                             tma_load_3d_hint(sb + h * kQ8HeadPage, &kmap, fb, 0, kvh, pid * kPage, policy);
@@ -604,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                         tma_load_2d(sb + kQ8VdOff, &vdmap, fb, hg * 16, pid * kPage);
                     } else {
                         mbar_arrive_expect_tx(fb, (uint32_t) (2 * nh * kHeadPage));
-                        const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                        const uint32_t sb = smem_u32(stages + (size_t) s * kSBytes);
                         for (int h = 0; h < nh; h++) {
                             const int kvh = hg * kHeadsPerGroup + h;
                             for (int half = 0; half < 2; half++) {
@@ -622,11 +654,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         if (lane == 0 && (!ok || *abort_flag)) {
             // Let every copy already issued land before the CTA's shared memory goes away.
             const int64_t n_issued = i;
-            for (int64_t j = n_issued > kStages ? n_issued - kStages : 0; j < n_issued; j++)
-                mbar_wait_bounded(smem_u32(&full[j % kStages]), (uint32_t) (j / kStages) & 1, nullptr);
+            for (int64_t j = n_issued > kNStages ? n_issued - kNStages : 0; j < n_issued; j++)
+                mbar_wait_bounded(smem_u32(&full[j % kNStages]), (uint32_t) (j / kNStages) & 1, nullptr);
         }
     } else if (lo < hi) {
-        // Consumers: warp w owns KV head hg*4 + w of every page-group.
+        // Consumers: warp w owns KV head hg*4 + w % 4 of every page-group (q8_0: slab w / 4 of it).
+        const int hw = warp % kHeadsPerGroup;
+        const int half = warp / kHeadsPerGroup;  // 0, or 1 for the second warp of a head (q8_0)
+        int64_t n_pieces = 0;                    // pieces finished (phases of the merge barriers)
         typename std::conditional<kQ8, HeadStateQ8, HeadState>::type st;
         Cursor cur;
         cur.locate(lo, pfx, p.n_seqs, p.n_hg);
@@ -635,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
         int len = 0;  // keys of the current segment's sequence inside the call's range
         for (int64_t x = lo; x < hi; x++, i++) {
             const int np = pfx[cur.b + 1] - pfx[cur.b];
-            const int kvh = cur.hg * kHeadsPerGroup + warp;
+            const int kvh = cur.hg * kHeadsPerGroup + hw;
             const bool active = kvh < p.n_head_kv;
             if (x == lo || cur.p == 0) {
                 piece_start = x;
@@ -646,9 +681,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                 }
                 len = range_len(p, p.seq_lens[cur.b]);
             }
-            const int s = (int) (i % kStages);
+            const int s = (int) (i % kNStages);
             // Warp-uniform outcome: ldmatrix / mma.sync below are warp-collective.
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full[s]), (uint32_t) (i / kStages) & 1,
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&full[s]), (uint32_t) (i / kNStages) & 1,
                                                              abort_flag, p.wait_ns))) {
                 if (lane == 0) {
                     report(p.status, kStatusTimeout, kSiteDecodeWaitFull, s);
@@ -659,12 +694,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
             const int32_t pid = stage_pid[s];
             if (active && pid >= 0 && pid < p.n_pages) {
                 const int valid = min(kPage, len - cur.p * kPage);
-                const uint32_t sb = smem_u32(stages + (size_t) s * kStageBytes);
+                const uint32_t sb = smem_u32(stages + (size_t) s * kSBytes);
                 if constexpr (kQ8) {
-                    const uint8_t *st_base = stages + (size_t) s * kStageBytes;
-                    process_page_q8(st, sb + warp * kQ8HeadPage, sb + kQ8VOff + warp * kQ8HeadPage,
-                                    st_base + kQ8KdOff + warp * 8, st_base + kQ8VdOff + warp * 8, p.q8_dpitch, valid,
-                                    p.scale_log2, lane);
+                    const uint8_t *st_base = stages + (size_t) s * kSBytes;
+                    process_page_q8(st, sb + hw * kQ8HeadPage, sb + kQ8VOff + hw * kQ8HeadPage,
+                                    st_base + kQ8KdOff + hw * 8, st_base + kQ8VdOff + hw * 8, p.q8_dpitch, valid,
+                                    p.scale_log2, lane, half, half + 1);
                 } else {
                     process_page(st, sb + warp * kHeadPage, sb + kHeadsPerGroup * kHeadPage + warp * kHeadPage,
                                  valid, p.scale_log2, lane);
@@ -675,6 +710,59 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
 
             if (cur.p == np - 1 || x == hi - 1) {
                 // Piece ends: finish the softmax sums and write the (partial) result.
+                if constexpr (kQ8) {
+                    // The slab-1 warp hands its state to the slab-0 warp of its head, which merges:
+                    // M = max(m_a, m_b), O = O_a 2^(m_a - M) + O_b 2^(m_b - M), the same for the sums.
+                    float *mb = merge_buf + (hw * 32 + lane) * 36;
+                    const uint32_t par = (uint32_t) (n_pieces & 1);
+                    bool ok = true;
+                    if (half == 1) {
+                        if (n_pieces > 0)
+                            ok = mbar_wait_bounded(smem_u32(&merge_taken[hw]), par ^ 1u, abort_flag, p.wait_ns);
+                        ok = __all_sync(0xffffffffu, ok);  // warp-uniform: __syncwarp below
+                        if (ok) {
+                            mb[0] = st.m[0], mb[1] = st.m[1], mb[2] = st.l[0], mb[3] = st.l[1];
+#pragma unroll
+                            for (int mt = 0; mt < 8; mt++)
+#pragma unroll
+                                for (int j = 0; j < 4; j++) mb[4 + mt * 4 + j] = st.o[mt][j];
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(smem_u32(&merge_ready[hw]));
+                        }
+                    } else {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait_bounded(smem_u32(&merge_ready[hw]), par, abort_flag, p.wait_ns));
+                        if (ok) {
+#pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                const float mo = mb[h], M = fmaxf(st.m[h], mo);
+                                const float fa = M == -INFINITY ? 0.f : fast_exp2(st.m[h] - M);
+                                const float fb = M == -INFINITY ? 0.f : fast_exp2(mo - M);
+                                st.l[h] = st.l[h] * fa + mb[2 + h] * fb;
+                                st.m[h] = M;
+#pragma unroll
+                                for (int mt = 0; mt < 8; mt++) {
+                                    st.o[mt][h] = st.o[mt][h] * fa + mb[4 + mt * 4 + h] * fb;
+                                    st.o[mt][h + 2] = st.o[mt][h + 2] * fa + mb[4 + mt * 4 + h + 2] * fb;
+                                }
+                            }
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(smem_u32(&merge_taken[hw]));
+                        }
+                    }
+                    n_pieces++;
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        if (lane == 0) {
+                            report(p.status, kStatusTimeout, kSiteDecodeWaitMerge, hw);
+                            *abort_flag = 1;
+                        }
+                        break;
+                    }
+                    if (half == 1) {
+                        cur.advance(pfx, p.n_seqs, p.n_hg);
+                        continue;
+                    }
+                }
                 const int g = lane >> 2, t = lane & 3;
                 float l[2];
                 l[0] = warp_sum_xor(st.l[0], 4);
@@ -696,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_split_kernel(const __grid_
                                     lse2 * 0.69314718055994531f;
                         } else {
                             const int64_t prow = ((int64_t) blockIdx.x * 2 + slot) * kPartRows +
-                                                 (int64_t) warp * kMaxGroup + n;
+                                                 (int64_t) hw * kMaxGroup + n;
                             dst = p.part_o + prow * kD;
                             if (g == 0) p.part_lse[prow] = lse2;
                         }

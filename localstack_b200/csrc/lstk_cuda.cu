@@ -432,7 +432,7 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) grid);
-    cfg.blockDim = dim3(decode::kThreads);
+    cfg.blockDim = dim3(q8 ? decode::SplitCfg<true>::kThreads : decode::SplitCfg<false>::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cfg.attrs = attr;
@@ -567,8 +567,7 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
     p.start_flag = t_start_flag;
     p.q8_dpitch = dpitch;
 
-    const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
-                        16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
+    const size_t smem = q8 ? decode::split_smem_bytes<true>(n_seqs) : decode::split_smem_bytes<false>(n_seqs);
     if (q8) {
         if ((rc = ensure_smem(&dev->decode_q8_smem, decode::decode_split_kernel<true>, smem,
                               "cudaFuncSetAttribute(decode q8_0)")))
@@ -1104,8 +1103,7 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     p.start_flag = t_start_flag;
     p.q8_dpitch = 0;
 
-    const size_t smem = 1024 + (size_t) decode::kStages * decode::kStageBytes + 2 * decode::kStages * sizeof(uint64_t) +
-                        16 + sizeof(int32_t) * ((size_t) n_seqs + 1);
+    const size_t smem = decode::split_smem_bytes<false>(n_seqs);
     if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel<false>, smem, "cudaFuncSetAttribute(decode)")))
         return rc;
     return launch_decode(kmap, vmap, kmap, vmap, false, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
