@@ -405,13 +405,15 @@ __device__ __forceinline__ void process_page_q8(HeadStateQ8 &st, uint32_t kbase,
             dk[0][0] = a0.x, dk[0][1] = a0.y, dk[0][2] = a1.x, dk[0][3] = a1.y;
             dk[1][0] = c0.x, dk[1][1] = c0.y, dk[1][2] = c1.x, dk[1][3] = c1.y;
         }
+        // i: (token tok0 + 8 (i >> 1), head 2t + (i & 1)); fused multiply-adds (the result is held to
+        // the attention tolerance, not to ggml's exact rounding order)
         float s[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {  // i: (token tok0 + 8 (i >> 1), head 2t + (i & 1))
+        for (int i = 0; i < 4; i++) {
             float acc = 0.f;
 #pragma unroll
             for (int blk = 0; blk < 4; blk++)
-                acc = __fadd_rn(acc, __fmul_rn((float) sb[blk][i], __fmul_rn(dk[i >> 1][blk], st.dq[i & 1][blk])));
+                acc = fmaf((float) sb[blk][i], dk[i >> 1][blk] * st.dq[i & 1][blk], acc);
             s[i] = acc;
         }
         const bool v0 = tok0 < valid, v1 = tok0 + 8 < valid;
@@ -436,15 +438,17 @@ __device__ __forceinline__ void process_page_q8(HeadStateQ8 &st, uint32_t kbase,
         const float p3 = fast_exp2(x[3] - mu[1]);
         st.l[0] = st.l[0] * alpha[0] + (p0 + p2);
         st.l[1] = st.l[1] * alpha[1] + (p1 + p3);
+        if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {  // only when a maximum moved
 #pragma unroll
-        for (int mt = 0; mt < 8; mt++) {
-            st.o[mt][0] *= alpha[0];
-            st.o[mt][1] *= alpha[1];
-            st.o[mt][2] *= alpha[0];
-            st.o[mt][3] *= alpha[1];
+            for (int mt = 0; mt < 8; mt++) {
+                st.o[mt][0] *= alpha[0];
+                st.o[mt][1] *= alpha[1];
+                st.o[mt][2] *= alpha[0];
+                st.o[mt][3] *= alpha[1];
+            }
         }
         // V scales of tokens tok0, tok0 + 8; a key that is not visible gets P' = 0 outright (its
-        // stale scale could be non-finite)
+        // stale scale could be non-finite; its P is already 0)
         const uint2 w0 = *reinterpret_cast<const uint2 *>(vd + tok0 * dpitch);
         const uint2 w1 = *reinterpret_cast<const uint2 *>(vd + (tok0 + 8) * dpitch);
         float dv[2][4];
@@ -459,8 +463,8 @@ __device__ __forceinline__ void process_page_q8(HeadStateQ8 &st, uint32_t kbase,
 #pragma unroll
         for (int blk = 0; blk < 4; blk++) {
             const float s0 = v0 ? dv[0][blk] : 0.f, s1 = v1 ? dv[1][blk] : 0.f;
-            const uint32_t pb0 = movmatrix_trans(pack_half2(v0 ? p0 * s0 : 0.f, v0 ? p1 * s0 : 0.f));
-            const uint32_t pb1 = movmatrix_trans(pack_half2(v1 ? p2 * s1 : 0.f, v1 ? p3 * s1 : 0.f));
+            const uint32_t pb0 = movmatrix_trans(pack_half2(p0 * s0, p1 * s0));
+            const uint32_t pb1 = movmatrix_trans(pack_half2(p2 * s1, p3 * s1));
             uint32_t r[4];
             ldsm_x4_trans(vbase + sw128_offset((uint32_t) (slab * 16 + lr + 8 * (li & 1)), (uint32_t) (2 * blk + (li >> 1))),
                           r);
