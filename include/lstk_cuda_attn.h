@@ -309,6 +309,16 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
  *   bf16 Wo projection). */
 int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
                    const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *stream);
+/* lstk_cuda_proj with a caller workspace: when the 128 x 256 output tiles would leave most SMs
+ * idle (small m: the per-GPU shapes of a sharded batch), K is split over the idle SMs into f32
+ * slices of the workspace and summed in slice order (plus the residual, rounded once) by a second
+ * kernel. lstk_cuda_proj_workspace_size gives the bytes that split needs on the current device (0:
+ * no split for this shape; a smaller workspace, or NULL, runs unsplit). Same results up to f32
+ * summation order. */
+size_t lstk_cuda_proj_workspace_size(int32_t m, int32_t n, int32_t k);
+int lstk_cuda_proj_ws(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                      const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *workspace,
+                      size_t workspace_bytes, void *stream);
 int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,
                        int64_t ldy, int32_t rows, int32_t cols, void *stream);
 int lstk_cuda_to_bf16(const float *x, int64_t ldx, void *y, int64_t ldy, int32_t rows, int32_t cols, void *stream);

@@ -118,6 +118,9 @@ def lib():
     L.lstk_cuda_attn_prefill.argtypes = [_LP, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _F, _P,
                                          _P, _SZ, _P]
     L.lstk_cuda_proj.argtypes = [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _I32, _I64, _P]
+    L.lstk_cuda_proj_workspace_size.argtypes = [_I32, _I32, _I32]
+    L.lstk_cuda_proj_workspace_size.restype = _SZ
+    L.lstk_cuda_proj_ws.argtypes = [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _I32, _I64, _P, _SZ, _P]
     L.lstk_cuda_rms_norm.argtypes = [_P, _I32, _I64, _P, _F, _P, _I64, _I32, _I32, _P]
     L.lstk_cuda_to_bf16.argtypes = [_P, _I64, _P, _I64, _I32, _I32, _P]
     L.lstk_cuda_kv_alloc.argtypes = [_P, _P, _P, _I32, _I32, _P, _P, _P, _P]

@@ -58,6 +58,10 @@ static_assert(kSmemBytes <= 232448, "shared memory over the 227 KiB limit");
 struct Params {
     int m, n, k;
     int m_tiles, n_tiles, k_blocks, n_work;
+    // K split (small M): work item = (m-tile, n-tile, slice), slice s covering K blocks
+    // [s * kb_per_split, (s + 1) * kb_per_split); each slice's f32 tile goes to slice s of a
+    // [k_splits][m][n] workspace (omap is then a 3-D map) and split_reduce_kernel sums them.
+    int k_splits, kb_per_split;
     void *out;
     int64_t ldo;
     int out_f32;
@@ -201,8 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             int it = 0;
             bool ok = true;
             for (int w = blockIdx.x; ok && w < p.n_work; w += gridDim.x) {
-                const int m0 = (w % p.m_tiles) * kBM, n0 = (w / p.m_tiles) * kBN;
-                for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+                const int m0 = (w % p.m_tiles) * kBM, n0 = ((w / p.m_tiles) % p.n_tiles) * kBN;
+                const int kb0 = (w / (p.m_tiles * p.n_tiles)) * p.kb_per_split;
+                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     const int s = it % kStages;
                     const uint32_t use = (uint32_t) (it / kStages);
                     if (use > 0 && !(ok = mbar_wait_bounded(smem_u32(&bars->empty[s]), (use - 1) & 1, abort_flag,
@@ -238,14 +244,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t) (buf * kBN);
-                for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+                const int kb0 = (w / (p.m_tiles * p.n_tiles)) * p.kb_per_split;
+                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     const int s = it % kStages;
                     if (!(ok = mbar_wait_bounded(smem_u32(&bars->full[s]), (uint32_t) (it / kStages) & 1, abort_flag,
                                                  p.wait_ns)))
                         break;
                     tc_fence_after();
                     const uint32_t so = (uint32_t) s * (kStageBytes >> 4);
-                    if (kb == 0) mma_f16_ss_k<0>(d, ha | (la + so), hb | (lb + so), kIdesc);
+                    if (kb == kb0) mma_f16_ss_k<0>(d, ha | (la + so), hb | (lb + so), kIdesc);
                     else mma_f16_ss_k<1>(d, ha | (la + so), hb | (lb + so), kIdesc);
 #pragma unroll
                     for (int kk = 1; kk < 4; kk++)  // K steps of 16 elements = 32 bytes inside the swizzle row
@@ -293,7 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const int buf = c & 1;
             const int m0 = (w % p.m_tiles) * kBM;
             const int64_t gm = (int64_t) m0 + r;
-            const int n0 = (w / p.m_tiles) * kBN;
+            const int n0 = ((w / p.m_tiles) % p.n_tiles) * kBN;
+            const int slice = w / (p.m_tiles * p.n_tiles);
             const int nch = min(kBN / 32, (p.n - n0 + 31) / 32);  // column blocks inside the matrix
             if (res_tma && lane == 0 && !*abort_flag) load_res(j, n0, m0);
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars->acc_full[buf]), (uint32_t) (c >> 1) & 1,
@@ -335,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && !*abort_flag) {  // rows / columns past the matrix are clipped by the store
-                    tma_store_2d(&omap, sb, gn, m0 + quad * 32);
+                    if (p.k_splits > 1) tma_store_3d(&omap, sb, gn, m0 + quad * 32, slice);
+                    else tma_store_2d(&omap, sb, gn, m0 + quad * 32);
                     tma_store_commit();
                 }
                 j++;
@@ -357,6 +367,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// Sum of the K split's f32 slices ws [k_splits][m][n] in slice order, plus the optional bf16
+// residual, rounded once to the output type (out [m][ldo]). One CTA row per output row (blockIdx.y),
+// four columns per thread as 16-byte slice loads (n is a multiple of 4 in a split).
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float *ws, int k_splits, int m, int n,
+                                                           const __nv_bfloat16 *res, int64_t ldr, void *out,
+                                                           int out_f32, int64_t ldo) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int row = blockIdx.y;
+    const int64_t slice = (int64_t) m * n;
+    for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < n; c += gridDim.x * blockDim.x * 4) {
+        const int64_t i = (int64_t) row * n + c;
+        float4 v = *reinterpret_cast<const float4 *>(ws + i);
+        for (int s = 1; s < k_splits; s++) {
+            const float4 u = *reinterpret_cast<const float4 *>(ws + s * slice + i);
+            v.x += u.x, v.y += u.y, v.z += u.z, v.w += u.w;
+        }
+        if (res != nullptr) {
+            const uint2 rr = *reinterpret_cast<const uint2 *>(res + (int64_t) row * ldr + c);
+            v.x += bf16_lo(rr.x), v.y += bf16_hi(rr.x), v.z += bf16_lo(rr.y), v.w += bf16_hi(rr.y);
+        }
+        if (out_f32)
+            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + (int64_t) row * ldo + c) = v;
+        else
+            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + (int64_t) row * ldo + c) =
+                make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
+    }
 }
 
 // ---- row kernels around the projections ----------------------------------------------------------

@@ -192,6 +192,22 @@ int encode_scales_2d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t
     return LSTK_OK;
 }
 
+// 3-D map over the projection's K-split workspace [slices][rows][cols] f32 with the store box of
+// encode_out_2d (32 x 32, 128-byte swizzle) in one slice: rows past `rows` are clipped per slice.
+int encode_3d_f32_out(CUtensorMap *map, void *base, uint64_t cols, uint64_t rows, uint64_t slices) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[3] = {cols, rows, slices};
+    const cuuint64_t strides[2] = {cols * 4, cols * rows * 4};
+    const cuuint32_t box[3] = {32, 32, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(LSTK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int) r));
+    return LSTK_OK;
+}
+
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 int check_layout(const lstk_kv_layout *L, const char *fn) {
@@ -886,8 +902,39 @@ static int launch_pdl(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaSt
     return LSTK_OK;
 }
 
-int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
-                   const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *stream) {
+// K slices for a projection, by a cost model in units of one K block of one tile (~0.42 us on
+// B200): rounds of the persistent grid x K blocks per slice, plus the reduce kernel's pass over
+// the f32 slices (measured ~3 TB/s: ~1.26 MB per unit). 1 = no split; at most 8 slices, each at
+// least 8 K blocks deep; n must be a multiple of 4 (the slices' rows are 16-byte multiples).
+static int proj_k_splits(int n_sms, int64_t m, int64_t n, int64_t k) {
+    const int64_t tiles = ((m + gemm::kBM - 1) / gemm::kBM) * ((n + gemm::kBN - 1) / gemm::kBN);
+    const int64_t kb = (k + gemm::kBK - 1) / gemm::kBK;
+    if (n % 4) return 1;
+    int best = 1;
+    double best_cost = (double) ((tiles + n_sms - 1) / n_sms) * (double) kb;
+    for (int s = 2; s <= 8 && kb / s >= 8; s++) {
+        const int64_t per = (kb + s - 1) / s;
+        const double cost = (double) ((tiles * s + n_sms - 1) / n_sms) * (double) per +
+                            (double) s * (double) m * (double) n * 4.0 / 1.26e6;
+        if (cost < best_cost) best = s, best_cost = cost;
+    }
+    return best;
+}
+
+size_t lstk_cuda_proj_workspace_size(int32_t m, int32_t n, int32_t k) {
+    int dev = 0, n_sms = 0;
+    if (m <= 0 || n <= 0 || k <= 0 || cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    const int splits = proj_k_splits(n_sms, m, n, k);
+    return splits > 1 ? (size_t) splits * (size_t) m * (size_t) n * sizeof(float) : 0;
+}
+
+static int proj_impl(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                     const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *workspace,
+                     size_t workspace_bytes, void *stream) {
     if (m < 0 || n < 0 || k <= 0) return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_proj: bad sizes (k must be > 0)");
     if (out_dtype != LSTK_DTYPE_BF16 && out_dtype != LSTK_DTYPE_F32)
         return set_error(LSTK_ERR_UNSUPPORTED, "lstk_cuda_proj: out_dtype must be bf16 or f32");
@@ -922,11 +969,21 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
     p.k_blocks = (k + gemm::kBK - 1) / gemm::kBK;
     const int64_t n_work = (int64_t) p.m_tiles * p.n_tiles;
     if (n_work > INT32_MAX) return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_proj: too many tiles");
-    p.n_work = (int) n_work;
-    p.out = out;
-    p.ldo = ldo;
-    p.out_f32 = out_dtype == LSTK_DTYPE_F32;
-    p.res = static_cast<const __nv_bfloat16 *>(residual);
+    // K split into f32 slices of the workspace when the tiles alone would leave most SMs idle
+    const int splits = workspace ? proj_k_splits(dev->n_sms, m, n, k) : 1;
+    const bool split = splits > 1 && workspace_bytes >= (size_t) splits * m * n * sizeof(float) &&
+                       aligned(workspace, 16);
+    p.k_splits = split ? splits : 1;
+    p.kb_per_split = split ? (p.k_blocks + splits - 1) / splits : p.k_blocks;
+    if (split) {
+        p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty slice
+        if ((rc = encode_3d_f32_out(&omap, workspace, (uint64_t) n, (uint64_t) m, (uint64_t) p.k_splits))) return rc;
+    }
+    p.n_work = (int) n_work * p.k_splits;
+    p.out = split ? workspace : out;
+    p.ldo = split ? n : ldo;
+    p.out_f32 = split ? 1 : out_dtype == LSTK_DTYPE_F32;
+    p.res = split ? nullptr : static_cast<const __nv_bfloat16 *>(residual);
     p.ldr = ldr;
     p.status = dev->status;
     p.wait_ns = t_pipeline_wait_ns;
@@ -934,11 +991,32 @@ int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32
         return rc;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned) std::min<int64_t>(n_work, dev->n_sms));
+    cfg.gridDim = dim3((unsigned) std::min<int64_t>(p.n_work, dev->n_sms));
     cfg.blockDim = dim3(gemm::kThreads);
     cfg.dynamicSmemBytes = gemm::kSmemBytes;
     launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
-    return launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, omap, rmap, p), "gemm_kernel");
+    rc = launch_pdl_check(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, amap, bmap, omap, rmap, p), "gemm_kernel");
+    if (rc || !split) return rc;
+    cudaLaunchConfig_t rcfg = {};
+    rcfg.gridDim = dim3((unsigned) ((n / 4 + 255) / 256), (unsigned) m);
+    rcfg.blockDim = dim3(256);
+    launch_pdl(rcfg, attr, static_cast<cudaStream_t>(stream));
+    return launch_pdl_check(cudaLaunchKernelEx(&rcfg, gemm::split_reduce_kernel, static_cast<const float *>(workspace),
+                                               p.k_splits, (int) m, (int) n,
+                                               static_cast<const __nv_bfloat16 *>(residual), ldr, out,
+                                               (int) (out_dtype == LSTK_DTYPE_F32), ldo),
+                            "split_reduce_kernel");
+}
+
+int lstk_cuda_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                   const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *stream) {
+    return proj_impl(x, ldx, w, ldw, m, n, k, residual, ldr, out, out_dtype, ldo, nullptr, 0, stream);
+}
+
+int lstk_cuda_proj_ws(const void *x, int64_t ldx, const void *w, int64_t ldw, int32_t m, int32_t n, int32_t k,
+                      const void *residual, int64_t ldr, void *out, int32_t out_dtype, int64_t ldo, void *workspace,
+                      size_t workspace_bytes, void *stream) {
+    return proj_impl(x, ldx, w, ldw, m, n, k, residual, ldr, out, out_dtype, ldo, workspace, workspace_bytes, stream);
 }
 
 int lstk_cuda_rms_norm(const void *x, int32_t x_dtype, int64_t ldx, const float *gamma, float eps, void *y,

@@ -19,9 +19,25 @@ def _rows(t, name):
     return t.shape[0], t.shape[1], t.stride(0)
 
 
-def proj(x, w, residual=None, out=None, out_dtype=torch.bfloat16, stream=None):
+_workspaces = {}  # device -> uint8 tensor for the K split of small-m projections (grown on demand)
+
+
+def _split_workspace(m, n, k, device):
+    need = lib().lstk_cuda_proj_workspace_size(m, n, k)
+    if need == 0:
+        return None
+    ws = _workspaces.get(device)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _workspaces[device] = ws
+    return ws
+
+
+def proj(x, w, residual=None, out=None, out_dtype=torch.bfloat16, stream=None, split_k=True):
     """out = x @ w.T (+ residual) on the tensor cores. x [m][k] bf16, w [n][k] bf16, residual
-    [m][n] bf16 (may be `out` itself); out [m][n] bf16 or f32."""
+    [m][n] bf16 (may be `out` itself); out [m][n] bf16 or f32. With split_k, small-m shapes split K
+    over the idle SMs through a workspace kept per device (allocated on first use of a shape: make
+    that call before any stream capture)."""
     m, k, ldx = _rows(x, "x")
     n, kw, ldw = _rows(w, "w")
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or kw != k:
@@ -37,8 +53,13 @@ def proj(x, w, residual=None, out=None, out_dtype=torch.bfloat16, stream=None):
     mo, no, ldo = _rows(out, "out")
     if (mo, no) != (m, n) or out.dtype not in (torch.bfloat16, torch.float32):
         raise ValueError("out must be [m][n] bf16 or f32")
-    check(lib().lstk_cuda_proj(_p(x), ldx, _p(w), ldw, m, n, k, _p(residual), ldr, _p(out), _DT[out.dtype], ldo,
-                               _stream(stream, x.device)))
+    ws = _split_workspace(m, n, k, x.device) if split_k else None
+    if ws is not None:
+        check(lib().lstk_cuda_proj_ws(_p(x), ldx, _p(w), ldw, m, n, k, _p(residual), ldr, _p(out), _DT[out.dtype], ldo,
+                                      _p(ws), ws.numel(), _stream(stream, x.device)))
+    else:
+        check(lib().lstk_cuda_proj(_p(x), ldx, _p(w), ldw, m, n, k, _p(residual), ldr, _p(out), _DT[out.dtype], ldo,
+                                   _stream(stream, x.device)))
     return out
 
 

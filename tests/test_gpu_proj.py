@@ -113,3 +113,19 @@ def test_to_bf16_is_round_to_nearest_even():
     # a strided source (rows of a wider buffer)
     xb = torch.randn((50, 200), generator=g, device=DEV)
     assert torch.equal(L.to_bf16(xb[:, 8:136]), xb[:, 8:136].bfloat16())
+
+
+@pytest.mark.parametrize("m,n,k,res,split", [(544, 2048, 4096, True, True), (1088, 5120, 2048, False, False),
+                                             (544, 5120, 2048, False, False), (77, 264, 2048, True, True),
+                                             (300, 1024, 8192, False, True)])
+def test_small_m_split_k(m, n, k, res, split):
+    # per-GPU shapes of a sharded config 5 (few tiles): K split over the idle SMs into f32 slices of
+    # a workspace, summed with the residual by the reduce kernel; the residual written in place
+    need = L.lib().lstk_cuda_proj_workspace_size(m, n, k)
+    x, w, g = _operands(m, n, k, m + k)
+    r = torch.randn((m, n), generator=g, device=DEV).bfloat16() if res else None
+    ref, mag = _ref(x, w, r)
+    out = L.proj(x, w, residual=r, out=r, out_dtype=torch.bfloat16) if res else L.proj(x, w, out_dtype=torch.float32)
+    L.check_status()
+    _check(out, ref, mag + (r.double().abs() if res else 0), res)
+    assert (need > 0) == split  # on 148 SMs: split when the tiles fill at most half of them
