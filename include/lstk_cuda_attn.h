@@ -230,6 +230,11 @@ int lstk_cuda_attn_decode_q8(const lstk_kv_layout *layout, const int8_t *k_qs, c
                              const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
                              int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
                              size_t workspace_bytes, int32_t n_ctas, void *stream);
+/* Byte moves between ggml's block_q8_0 rows (n_rows rows of 128 values = 4 blocks of 34 bytes:
+ * f16 d, then 32 int8) and the planes (qs [n_rows][128], d [n_rows][4]); n_rows = n_cells *
+ * n_head_kv for a whole cache. For a cache kept as a ggml q8_0 tensor. Pointers 2-byte aligned. */
+int lstk_cuda_q8_from_ggml_blocks(const void *blocks, int64_t n_rows, int8_t *qs, void *d, void *stream);
+int lstk_cuda_q8_to_ggml_blocks(const int8_t *qs, const void *d, int64_t n_rows, void *blocks, void *stream);
 
 /* ---- One context over several processes / GPUs: peer-memory exchange and merge -------------
  * (no counterpart in the reference, which runs in one process). Rank r of R decodes its

@@ -8,6 +8,7 @@
 #include "host_util.h"
 #include "kv_append.cuh"
 #include "kv_pages.cuh"
+#include "q8_layout.cuh"
 #include "prefill.cuh"
 
 #include "lstk_cuda_attn.h"
@@ -651,6 +652,43 @@ int lstk_cuda_attn_decode_q8(const lstk_kv_layout *layout, const int8_t *k_qs, c
     return decode_range(layout, k_qs, v_qs, q, q_dtype, n_seqs, n_head, block_tables, max_blocks_per_seq, seq_lens,
                         max_seq_len, 0, INT32_MAX, scale, out, lse_out, workspace, workspace_bytes, n_ctas, stream,
                         nullptr, &q8);
+}
+
+static int launch_pdl(cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr, cudaStream_t s);
+
+// Copies between ggml's block_q8_0 rows and the q8_0 planes (q8_layout.cuh).
+static int q8_convert(const void *src_a, const void *src_b, int64_t n_rows, void *dst_a, void *dst_b, bool to_blocks,
+                      void *stream) {
+    if (n_rows < 0 || !src_a || !dst_a || (!to_blocks && !dst_b) || (to_blocks && !src_b))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_q8 conversion: bad arguments");
+    if (!aligned(src_a, 2) || !aligned(dst_a, 2) || (src_b && !aligned(src_b, 2)) || (dst_b && !aligned(dst_b, 2)))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_q8 conversion: pointers must be 2-byte aligned");
+    if (n_rows == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    int rc = bind_device(dst_a, &dev);
+    if (rc) return rc;
+    const int64_t n_blocks = n_rows * 4;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) std::min<int64_t>((n_blocks * q8::kBlockWords + 255) / 256, (int64_t) dev->n_sms * 16));
+    cfg.blockDim = dim3(256);
+    launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
+    if (to_blocks)
+        return launch_pdl_check(cudaLaunchKernelEx(&cfg, q8::to_blocks_kernel, static_cast<const uint16_t *>(src_a),
+                                                   static_cast<const uint16_t *>(src_b), n_blocks,
+                                                   static_cast<uint16_t *>(dst_a)),
+                                "q8 to_blocks_kernel");
+    return launch_pdl_check(cudaLaunchKernelEx(&cfg, q8::from_blocks_kernel, static_cast<const uint16_t *>(src_a), n_blocks,
+                                               static_cast<uint16_t *>(dst_a), static_cast<uint16_t *>(dst_b)),
+                            "q8 from_blocks_kernel");
+}
+
+int lstk_cuda_q8_from_ggml_blocks(const void *blocks, int64_t n_rows, int8_t *qs, void *d, void *stream) {
+    return q8_convert(blocks, nullptr, n_rows, qs, d, false, stream);
+}
+
+int lstk_cuda_q8_to_ggml_blocks(const int8_t *qs, const void *d, int64_t n_rows, void *blocks, void *stream) {
+    return q8_convert(qs, d, n_rows, blocks, nullptr, true, stream);
 }
 
 int lstk_cuda_attn_merge(const float *o_parts, const float *lse_parts, int32_t n_parts, int64_t n_rows,

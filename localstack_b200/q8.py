@@ -32,6 +32,25 @@ class Q8Cache:
     def device(self):
         return self.qs.device
 
+    def to_ggml_blocks(self, stream=None):
+        """The cache as ggml's block_q8_0 rows: uint8 [n_cells][n_head_kv][4 * 34]."""
+        n_cells, hkv, _ = self.qs.shape
+        out = torch.empty((n_cells, hkv, 4 * 34), dtype=torch.uint8, device=self.device)
+        check(lib().lstk_cuda_q8_to_ggml_blocks(_p(self.qs), _p(self.d), n_cells * hkv, _p(out),
+                                                _stream(stream, self.device)))
+        return out
+
+    @staticmethod
+    def from_ggml_blocks(blocks, stream=None):
+        """A cache from ggml's block_q8_0 rows (uint8 [n_cells][n_head_kv][4 * 34])."""
+        n_cells, hkv, nb = blocks.shape
+        if blocks.dtype != torch.uint8 or nb != 4 * 34 or not blocks.is_contiguous():
+            raise ValueError("blocks must be a contiguous uint8 [n_cells][n_head_kv][136] tensor")
+        c = Q8Cache(n_cells, hkv, blocks.device)
+        check(lib().lstk_cuda_q8_from_ggml_blocks(_p(blocks), n_cells * hkv, _p(c.qs), _p(c.d),
+                                                  _stream(stream, blocks.device)))
+        return c
+
     def dequantize(self):
         """f32 values d * q [n_cells][n_head_kv][128]."""
         return self.qs.float() * self.d.float().repeat_interleave(32, dim=-1)

@@ -134,3 +134,34 @@ def test_append_then_decode_q8_chain():
     L.check_status()
     ref = O.paged_attn_q8(q_ref, np.arange(len(lens)), pos, kqs, kd, vqs, vd, bt2, lens, SCALE, mode=O.MODE_GGML)
     assert within(out.cpu().numpy(), ref), max_err(out.cpu().numpy(), ref)
+
+
+def test_ggml_block_layout_round_trip():
+    """The planes hold exactly ggml's block_q8_0 bytes: packing a cache into 34-byte blocks (f16 d,
+    then 32 int8) matches a numpy packing of the same planes, and unpacking restores them."""
+    rng = np.random.default_rng(9)
+    n_cells, hkv = 96, 4
+    x = rng.standard_normal((n_cells, hkv, 128)).astype(np.float32)
+    qs, d = O.quantize_q8_0(x)
+    c = L.Q8Cache(n_cells, hkv, DEV)
+    c.qs.copy_(torch.from_numpy(qs))
+    c.d.copy_(torch.from_numpy(d.view(np.int16)).view(torch.float16))
+    blocks = c.to_ggml_blocks()
+    L.check_status()
+    ref = np.empty((n_cells, hkv, 4, 34), np.uint8)
+    ref[..., :2] = d.reshape(n_cells, hkv, 4, 1).view(np.uint8).reshape(n_cells, hkv, 4, 2)
+    ref[..., 2:] = qs.reshape(n_cells, hkv, 4, 32).view(np.uint8)
+    assert np.array_equal(blocks.cpu().numpy(), ref.reshape(n_cells, hkv, 136))
+    back = L.Q8Cache.from_ggml_blocks(blocks)
+    L.check_status()
+    assert torch.equal(back.qs, c.qs) and torch.equal(back.d.view(torch.int16), c.d.view(torch.int16))
+
+
+def test_decode_q8_config4_131072_keys():
+    """Config 4 over a q8_0 cache: one 131072-key context (4096 pages at random places)."""
+    rng = np.random.default_rng(131)
+    args, (q, kqs, kd, vqs, vd, bt) = _decode_case(rng, [131072], 32, 4)
+    out = L.attn_decode_q8(*args, SCALE, max_seq_len=131072)
+    L.check_status()
+    gg = O.paged_attn_q8(q, [0], [131071], kqs, kd, vqs, vd, bt, [131072], SCALE, mode=O.MODE_GGML)
+    assert within(out.cpu().numpy(), gg), max_err(out.cpu().numpy(), gg)
