@@ -230,6 +230,18 @@ int lstk_cuda_attn_decode_q8(const lstk_kv_layout *layout, const int8_t *k_qs, c
                              const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *seq_lens,
                              int32_t max_seq_len, float scale, float *out, float *lse_out, void *workspace,
                              size_t workspace_bytes, int32_t n_ctas, void *stream);
+/* Prefill over a q8_0 cache: the pages the call reads (kv_lens[b] keys of each sequence through
+ * its block table) are dequantised (d * q rounded once to f16) into a compact f16 cache in
+ * `scratch` with dense block tables, and lstk_cuda_attn_prefill runs on it (same arguments and
+ * results; its `workspace` as for the f16 call). The scratch holds n_seqs * max_blocks_per_seq
+ * pages of K and V: lstk_cuda_q8_prefill_scratch_size bytes, 256-byte aligned. */
+size_t lstk_cuda_q8_prefill_scratch_size(int32_t n_seqs, int32_t max_blocks_per_seq, int32_t n_head_kv);
+int lstk_cuda_attn_prefill_q8(const lstk_kv_layout *layout, const int8_t *k_qs, const void *k_d, const int8_t *v_qs,
+                              const void *v_d, const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                              const int32_t *q_seq_start, int32_t max_q_len, int64_t total_tokens,
+                              const int32_t *q_pos0, const int32_t *kv_lens, const int32_t *block_tables,
+                              int32_t max_blocks_per_seq, float scale, float *out, void *workspace,
+                              size_t workspace_bytes, void *scratch, size_t scratch_bytes, void *stream);
 /* Byte moves between ggml's block_q8_0 rows (n_rows rows of 128 values = 4 blocks of 34 bytes:
  * f16 d, then 32 int8) and the planes (qs [n_rows][128], d [n_rows][4]); n_rows = n_cells *
  * n_head_kv for a whole cache. For a cache kept as a ggml q8_0 tensor. Pointers 2-byte aligned. */

@@ -18,4 +18,4 @@ from .attn import (  # noqa: F401
 )
 from .pages import DevicePages  # noqa: F401,E402
 from .proj import proj, rms_norm, to_bf16  # noqa: F401,E402
-from .q8 import Q8Cache, alloc_cache_q8, attn_decode_q8, kv_append_q8  # noqa: F401,E402
+from .q8 import Q8Cache, alloc_cache_q8, attn_decode_q8, attn_prefill_q8, kv_append_q8  # noqa: F401,E402

@@ -102,6 +102,10 @@ def lib():
     L.lstk_cuda_attn_merge.argtypes = [_P, _P, _I32, _I64, _I32, _I64, _I64, _P, _P, _P]
     L.lstk_cuda_kv_append_q8.argtypes = [_LP, _P, _P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I64, _I32, _I32, _P, _P,
                                          _P, _P, _F, _P, _I32, _P, _I32, _P]
+    L.lstk_cuda_q8_prefill_scratch_size.argtypes = [_I32, _I32, _I32]
+    L.lstk_cuda_q8_prefill_scratch_size.restype = _SZ
+    L.lstk_cuda_attn_prefill_q8.argtypes = [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P,
+                                            _I32, _F, _P, _P, _SZ, _P, _SZ, _P]
     L.lstk_cuda_q8_from_ggml_blocks.argtypes = [_P, _I64, _P, _P, _P]
     L.lstk_cuda_q8_to_ggml_blocks.argtypes = [_P, _P, _I64, _P, _P]
     L.lstk_cuda_attn_decode_q8.argtypes = [_LP, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _P, _I32, _F, _P, _P,

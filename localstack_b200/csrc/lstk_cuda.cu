@@ -811,6 +811,62 @@ int lstk_cuda_attn_prefill(const lstk_kv_layout *layout, const void *k_cache, co
                             "prefill_kernel");
 }
 
+// Scratch of lstk_cuda_attn_prefill_q8: the compact f16 K and V caches (n_seqs * max_blocks pages)
+// and their dense block tables, each 256-byte aligned.
+static size_t q8_scratch_cache_bytes(int32_t n_seqs, int32_t max_blocks, int32_t n_head_kv) {
+    return align_up((size_t) n_seqs * max_blocks * 32 * n_head_kv * 128 * sizeof(__half), 256);
+}
+
+size_t lstk_cuda_q8_prefill_scratch_size(int32_t n_seqs, int32_t max_blocks_per_seq, int32_t n_head_kv) {
+    if (n_seqs <= 0 || max_blocks_per_seq <= 0 || n_head_kv <= 0) return 0;
+    return 2 * q8_scratch_cache_bytes(n_seqs, max_blocks_per_seq, n_head_kv) +
+           align_up(sizeof(int32_t) * (size_t) n_seqs * max_blocks_per_seq, 256);
+}
+
+int lstk_cuda_attn_prefill_q8(const lstk_kv_layout *layout, const int8_t *k_qs, const void *k_d, const int8_t *v_qs,
+                              const void *v_d, const void *q, int32_t q_dtype, int32_t n_seqs, int32_t n_head,
+                              const int32_t *q_seq_start, int32_t max_q_len, int64_t total_tokens,
+                              const int32_t *q_pos0, const int32_t *kv_lens, const int32_t *block_tables,
+                              int32_t max_blocks_per_seq, float scale, float *out, void *workspace,
+                              size_t workspace_bytes, void *scratch, size_t scratch_bytes, void *stream) {
+    int rc = check_layout(layout, "lstk_cuda_attn_prefill_q8");
+    if (rc) return rc;
+    if (!k_qs || !k_d || !v_qs || !v_d || !kv_lens || !block_tables || !scratch || n_seqs < 0 || max_blocks_per_seq <= 0)
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill_q8: bad arguments");
+    if (max_blocks_per_seq > 65535 || n_seqs > 65535)
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill_q8: more than 65535 sequences or pages per sequence");
+    if (!aligned(k_qs, 16) || !aligned(v_qs, 16) || !aligned(k_d, 2) || !aligned(v_d, 2) || !aligned(scratch, 256))
+        return set_error(LSTK_ERR_INVALID_ARG, "lstk_cuda_attn_prefill_q8: misaligned plane or scratch");
+    const int hkv = layout->n_head_kv;
+    if (scratch_bytes < lstk_cuda_q8_prefill_scratch_size(n_seqs, max_blocks_per_seq, hkv))
+        return set_error(LSTK_ERR_CAPACITY, "lstk_cuda_attn_prefill_q8: scratch too small");
+    if (n_seqs == 0) return clear_error();
+    DeviceInfo *dev = nullptr;
+    if ((rc = bind_device(k_qs, &dev))) return rc;
+    uint8_t *sc = static_cast<uint8_t *>(scratch);
+    const size_t cache_bytes = q8_scratch_cache_bytes(n_seqs, max_blocks_per_seq, hkv);
+    __half *k16 = reinterpret_cast<__half *>(sc);
+    __half *v16 = reinterpret_cast<__half *>(sc + cache_bytes);
+    int32_t *bt16 = reinterpret_cast<int32_t *>(sc + 2 * cache_bytes);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) max_blocks_per_seq, (unsigned) n_seqs);
+    cfg.blockDim = dim3(256);
+    launch_pdl(cfg, attr, static_cast<cudaStream_t>(stream));
+    if ((rc = launch_pdl_check(cudaLaunchKernelEx(&cfg, q8::gather_dequant_kernel, k_qs,
+                                                  static_cast<const __half *>(k_d), v_qs,
+                                                  static_cast<const __half *>(v_d), hkv,
+                                                  (int64_t) (layout->n_cells / layout->block_size), block_tables,
+                                                  (int) max_blocks_per_seq, kv_lens, k16, v16, bt16, dev->status),
+                               "q8 gather_dequant_kernel")))
+        return rc;
+    lstk_kv_layout l16 = *layout;
+    l16.n_cells = (int64_t) n_seqs * max_blocks_per_seq * 32;
+    return lstk_cuda_attn_prefill(&l16, k16, v16, q, q_dtype, n_seqs, n_head, q_seq_start, max_q_len, total_tokens,
+                                  q_pos0, kv_lens, bt16, max_blocks_per_seq, scale, out, workspace, workspace_bytes,
+                                  stream);
+}
+
 static int pages_state(const lstk_kv_pages *st, pages::State *out) {
     if (!st || !st->free_blocks || !st->free_top || !st->block_tables || !st->seq_lens || !st->used_hwm ||
         st->n_slots <= 0 || st->max_blocks <= 0)

@@ -103,3 +103,37 @@ def attn_decode_q8(kq: Q8Cache, vq: Q8Cache, q, block_tables, seq_lens, scale=No
                                          int(max_seq_len), float(scale), _p(out), _p(lse_out), _p(workspace.buf),
                                          workspace.buf.numel(), int(n_ctas), _stream(stream, kq.device)))
     return (out, lse_out) if want_lse else out
+
+
+def attn_prefill_q8(kq: Q8Cache, vq: Q8Cache, q, q_seq_start, q_pos0, kv_lens, block_tables, max_q_len, scale=None,
+                    out=None, workspace=None, scratch=None, stream=None):
+    """Causal prefill over q8_0 planes: the pages the call reads are dequantised into a compact f16
+    scratch cache (`scratch`: uint8 of lstk_cuda_q8_prefill_scratch_size bytes, allocated when
+    None) and the tensor-core prefill runs on it. Arguments and result as attn_prefill."""
+    L = kq.layout
+    total, Hq, _ = q.shape
+    B = q_pos0.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(HEAD_DIM)
+    if q.dtype not in (torch.float16, torch.float32) or not q.is_contiguous():
+        raise ValueError("q must be a contiguous f16 or f32 tensor [total_tokens][Hq][128]")
+    for name, t in (("q_seq_start", q_seq_start), ("q_pos0", q_pos0), ("kv_lens", kv_lens),
+                    ("block_tables", block_tables)):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    max_blocks = block_tables.shape[1]
+    if out is None:
+        out = torch.empty((total, Hq, HEAD_DIM), dtype=torch.float32, device=q.device)
+    ws_need = lib().lstk_cuda_attn_prefill_workspace_size(B, Hq, L.n_head_kv, HEAD_DIM, int(max_q_len), max_blocks,
+                                                          total, _DT[q.dtype])
+    if ws_need and (workspace is None or workspace.numel() < ws_need):
+        workspace = torch.empty(ws_need, dtype=torch.uint8, device=q.device)
+    sc_need = lib().lstk_cuda_q8_prefill_scratch_size(B, max_blocks, L.n_head_kv)
+    if scratch is None or scratch.numel() < sc_need:
+        scratch = torch.empty(sc_need, dtype=torch.uint8, device=q.device)
+    check(lib().lstk_cuda_attn_prefill_q8(ctypes.byref(L), _p(kq.qs), _p(kq.d), _p(vq.qs), _p(vq.d), _p(q),
+                                          _DT[q.dtype], B, Hq, _p(q_seq_start), int(max_q_len), total, _p(q_pos0),
+                                          _p(kv_lens), _p(block_tables), max_blocks, float(scale), _p(out),
+                                          _p(workspace), workspace.numel() if workspace is not None else 0,
+                                          _p(scratch), scratch.numel(), _stream(stream, kq.device)))
+    return out

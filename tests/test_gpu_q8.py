@@ -165,3 +165,37 @@ def test_decode_q8_config4_131072_keys():
     L.check_status()
     gg = O.paged_attn_q8(q, [0], [131071], kqs, kd, vqs, vd, bt, [131072], SCALE, mode=O.MODE_GGML)
     assert within(out.cpu().numpy(), gg), max_err(out.cpu().numpy(), gg)
+
+
+@pytest.mark.parametrize("q_lens,ctx_before,Hq,Hkv", [([2048], [0], 16, 8), ([512, 512, 200, 512], [0, 512, 1000, 33], 32, 4),
+                                                      ([1, 77, 300], [0, 5, 0], 16, 2)])
+def test_prefill_q8_vs_oracle(q_lens, ctx_before, Hq, Hkv):
+    """Prefill over q8_0 planes (pages dequantised into an f16 scratch, then the tensor-core
+    prefill) against the oracle's exact mode over the same q8_0 cache (f32 query, the dequantised
+    K / V, double): the north-star tolerance."""
+    rng = np.random.default_rng(sum(q_lens) + Hq)
+    kv_lens = [c + t for c, t in zip(ctx_before, q_lens)]
+    bt, n_pages = scattered_block_tables(rng, kv_lens)
+    n_cells = n_pages * 32
+    k = rng.standard_normal((n_cells, Hkv, 128)).astype(np.float32)
+    k = k / np.sqrt(np.mean(k * k, axis=-1, keepdims=True) + 1e-6)
+    v = rng.standard_normal((n_cells, Hkv, 128)).astype(np.float32)
+    kqs, kd = O.quantize_q8_0(k)
+    vqs, vd = O.quantize_q8_0(v)
+    kq, vq = L.Q8Cache(n_cells, Hkv, DEV), L.Q8Cache(n_cells, Hkv, DEV)
+    for cache, qs, d in ((kq, kqs, kd), (vq, vqs, vd)):
+        cache.qs.copy_(torch.from_numpy(qs))
+        cache.d.copy_(torch.from_numpy(d.view(np.int16)).view(torch.float16))
+    total = int(sum(q_lens))
+    q = random_q(rng, total, Hq).astype(np.float16)
+    starts = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    t32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    out = L.attn_prefill_q8(kq, vq, torch.from_numpy(q).to(DEV), torch.from_numpy(starts).to(DEV), t32(ctx_before),
+                            t32(kv_lens), torch.from_numpy(bt).to(DEV), max(q_lens), SCALE)
+    L.check_status()
+    q_seq = np.concatenate([np.full(n, b, np.int32) for b, n in enumerate(q_lens)])
+    q_pos = np.concatenate([np.arange(c, c + n, dtype=np.int32) for c, n in zip(ctx_before, q_lens)])
+    ex = O.paged_attn_q8(q.astype(np.float32), q_seq, q_pos, kqs, kd, vqs, vd, bt, kv_lens, SCALE, causal=True,
+                         mode=O.MODE_EXACT)
+    o = out.cpu().numpy()
+    assert within(o, ex), max_err(o, ex)
