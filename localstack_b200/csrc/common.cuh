@@ -206,6 +206,11 @@ __device__ __forceinline__ void tma_store_wait_read() {
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Pulls the 128-byte line holding p into L2. Only a hint: L2 is where every SM's (and the
+// previous kernel's) writes land, so a line prefetched early never makes a later load stale.
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
 
 // Programmatic dependent launch. A grid launched with programmatic stream serialization may be
 // scheduled before its predecessor in the stream has finished; pdl_wait() blocks until every

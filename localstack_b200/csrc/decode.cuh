@@ -508,6 +508,51 @@ __global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, 1) decode_split_kerne
     int32_t *pfx = reinterpret_cast<int32_t *>(full + SplitCfg<kQ8>::kBarriers) + 4;
 
     __shared__ int32_t stage_pid[kNStages];  // page id of each stage's page-group (producer -> consumers)
+    // Before waiting for the previous kernel (whose work it may overlap): barrier set-up, the
+    // tensor-map prefetch, and L2 prefetches of what the prologue and the producer read first -
+    // seq_lens, and for a single sequence the block-table entries of this CTA's range as it would
+    // be if the sequence filled the call's range (a guess; wrong guesses only cost the prefetch).
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < kNStages; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kConsumers);
+        }
+        if constexpr (kQ8)
+            for (int h = 0; h < kHeadsPerGroup; h++) {
+                mbar_init(smem_u32(&merge_ready[h]), 1);
+                mbar_init(smem_u32(&merge_taken[h]), 1);
+            }
+        fence_barrier_init();
+    } else if (threadIdx.x == kConsumers * 32) {
+        prefetch_tensormap(&kmap);
+        prefetch_tensormap(&vmap);
+        if constexpr (kQ8) {
+            prefetch_tensormap(&kdmap);
+            prefetch_tensormap(&vdmap);
+        }
+    }
+    // (Warps 1-3 issue the prefetches, so thread 0's barrier set-up stays short; float arithmetic
+    // is plenty for a guess.)
+    if (warp >= 1 && warp < kConsumers) {
+        const int t = threadIdx.x - 32;
+        if (t * 32 < p.n_seqs) prefetch_l2(p.seq_lens + t * 32);
+        if (p.n_seqs == 1) {
+            const int64_t span =
+                min((int64_t) p.max_blocks, ((int64_t) p.kv_end + kPage - 1) / kPage) - (int64_t) p.kv_page0;
+            if (span > 0) {
+                const float per = (float) span * (float) p.n_hg / (float) gridDim.x;  // page-groups per CTA
+                const int64_t x0 = (int64_t) (per * (float) blockIdx.x);
+                const int64_t x1 = min((int64_t) (per * (float) (blockIdx.x + 1)) + 1, span * p.n_hg);
+                for (int64_t x = x0 + 32 * t; x < x1 + 31; x += 32 * (kConsumers - 1) * 32) {
+                    int64_t xe = x < x1 ? x : x1 - 1;  // the range's last entry closes the loop
+                    if (xe < x0) continue;
+                    while (xe >= span) xe -= span;  // the entry of head group xe / span's page
+                    prefetch_l2(p.block_tables + p.kv_page0 + xe);
+                }
+            }
+        }
+    }
     // Inputs (q, seq_lens, tables, pages) may come from the previous kernel in the stream; the
     // combine grid may be scheduled right away (it waits for this grid to complete).
     pdl_wait();
@@ -540,19 +585,6 @@ __global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, 1) decode_split_kerne
             acc += (range_len(p, p.seq_lens[b]) + kPage - 1) / kPage;
         }
         if (threadIdx.x == kNThreads - 1) pfx[p.n_seqs] = acc;
-        if (threadIdx.x == 0) {
-            *abort_flag = 0;
-            for (int s = 0; s < kNStages; s++) {
-                mbar_init(smem_u32(&full[s]), 1);
-                mbar_init(smem_u32(&empty[s]), kConsumers);
-            }
-            if constexpr (kQ8)
-                for (int h = 0; h < kHeadsPerGroup; h++) {
-                    mbar_init(smem_u32(&merge_ready[h]), 1);
-                    mbar_init(smem_u32(&merge_taken[h]), 1);
-                }
-            fence_barrier_init();
-        }
         __syncthreads();
         if (blockIdx.x == 0)
             for (int b = threadIdx.x; b <= p.n_seqs; b += kNThreads) p.prefix[b] = pfx[b];
@@ -572,12 +604,6 @@ __global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, 1) decode_split_kerne
         uint64_t policy = 0;
         bool ok = true;
         if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-            if constexpr (kQ8) {
-                prefetch_tensormap(&kdmap);
-                prefetch_tensormap(&vdmap);
-            }
             policy = l2_policy_evict_first();
             if (p.start_flag != nullptr && !flag_wait_bounded(p.start_flag, abort_flag, p.wait_ns)) {
                 report(p.status, kStatusTimeout, kSiteDecodeWaitStart, blockIdx.x);
@@ -816,6 +842,7 @@ constexpr int kCombineWarps = kCombineThreads / 32;
 
 struct CombineParams {
     int n_seqs, n_head, n_head_kv, group, n_hg, grid;
+    int dsplit;  // CTAs per output row (1, 2 or 4), each owning 128 / dsplit consecutive dims
     const int32_t *prefix;
     const float *part_o;
     const float *part_lse;
@@ -830,50 +857,65 @@ struct CombineParams {
     DeviceStatus *status;
 };
 
-// The end of a combine CTA's row: without an exchange, out / lse_out get the local row. With
-// one, the row's local (O, lse) goes to every rank (exchange.cuh's mailboxes) and out / lse_out
-// get the log-sum-exp merge of the R ranks' rows. The row travels as 129 words of 8 bytes - a
-// value's f32 bits and the call's epoch - stored straight into slot `rank` of every rank's
-// mailbox (plain peer stores); a reader polls the words of its own mailbox until each carries
+// CTAs per output row of the combine: enough that a row split over many pieces (one long
+// sequence over the whole grid: up to 148 pieces of 512 bytes) is read by several SMs, while a
+// batch of short rows keeps one CTA per row. Fused exchange: every combine CTA owns an epoch
+// counter in the mailbox header, so the grid must fit it.
+__host__ __device__ inline int combine_dsplit(int n_seqs, int n_hg, int grid, bool exchange, int max_ctas) {
+    const int64_t segs = (int64_t) n_seqs * n_hg;
+    const int64_t per = segs > 0 ? grid / segs : 0;  // pieces per segment, about
+    int d = per >= 32 ? 4 : per >= 8 ? 2 : 1;
+    while (exchange && d > 1 && segs * kPartRows * d > max_ctas) d >>= 1;
+    return d;
+}
+
+// The end of a combine CTA's share of a row: dims [d0, d0 + nd), thread t < nd holding dim
+// d0 + t in o, and the row's lse (natural log; every CTA of the row has the same). Without an
+// exchange, out (and, from the row's first CTA, lse_out) get the local values. With one, the
+// share goes to every rank (exchange.cuh's mailboxes) and out / lse_out get the log-sum-exp merge
+// of the R ranks' rows. A row travels as 129 words of 8 bytes - a value's f32 bits and the call's
+// epoch - stored straight into slot `rank` of every rank's mailbox (plain peer stores; the lse
+// word by the row's first CTA); a reader polls the words of its own mailbox until each carries
 // the epoch, and an 8-byte word is written and read whole, so no flag and no system-scope fence
-// is needed. Waits are bounded by wait_ns (on timeout the status records it and the row is
-// zeros). The CTA's epoch counter is the mailbox header entry of its linear index, so calls
-// replay from a CUDA graph; words alternate between two banks by epoch parity (a rank is at most
-// one call ahead of a peer: it needs the peer's row of the current call to finish it). Every
-// thread of the CTA calls this; o is read from threads tid < kD, lse (natural log) from thread 0.
+// is needed. Waits are bounded by wait_ns (on timeout the status records it and the share is
+// zeros). The epoch is the mailbox header counter of the CTA's linear index, advanced once per
+// call by every CTA of the grid (see advance_epoch), so calls replay from a CUDA graph and the
+// CTAs of one row always agree on it; words alternate between two banks by epoch parity (a rank
+// is at most one call ahead of a peer: it needs the peer's row of the current call to finish it).
 template <bool kExchange>
-__device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, float o, float lse) {
+__device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, int d0, int nd, float o, float lse) {
     const int tid = threadIdx.x;
+    const bool first = d0 == 0;
     if constexpr (!kExchange) {
-        if (tid < kD) p.out[row * kD + tid] = o;
-        if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = lse;
+        if (tid < nd) p.out[row * kD + d0 + tid] = o;
+        if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = lse;
     } else {
         constexpr int kMaxRanks = kCombineThreads;
-        __shared__ float o_s[kD + 1];     // the local row, then its lse
+        __shared__ float o_s[kD + 1];       // the local share, then its lse
         __shared__ float lse_s[kMaxRanks];  // every rank's lse of the row
         __shared__ int timed_out;
         const int R = p.n_ranks;
         const int64_t n_rows = (int64_t) p.n_seqs * p.n_head;
         uint8_t *own = p.mailboxes[p.rank];
         const int cta = (blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z;
-        uint32_t *my_epoch = reinterpret_cast<uint32_t *>(own) + cta;
-        const uint32_t epoch = *my_epoch + 1u;
+        const uint32_t epoch = reinterpret_cast<const uint32_t *>(own)[cta] + 1u;
         const int bank = (int) (epoch & 1u);
         const size_t w_off = exchange::words_offset(R, n_rows);
         const int64_t slot = n_rows * (kD + 1);  // words per (bank, source)
-        if (tid < kD) o_s[tid] = o;
-        if (tid == 0) o_s[kD] = lse, timed_out = 0;
+        if (tid < nd) o_s[tid] = o;
+        if (tid == 0) o_s[nd] = lse, timed_out = 0;
         __syncthreads();
         const uint64_t tag = (uint64_t) epoch << 32;
-        for (int i = tid; i < R * (kD + 1); i += blockDim.x) {
-            const int r = i / (kD + 1), d = i - r * (kD + 1);
+        const int per = nd + (first ? 1 : 0);  // words this CTA sends to each rank
+        for (int i = tid; i < R * per; i += blockDim.x) {
+            const int r = i / per, e = i - r * per;
+            const int d = e < nd ? d0 + e : kD;
             uint64_t *w = reinterpret_cast<uint64_t *>(p.mailboxes[r] + w_off) + ((int64_t) bank * R + p.rank) * slot +
                           row * (kD + 1) + d;
-            exchange::st_relaxed_sys_u64(w, tag | __float_as_uint(o_s[d]));
+            exchange::st_relaxed_sys_u64(w, tag | __float_as_uint(o_s[e]));
         }
-        // Poll the own mailbox: thread r < R the lse word of source r, thread d < kD the value
-        // words of element d from every source (its own values; the lse comes through shared
-        // memory after the barrier).
+        // Poll the own mailbox: thread r < R the lse word of source r, thread t < nd the value
+        // words of dim d0 + t from every source (the lse values come through shared memory).
         const uint64_t *base = reinterpret_cast<const uint64_t *>(own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
         volatile int *const abort = &timed_out;
         auto await = [&](const uint64_t *w, float &v, int src) {
@@ -895,14 +937,14 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         };
         if (tid < R) await(base + (int64_t) tid * slot + kD, lse_s[tid], tid);
         __syncthreads();
-        if (tid < kD) {
+        if (tid < nd) {
             float v = 0.f, l = -INFINITY;
             float M = -INFINITY;
             for (int r = 0; r < R; r++) M = fmaxf(M, lse_s[r]);
             float den = 0.f, acc = 0.f;
             for (int r = 0; r < R; r++) {
                 float x;
-                await(base + (int64_t) r * slot + tid, x, r);
+                await(base + (int64_t) r * slot + d0 + tid, x, r);
                 if (M != -INFINITY) {
                     const float wt = __expf(lse_s[r] - M);
                     den += wt;
@@ -913,121 +955,178 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
                 v = acc / den;
                 l = M + __logf(den);
             }
-            p.out[row * kD + tid] = v;
-            if (tid == 0 && p.lse_out != nullptr) p.lse_out[row] = l;
+            p.out[row * kD + d0 + tid] = v;
+            if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = l;
         }
         __syncthreads();
-        if (timed_out && tid < kD) p.out[row * kD + tid] = 0.f;  // every thread's result is void
-        if (tid == 0) {
-            if (timed_out && p.lse_out != nullptr) p.lse_out[row] = -INFINITY;
-            *my_epoch = epoch;  // read by this CTA's successor in the next call
+        if (timed_out && tid < nd) p.out[row * kD + d0 + tid] = 0.f;  // every thread's result is void
+        if (timed_out && tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = -INFINITY;
+    }
+}
+
+// Every CTA of an exchanging combine grid, whatever it does, advances its epoch counter once per
+// call (after its last read of it), so CTAs that share a row in one call have the same history.
+template <bool kExchange>
+__device__ __forceinline__ void advance_epoch(const CombineParams &p) {
+    if constexpr (kExchange) {
+        if (threadIdx.x == 0) {
+            uint32_t *ctr = reinterpret_cast<uint32_t *>(p.mailboxes[p.rank]) +
+                            (blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z;
+            *ctr = *ctr + 1u;
         }
     }
 }
 
-// One CTA per (sequence b, head group hg, KV head w of the group, query head n of its group):
-// the 128 dims of one output row. The row's partial pieces (one per CTA whose range touched the
-// segment; up to gridDim of the split kernel for a single long sequence) are handled in three
-// passes: one thread per piece finds its partial row and lse (the only place the range
-// arithmetic runs), then the weights exp2(lse - M), then the 8 warps sum weighted rows with the
-// loads of several pieces in flight per warp (lanes own 4 dims each).
+// Merges (m, den, acc) running states: M = max, weights 2^(m - M).
+__device__ __forceinline__ void merge_state(float &m, float &den, float4 &acc, float m2, float den2, float4 acc2) {
+    const float M = fmaxf(m, m2);
+    if (M == -INFINITY) return;
+    const float f1 = exp2f(m - M), f2 = exp2f(m2 - M);
+    den = den * f1 + den2 * f2;
+    acc.x = acc.x * f1 + acc2.x * f2;
+    acc.y = acc.y * f1 + acc2.y * f2;
+    acc.z = acc.z * f1 + acc2.z * f2;
+    acc.w = acc.w * f1 + acc2.w * f2;
+    m = M;
+}
 
+// Grid (sequence b, head group hg, 32 x dsplit): CTA z owns query row z / dsplit of the group's
+// 4 x 8 partial rows (KV head w, query head n) and dims [d0, d0 + nd) of it, nd = 128 / dsplit.
+// The row's pieces - one per split CTA whose range touched the segment, up to the split grid for
+// a single long sequence - are read in one pass: lane group j of a warp (nd / 4 lanes, a float4
+// each) takes pieces j, j + stride, ... and loads each piece's lse together with its slice of O,
+// so the whole row costs one memory round trip after the prefix; each lane keeps an online
+// (max, sum, accumulator) state, merged across lane groups by shuffles and across warps in shared
+// memory. Piece i is split CTA c0 + i; its record is slot 0 of that CTA's pair, except for the
+// first piece when the CTA's range began in an earlier segment (slot 1).
 template <bool kExchange>
-__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const CombineParams p) {
+__global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(const CombineParams p) {
     pdl_wait();  // the split grid's partials and prefix are complete and visible
+    const int S = p.dsplit;
     const int b = blockIdx.x, hg = blockIdx.y;
-    const int w = blockIdx.z / kMaxGroup, n = blockIdx.z % kMaxGroup;
+    const int zr = blockIdx.z / S, q = blockIdx.z - zr * S;
+    const int w = zr / kMaxGroup, n = zr % kMaxGroup;
     const int kvh = hg * kHeadsPerGroup + w;
-    if (kvh >= p.n_head_kv || n >= p.group) return;
+    const int nd = kD / S, d0 = q * nd;
+    if (kvh >= p.n_head_kv || n >= p.group) {
+        advance_epoch<kExchange>(p);
+        return;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t out_row = (int64_t) b * p.n_head + (int64_t) kvh * p.group + n;
-    const int32_t pb = p.prefix[b];
-    const int np = p.prefix[b + 1] - pb;
-    if (np == 0) {
-        finish_row<kExchange>(p, out_row, 0.f, -INFINITY);
-        return;
-    }
-    const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
-    const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
-    const int c0 = cta_of(x0, P, p.grid);
-    const int c1 = cta_of(x0 + np - 1, P, p.grid);
-    if (c0 == c1) {  // the split kernel wrote this row directly (with an exchange, its local row)
-        if constexpr (kExchange)
-            finish_row<true>(p, out_row, tid < kD ? p.out[out_row * kD + tid] : 0.f, p.lse_out[out_row]);
-        return;
-    }
     const int part_row = w * kMaxGroup + n;
-    const int n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
-    __shared__ float wt_s[kMaxCtas];
-    __shared__ int row_s[kMaxCtas];
-    __shared__ float red_max[kCombineWarps], red_sum[kCombineWarps];
-    __shared__ __align__(16) float acc_s[kCombineWarps][kD];  // written as float4
-    // Pass 1: piece i = CTA c0 + i. Its slot is 1 if the CTA's range began in an earlier
-    // segment; an empty range (more CTAs than page-groups) contributes nothing.
-    float mx = -INFINITY;
-    for (int i = tid; i < n_pc; i += kCombineThreads) {
-        const int c = c0 + i;
-        const int64_t lo = range_lo(c, P, p.grid);
-        int prow = -1;
-        float l = -INFINITY;
-        if (range_lo(c + 1, P, p.grid) > lo) {
-            prow = (c * 2 + (lo < x0 ? 1 : 0)) * kPartRows + part_row;
-            l = p.part_lse[prow];
-        }
-        row_s[i] = prow;
-        wt_s[i] = l;
-        mx = fmaxf(mx, l);
-    }
-    mx = warp_max_xor(mx, 1);
-    if (lane == 0) red_max[warp] = mx;
-    __syncthreads();
-    float M = red_max[0];
-    for (int i = 1; i < kCombineWarps; i++) M = fmaxf(M, red_max[i]);
-    // Pass 2: weights (0 for empty pieces or when every piece is empty).
-    float den = 0.f;
-    for (int i = tid; i < n_pc; i += kCombineThreads) {
-        const float wv = (row_s[i] >= 0 && M != -INFINITY) ? exp2f(wt_s[i] - M) : 0.f;
-        wt_s[i] = wv;
-        den += wv;
-    }
-    den = warp_sum_xor(den, 1);
-    if (lane == 0) red_sum[warp] = den;
-    __syncthreads();
-    // Pass 3: warp k sums pieces k, k + 8, ..., loading 24 of them at a time before any use, so a
-    // long sequence split over a whole grid of CTAs (148 pieces) costs one memory round trip here.
-    constexpr int kBatch = 24;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i0 = warp; i0 < n_pc; i0 += kCombineWarps * kBatch) {
-        float4 v[kBatch];
-        float wv[kBatch];
+    const int lp = nd / 4;  // lanes per piece
+    const int pw = 32 / lp;  // pieces per warp load
+    const int sub = warp * pw + lane / lp, li = lane % lp;
+    const int stride = kCombineWarps * pw;
+    constexpr int kBatch = 8;  // one batch covers the pieces of a lane group in every dsplit case
+    float lv[kBatch];
+    float4 v[kBatch];
+    // Loads one batch: pieces i0, i0 + stride, ... of the CTA range [c0, c0 + n_pc).
+    auto load = [&](int i0, int c0, int n_pc, int first_slot, bool may_be_empty, int64_t P) {
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
-            const int i = i0 + k * kCombineWarps;
-            wv[k] = i < n_pc ? wt_s[i] : 0.f;
-            v[k] = wv[k] > 0.f ? reinterpret_cast<const float4 *>(p.part_o + (int64_t) row_s[i] * kD)[lane]
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < kBatch; k++) {
-            if (wv[k] > 0.f) {
-                acc.x += wv[k] * v[k].x;
-                acc.y += wv[k] * v[k].y;
-                acc.z += wv[k] * v[k].z;
-                acc.w += wv[k] * v[k].w;
+            const int i = i0 + k * stride;
+            lv[k] = -INFINITY;
+            v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n_pc) {
+                const int c = c0 + i;
+                bool ok = true;
+                if (may_be_empty) ok = range_lo(c + 1, P, p.grid) > range_lo(c, P, p.grid);
+                if (ok) {
+                    const int64_t prow = (int64_t) (c * 2 + (i == 0 ? first_slot : 0)) * kPartRows + part_row;
+                    lv[k] = p.part_lse[prow];
+                    v[k] = reinterpret_cast<const float4 *>(p.part_o + prow * kD + d0)[li];
+                }
             }
         }
-    }
-    reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
-    __syncthreads();
-    float total = 0.f, o = 0.f;
-    if (tid < kD) {
-        for (int i = 0; i < kCombineWarps; i++) {
-            total += red_sum[i];
-            o += acc_s[i][tid];
+    };
+    float m = -INFINITY, den = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto accumulate = [&]() {
+        float bm = m;
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) bm = fmaxf(bm, lv[k]);
+        if (bm != -INFINITY) {
+            const float f = exp2f(m - bm);
+            den *= f;
+            acc.x *= f, acc.y *= f, acc.z *= f, acc.w *= f;
+#pragma unroll
+            for (int k = 0; k < kBatch; k++) {
+                const float wt = exp2f(lv[k] - bm);  // 0 for an absent piece
+                den += wt;
+                acc.x += wt * v[k].x, acc.y += wt * v[k].y, acc.z += wt * v[k].z, acc.w += wt * v[k].w;
+            }
+            m = bm;
+        }
+    };
+    // One sequence whose head groups divide the split grid evenly (a single context over the
+    // whole grid): the row's pieces are loaded in the same round trip as the prefix, on the
+    // assumption that head group hg's segment is exactly CTAs [hg g, (hg + 1) g), g = grid / n_hg.
+    // That holds when the sequence has at least g pages (P >= grid: CTA hg g's range then starts
+    // at the segment's first page-group and no range is empty, so every piece is its CTA's
+    // first, slot 0); otherwise the pieces are loaded again below.
+    const int per_hg = p.grid / p.n_hg;
+    const bool guess = p.n_seqs == 1 && per_hg * p.n_hg == p.grid && per_hg >= 2 && per_hg <= stride * kBatch;
+    if (guess) load(sub, hg * per_hg, per_hg, 0, false, 0);
+    const int32_t pb = p.prefix[b];
+    const int np = p.prefix[b + 1] - pb;
+    const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
+    if (guess && P >= p.grid) {
+        accumulate();
+    } else {
+        if (np == 0) {
+            finish_row<kExchange>(p, out_row, d0, nd, 0.f, -INFINITY);
+            advance_epoch<kExchange>(p);
+            return;
+        }
+        const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
+        const int c0 = cta_of(x0, P, p.grid);
+        const int c1 = cta_of(x0 + np - 1, P, p.grid);
+        if (c0 == c1) {  // the split kernel wrote this row directly (with an exchange, its local row)
+            if constexpr (kExchange)
+                finish_row<true>(p, out_row, d0, nd, tid < nd ? p.out[out_row * kD + d0 + tid] : 0.f,
+                                 p.lse_out[out_row]);
+            advance_epoch<kExchange>(p);
+            return;
+        }
+        const int n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
+        const int first_slot = range_lo(c0, P, p.grid) < x0 ? 1 : 0;
+        const bool may_be_empty = P < p.grid;  // only then can a split CTA's range be empty
+        for (int i0 = sub; i0 < n_pc; i0 += stride * kBatch) {
+            load(i0, c0, n_pc, first_slot, may_be_empty, P);
+            accumulate();
         }
     }
-    finish_row<kExchange>(p, out_row, total > 0.f ? o / total : 0.f,
+    // Lane groups of a warp hold the same dims: merge them (offsets lp, 2 lp, ...).
+    for (int off = lp; off < 32; off <<= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+        const float den2 = __shfl_xor_sync(0xffffffffu, den, off);
+        float4 a2;
+        a2.x = __shfl_xor_sync(0xffffffffu, acc.x, off);
+        a2.y = __shfl_xor_sync(0xffffffffu, acc.y, off);
+        a2.z = __shfl_xor_sync(0xffffffffu, acc.z, off);
+        a2.w = __shfl_xor_sync(0xffffffffu, acc.w, off);
+        merge_state(m, den, acc, m2, den2, a2);
+    }
+    __shared__ float m_s[kCombineWarps], den_s[kCombineWarps];
+    __shared__ __align__(16) float acc_s[kCombineWarps][kD];  // written as float4
+    if (lane < lp) reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
+    if (lane == 0) m_s[warp] = m, den_s[warp] = den;
+    __syncthreads();
+    float M = -INFINITY;
+    for (int k = 0; k < kCombineWarps; k++) M = fmaxf(M, m_s[k]);
+    float o = 0.f, total = 0.f;
+    if (M != -INFINITY && tid < nd) {
+        for (int k = 0; k < kCombineWarps; k++) {
+            const float f = exp2f(m_s[k] - M);
+            total += den_s[k] * f;
+            o += acc_s[k][tid] * f;
+        }
+    }
+    finish_row<kExchange>(p, out_row, d0, nd, total > 0.f ? o / total : 0.f,
                           total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY);
+    advance_epoch<kExchange>(p);
 }
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.

@@ -478,7 +478,8 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     c.n_ranks = ex ? ex->n_ranks : 1;
     c.wait_ns = ex ? ex->wait_ns : 0;
     c.status = p.status;
-    cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, decode::kPartRows);
+    c.dsplit = decode::combine_dsplit(p.n_seqs, p.n_hg, grid, ex != nullptr, exchange::kMaxCtas);
+    cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, (unsigned) (decode::kPartRows * c.dsplit));
     cfg.blockDim = dim3(decode::kCombineThreads);
     cfg.dynamicSmemBytes = 0;
     if (ex)

@@ -75,6 +75,36 @@ def test_split_count_invariance(n_ctas):
     _assert_parity(out, ex, gg)
 
 
+@pytest.mark.parametrize("Hq,Hkv,ctx,n_ctas,pad_pages", [
+    (32, 4, 16384 + 5, 0, 0),    # one head group over the whole grid (148 pieces per row)
+    (16, 8, 513, 0, 0),          # config 1: two head groups, grid 34 = 2 x 17
+    (16, 8, 4000, 7, 0),         # a grid the head groups do not divide
+    (48, 12, 3000, 30, 0),       # three head groups, grid 30 = 3 x 10
+    (48, 12, 3000, 0, 0),        # three head groups, grid 148
+    (32, 4, 300, 0, 40),         # table wider than the sequence: more CTAs than page-groups
+    (16, 8, 200, 0, 20),         # the same with two head groups
+])
+def test_single_sequence_combine(Hq, Hkv, ctx, n_ctas, pad_pages):
+    # One sequence split over many CTAs: the combine loads the row's pieces together with the
+    # prefix when the head groups divide the grid and every CTA holds a page-group; the other
+    # cases (uneven grid, empty CTA ranges from a table wider than the sequence) take the
+    # general path. Every case against the oracle.
+    rng = np.random.default_rng(ctx + Hkv)
+    bt, n_pages = scattered_block_tables(rng, [ctx])
+    if pad_pages:
+        bt = np.concatenate([bt, np.full((1, pad_pages), bt[0, 0], np.int32)], axis=1)
+    kc, vc = random_cache(rng, n_pages, Hkv)
+    q = random_q(rng, 1, Hq)
+    dev = "cuda"
+    f = lambda a: torch.from_numpy(a.view(np.int16)).to(dev).view(torch.float16)
+    out, lse = L.attn_decode(f(kc), f(vc), torch.from_numpy(q).to(dev), torch.from_numpy(bt).to(dev),
+                             torch.tensor([ctx], dtype=torch.int32, device=dev), SCALE, n_ctas=n_ctas, want_lse=True)
+    L.check_status()
+    ex, lse_ex = O.paged_attn(q, [0], [ctx - 1], kc, vc, bt, [ctx], SCALE, mode=O.MODE_EXACT, want_lse=True)
+    assert within(out.cpu().numpy(), ex), max_err(out.cpu().numpy(), ex)
+    assert np.allclose(lse.cpu().numpy(), lse_ex, atol=1e-3, rtol=1e-4)
+
+
 def test_page_permutation_is_bit_invariant():
     # Same K/V content placed in differently permuted pages -> identical output bits.
     rng = np.random.default_rng(5)
