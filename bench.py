@@ -901,7 +901,7 @@ def config4_split(L, dev, world):
     import torch
     import torch.distributed as dist
 
-    from localstack_b200.shard import KvSplitDecode, chunk_keys
+    from localstack_b200.shard import KvSplitDecode, PeerBarrier, chunk_keys
 
     rank = dist.get_rank()
     ctx = 131072
@@ -930,9 +930,14 @@ def config4_split(L, dev, world):
     # L2 flush by READING 256 MB: the cache is left full of clean lines (a flush by writing would
     # leave dirty lines whose write-back then competes with the decode's reads).
     flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
-    align = torch.zeros(1, device=dev)
+    # Each timed step starts on every rank together: a device-side barrier of the ranks' streams
+    # (one exchange of a dummy row over peer memory; exit skew about one NVLink store latency,
+    # where an NCCL all-reduce's exit is skewed by its ring/tree order), then ~10 us of GPU sleep
+    # so every host has queued the step behind it.
+    pbar = PeerBarrier(dev)
     res = {"n_gpus": world, "pages_per_rank": n_local, "l2": "flushed (256 MB read) before each step",
            "timing": "CUDA graph of one step, max over ranks",
+           "start": "device peer barrier + 10 us GPU sleep before each step (ranks start within ~1 us)",
            "check": "every rank's merged output after the timed replays vs a one-GPU decode of the whole context "
                     "(|d| <= 2e-3 + 1e-2 |ref|), max over ranks"}
     ok_all = True
@@ -956,7 +961,8 @@ def config4_split(L, dev, world):
         torch.cuda.synchronize()
         for a, b in evs:
             flush.sum()
-            dist.all_reduce(align)  # both ranks' streams start the step together
+            pbar()
+            torch.cuda._sleep(20000)
             a.record()
             g.replay()
             b.record()
@@ -978,6 +984,7 @@ def config4_split(L, dev, world):
             ok_all = ok_all and entry["within_tolerance"]
         dec.close()
         res[exchange] = entry
+    pbar.close()
     res["ms"], res["gbs"] = res["fused"]["ms"], res["fused"]["gbs"]
     res["outputs_match"] = ok_all
     if not ok_all and rank == 0:

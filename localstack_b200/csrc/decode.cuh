@@ -69,7 +69,15 @@ struct Params {
     const int32_t *start_flag;  // optional: the producer waits for it to be non-zero before loading
 };
 
-__host__ __device__ inline int64_t range_lo(int c, int64_t P, int G) { return ((int64_t) c * P) / G; }
+// First page-group of CTA c's range: floor(c P / G). Computed in double precision, which is
+// exact here: c P < 2^53 is represented exactly, the quotient is correctly rounded, and a
+// non-integer quotient lies at least 1/G below the next integer - more than half an ulp of any
+// value below 2^42 while G < 4096 (G <= kMaxCtas, P below 2^31 page-groups) - so the floor of
+// the rounded quotient is the floor of the exact one. (A 64-bit integer division costs several
+// times the instructions.)
+__host__ __device__ inline int64_t range_lo(int c, int64_t P, int G) {
+    return (int64_t) ((double) c * (double) P / (double) G);
+}
 
 // Keys of sequence b inside the call's range, counted from the range's first page.
 __device__ __forceinline__ int range_len(const Params &p, int32_t len) {
@@ -79,7 +87,7 @@ __device__ __forceinline__ int range_len(const Params &p, int32_t len) {
 
 // Index of the CTA whose range [lo_c, lo_{c+1}) contains page-group x.
 __device__ inline int cta_of(int64_t x, int64_t P, int G) {
-    int c = (int) ((x * G) / P);
+    int c = (int) ((double) x * (double) G / (double) P);
     while (c + 1 < G && range_lo(c + 1, P, G) <= x) c++;
     while (c > 0 && range_lo(c, P, G) > x) c--;
     return c;
@@ -869,6 +877,13 @@ __host__ __device__ inline int combine_dsplit(int n_seqs, int n_hg, int grid, bo
     return d;
 }
 
+// Batches whose segments average fewer than 8 pieces (more sequences than a few per grid) merge
+// a row per warp (decode_combine_rows_kernel); longer rows spread over CTAs.
+__host__ __device__ inline bool combine_by_rows(int n_seqs, int n_hg, int grid) {
+    const int64_t segs = (int64_t) n_seqs * n_hg;
+    return segs > 0 && grid / segs < 8;
+}
+
 // The end of a combine CTA's share of a row: dims [d0, d0 + nd), thread t < nd holding dim
 // d0 + t in o, and the row's lse (natural log; every CTA of the row has the same). Without an
 // exchange, out (and, from the row's first CTA, lse_out) get the local values. With one, the
@@ -1000,7 +1015,7 @@ __device__ __forceinline__ void merge_state(float &m, float &den, float4 &acc, f
 // memory. Piece i is split CTA c0 + i; its record is slot 0 of that CTA's pair, except for the
 // first piece when the CTA's range began in an earlier segment (slot 1).
 template <bool kExchange>
-__global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(const CombineParams p) {
+__global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_kernel(const CombineParams p) {
     pdl_wait();  // the split grid's partials and prefix are complete and visible
     const int S = p.dsplit;
     const int b = blockIdx.x, hg = blockIdx.y;
@@ -1069,29 +1084,47 @@ __global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(cons
     const int per_hg = p.grid / p.n_hg;
     const bool guess = p.n_seqs == 1 && per_hg * p.n_hg == p.grid && per_hg >= 2 && per_hg <= stride * kBatch;
     if (guess) load(sub, hg * per_hg, per_hg, 0, false, 0);
-    const int32_t pb = p.prefix[b];
-    const int np = p.prefix[b + 1] - pb;
-    const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
-    if (guess && P >= p.grid) {
+    // The row's plan, worked out by one thread (the range arithmetic is the costly part of a
+    // short row) and shared: 0 = the guess holds, 1 = no keys, 2 = written by one split CTA,
+    // 3 = pieces c0 .. c0 + n_pc - 1.
+    __shared__ int plan_s[4];
+    __shared__ long long plan_P;
+    if (tid == 0) {
+        const int32_t pb = p.prefix[b];
+        const int np = p.prefix[b + 1] - pb;
+        const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
+        int mode = 0, c0 = 0, n_pc = 0, first_slot = 0;
+        if (!(guess && P >= p.grid)) {
+            if (np == 0) {
+                mode = 1;
+            } else {
+                const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
+                c0 = cta_of(x0, P, p.grid);
+                const int c1 = cta_of(x0 + np - 1, P, p.grid);
+                mode = c0 == c1 ? 2 : 3;
+                n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
+                first_slot = range_lo(c0, P, p.grid) < x0 ? 1 : 0;
+            }
+        }
+        plan_s[0] = mode, plan_s[1] = c0, plan_s[2] = n_pc, plan_s[3] = first_slot;
+        plan_P = P;
+    }
+    __syncthreads();
+    const int mode = plan_s[0];
+    if (mode == 0) {
         accumulate();
+    } else if (mode == 1) {
+        finish_row<kExchange>(p, out_row, d0, nd, 0.f, -INFINITY);
+        advance_epoch<kExchange>(p);
+        return;
+    } else if (mode == 2) {  // the split kernel wrote this row directly (with an exchange, its local row)
+        if constexpr (kExchange)
+            finish_row<true>(p, out_row, d0, nd, tid < nd ? p.out[out_row * kD + d0 + tid] : 0.f, p.lse_out[out_row]);
+        advance_epoch<kExchange>(p);
+        return;
     } else {
-        if (np == 0) {
-            finish_row<kExchange>(p, out_row, d0, nd, 0.f, -INFINITY);
-            advance_epoch<kExchange>(p);
-            return;
-        }
-        const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
-        const int c0 = cta_of(x0, P, p.grid);
-        const int c1 = cta_of(x0 + np - 1, P, p.grid);
-        if (c0 == c1) {  // the split kernel wrote this row directly (with an exchange, its local row)
-            if constexpr (kExchange)
-                finish_row<true>(p, out_row, d0, nd, tid < nd ? p.out[out_row * kD + d0 + tid] : 0.f,
-                                 p.lse_out[out_row]);
-            advance_epoch<kExchange>(p);
-            return;
-        }
-        const int n_pc = c1 - c0 + 1;  // <= p.grid <= kMaxCtas
-        const int first_slot = range_lo(c0, P, p.grid) < x0 ? 1 : 0;
+        const int c0 = plan_s[1], n_pc = plan_s[2], first_slot = plan_s[3];
+        const int64_t P = plan_P;
         const bool may_be_empty = P < p.grid;  // only then can a split CTA's range be empty
         for (int i0 = sub; i0 < n_pc; i0 += stride * kBatch) {
             load(i0, c0, n_pc, first_slot, may_be_empty, P);
@@ -1127,6 +1160,90 @@ __global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(cons
     finish_row<kExchange>(p, out_row, d0, nd, total > 0.f ? o / total : 0.f,
                           total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY);
     advance_epoch<kExchange>(p);
+}
+
+// The combine for a batch of short rows (no exchange): grid (sequence b, head group hg, KV head
+// w of the group), warp n merging query row n's pieces on its own - lane l the float4 of dims
+// 4l .. 4l + 3 of each piece, kBatch pieces in flight, an online (max, sum, accumulator) state -
+// and writing the row, so nothing crosses warps after the segment's plan, which thread 0 works
+// out once for the CTA's eight rows. Chosen where segments have few pieces (many sequences per
+// grid); a long row over many pieces takes decode_combine_kernel, which spreads it over CTAs.
+__global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_rows_kernel(const CombineParams p) {
+    pdl_wait();  // the split grid's partials and prefix are complete and visible
+    const int b = blockIdx.x, hg = blockIdx.y, w = blockIdx.z;
+    const int kvh = hg * kHeadsPerGroup + w;
+    if (kvh >= p.n_head_kv) return;
+    const int tid = threadIdx.x, lane = tid & 31, n = tid >> 5;
+    __shared__ int plan_s[4];  // mode (1 no keys, 2 written by one split CTA, 3 pieces), c0, n_pc, first slot
+    __shared__ long long plan_P;
+    if (tid == 0) {
+        const int32_t pb = p.prefix[b];
+        const int np = p.prefix[b + 1] - pb;
+        const int64_t P = (int64_t) p.n_hg * p.prefix[p.n_seqs];
+        int mode = 1, c0 = 0, n_pc = 0, first_slot = 0;
+        if (np > 0) {
+            const int64_t x0 = (int64_t) p.n_hg * pb + (int64_t) hg * np;
+            c0 = cta_of(x0, P, p.grid);
+            const int c1 = cta_of(x0 + np - 1, P, p.grid);
+            mode = c0 == c1 ? 2 : 3;
+            n_pc = c1 - c0 + 1;
+            first_slot = range_lo(c0, P, p.grid) < x0 ? 1 : 0;
+        }
+        plan_s[0] = mode, plan_s[1] = c0, plan_s[2] = n_pc, plan_s[3] = first_slot;
+        plan_P = P;
+    }
+    __syncthreads();
+    const int mode = plan_s[0];
+    if (n >= p.group || mode == 2) return;
+    const int64_t out_row = (int64_t) b * p.n_head + (int64_t) kvh * p.group + n;
+    float4 *dst = reinterpret_cast<float4 *>(p.out + out_row * kD) + lane;
+    if (mode == 1) {
+        *dst = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane == 0 && p.lse_out != nullptr) p.lse_out[out_row] = -INFINITY;
+        return;
+    }
+    const int c0 = plan_s[1], n_pc = plan_s[2], first_slot = plan_s[3];
+    const int64_t P = plan_P;
+    const bool may_be_empty = P < p.grid;
+    const int part_row = w * kMaxGroup + n;
+    constexpr int kBatch = 8;
+    float m = -INFINITY, den = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = 0; i0 < n_pc; i0 += kBatch) {
+        float lv[kBatch];
+        float4 v[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int i = i0 + k, c = c0 + i;
+            lv[k] = -INFINITY;
+            v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n_pc && (!may_be_empty || range_lo(c + 1, P, p.grid) > range_lo(c, P, p.grid))) {
+                const int64_t prow = (int64_t) (c * 2 + (i == 0 ? first_slot : 0)) * kPartRows + part_row;
+                lv[k] = p.part_lse[prow];
+                v[k] = reinterpret_cast<const float4 *>(p.part_o + prow * kD)[lane];
+            }
+        }
+        float bm = m;
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) bm = fmaxf(bm, lv[k]);
+        if (bm != -INFINITY) {
+            const float f = exp2f(m - bm);
+            den *= f;
+            acc.x *= f, acc.y *= f, acc.z *= f, acc.w *= f;
+#pragma unroll
+            for (int k = 0; k < kBatch; k++) {
+                const float wt = exp2f(lv[k] - bm);  // 0 for an absent piece
+                den += wt;
+                acc.x += wt * v[k].x, acc.y += wt * v[k].y, acc.z += wt * v[k].z, acc.w += wt * v[k].w;
+            }
+            m = bm;
+        }
+    }
+    // Divided as decode_combine_kernel divides: a row of up to 8 pieces then gets the same bits
+    // from both kernels (the same weights, summed in piece order).
+    *dst = den > 0.f ? make_float4(acc.x / den, acc.y / den, acc.z / den, acc.w / den) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lane == 0 && p.lse_out != nullptr)
+        p.lse_out[out_row] = den > 0.f ? (m + __log2f(den)) * 0.69314718055994531f : -INFINITY;
 }
 
 // LSE merge of n_parts partial results (natural-log lse), one warp per output row.

@@ -479,9 +479,14 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     c.wait_ns = ex ? ex->wait_ns : 0;
     c.status = p.status;
     c.dsplit = decode::combine_dsplit(p.n_seqs, p.n_hg, grid, ex != nullptr, exchange::kMaxCtas);
-    cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, (unsigned) (decode::kPartRows * c.dsplit));
     cfg.blockDim = dim3(decode::kCombineThreads);
     cfg.dynamicSmemBytes = 0;
+    if (!ex && decode::combine_by_rows(p.n_seqs, p.n_hg, grid)) {
+        cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, decode::kHeadsPerGroup);
+        return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_rows_kernel, c),
+                                "decode_combine_rows_kernel");
+    }
+    cfg.gridDim = dim3((unsigned) p.n_seqs, (unsigned) p.n_hg, (unsigned) (decode::kPartRows * c.dsplit));
     if (ex)
         return launch_pdl_check(cudaLaunchKernelEx(&cfg, decode::decode_combine_kernel<true>, c),
                                 "decode_combine_kernel (exchange)");

@@ -78,6 +78,76 @@ def all_gather_records(gathered, local, group=None):
     return gathered
 
 
+class PeerMailboxes:
+    """This rank's exchange mailbox for `rows` rows (allocated by the library in this GPU's memory)
+    and the peers' mailboxes mapped through CUDA IPC handles shared once over the process group;
+    `ptrs` is the int64 device tensor of the R mailbox addresses the exchange kernels take. Every
+    rank of `group` builds it collectively and calls close() collectively."""
+
+    def __init__(self, rows, device, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        L = lib()
+        nbytes = L.lstk_cuda_mailbox_bytes(self.world, rows, HEAD_DIM)
+        own, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            check(L.lstk_cuda_mailbox_alloc(nbytes, ctypes.byref(own), handle))
+        self._own = own
+        self._peers = []
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(own.value)
+                continue
+            peer = ctypes.c_void_p()
+            check(L.lstk_cuda_mailbox_open(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)))
+            self._peers.append(peer)
+            ptrs.append(peer.value)
+        self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)
+
+    def close(self):
+        """Releases the peer mappings and the own mailbox once every rank is done with them."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still writes into another's mailbox
+        L = lib()
+        for peer in self._peers:
+            check(L.lstk_cuda_mailbox_close(peer))
+        self._peers = []
+        dist.barrier(group=self.group)  # no rank still maps this rank's mailbox
+        check(L.lstk_cuda_mailbox_free(self._own))
+        self._own = None
+
+
+class PeerBarrier:
+    """A barrier of the ranks' CUDA streams, on the device: one exchange-merge of a single dummy
+    row over peer memory (lstk_cuda_attn_exchange_merge), so each rank's kernel returns once every
+    rank's stream has reached the same call (bounded by wait_ns; a timeout sets
+    LSTK_ERR_TIMEOUT). Its exit skew across ranks is about one NVLink store latency, far below
+    the exit skew of a small NCCL collective; used to start the ranks of a timed step together."""
+
+    def __init__(self, device, group=None, wait_ns=0):
+        self.mb = PeerMailboxes(1, device, group)
+        self.wait_ns = int(wait_ns)
+        self.o = torch.zeros(HEAD_DIM, dtype=torch.float32, device=device)
+        self.lse = torch.zeros(1, dtype=torch.float32, device=device)
+        self.out = torch.empty_like(self.o)
+        self.lse_out = torch.empty_like(self.lse)
+
+    def __call__(self):
+        check(lib().lstk_cuda_attn_exchange_merge(_p(self.mb.ptrs), self.mb.rank, self.mb.world, _p(self.o),
+                                                  _p(self.lse), 1, HEAD_DIM, self.wait_ns, _p(self.out),
+                                                  _p(self.lse_out), _stream(None, self.o.device)))
+
+    def close(self):
+        self.mb.close()
+
+
 class KvSplitDecode:
     """Decode of sequences whose pages are split over the ranks of `group` in contiguous chunks.
 
@@ -101,46 +171,18 @@ class KvSplitDecode:
         self.ws = DecodeWorkspace(n_seqs, n_head, n_head_kv, device)
         self.out = torch.empty((n_seqs, n_head, HEAD_DIM), dtype=torch.float32, device=device)
         self.lse = torch.empty((n_seqs, n_head), dtype=torch.float32, device=device)
-        self._own, self._peers = None, []
+        self._mb = None
         if exchange == "collective":
             self.gathered = torch.empty(self.world * rec, dtype=torch.float32, device=device)
         else:
-            self._open_mailboxes(device)
-
-    def _open_mailboxes(self, device):
-        L = lib()
-        nbytes = L.lstk_cuda_mailbox_bytes(self.world, self.rows, HEAD_DIM)
-        own, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
-        with torch.cuda.device(device):
-            check(L.lstk_cuda_mailbox_alloc(nbytes, ctypes.byref(own), handle))
-        self._own = own
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=self.group)
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(own.value)
-                continue
-            peer = ctypes.c_void_p()
-            check(L.lstk_cuda_mailbox_open(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)))
-            self._peers.append(peer)
-            ptrs.append(peer.value)
-        self.mailboxes = torch.tensor(ptrs, dtype=torch.int64, device=device)
-        dist.barrier(group=self.group)
+            self._mb = PeerMailboxes(self.rows, device, group)
+            self.mailboxes = self._mb.ptrs
 
     def close(self):
         """Releases the peer mappings and the own mailbox once every rank is done with them."""
-        if self._own is None:
-            return
-        torch.cuda.synchronize()
-        dist.barrier(group=self.group)  # no rank still writes into another's mailbox
-        L = lib()
-        for peer in self._peers:
-            check(L.lstk_cuda_mailbox_close(peer))
-        self._peers = []
-        dist.barrier(group=self.group)  # no rank still maps this rank's mailbox
-        check(L.lstk_cuda_mailbox_free(self._own))
-        self._own = None
+        if self._mb is not None:
+            self._mb.close()
+            self._mb = None
 
     def __call__(self, k_cache, v_cache, q, block_tables, chunk_lens, scale=None, max_seq_len=0):
         if self.exchange == "fused":

@@ -92,7 +92,7 @@ def kv_split_cpu(rank, world, port, result_dir):
 def kv_split_nccl(rank, world, port, result_dir):
     """The product's KvSplitDecode over NCCL: rank r's block table lists only its chunk's pages."""
     import localstack_b200 as L
-    from localstack_b200.shard import KvSplitDecode, chunk_keys, page_chunks
+    from localstack_b200.shard import KvSplitDecode, PeerBarrier, chunk_keys, page_chunks
 
     _join(rank, world, port, "nccl")
     res = {}
@@ -134,6 +134,14 @@ def kv_split_nccl(rank, world, port, result_dir):
                 res[f"split_{exchange}_graph"] = [within(dec.out.cpu().numpy(), ex), max_err(dec.out.cpu().numpy(), ex)]
                 del g
             dec.close()
+        # The device-side barrier of the ranks' streams that starts each timed split step.
+        pbar = PeerBarrier(dev)
+        for _ in range(5):
+            pbar()
+        torch.cuda.synchronize()
+        L.check_status()
+        pbar.close()
+        res["peer_barrier"] = [True, 0.0]
     finally:
         dist.destroy_process_group()
     with open(os.path.join(result_dir, f"rank{rank}.json"), "w") as f:

@@ -105,6 +105,23 @@ def test_single_sequence_combine(Hq, Hkv, ctx, n_ctas, pad_pages):
     assert np.allclose(lse.cpu().numpy(), lse_ex, atol=1e-3, rtol=1e-4)
 
 
+@pytest.mark.parametrize("Hq,Hkv,n_ctas", [(32, 4, 0), (16, 8, 0), (8, 1, 0), (32, 4, 300), (48, 12, 0)])
+def test_many_sequences_combine_by_rows(Hq, Hkv, n_ctas):
+    # A batch with more sequences than a few per CTA grid: the combine merges one row per warp
+    # (pieces of rows split across CTA boundaries, rows a single CTA finished, empty sequences).
+    rng = np.random.default_rng(Hq + Hkv + n_ctas)
+    lens = rng.integers(1, 3000, 40).tolist()
+    lens[3] = 0
+    lens[17] = 0
+    lens[20] = 20000
+    out, lse_gpu, ex, gg, lse = _decode(lens, Hq, Hkv, seed=Hq + Hkv + n_ctas, n_ctas=n_ctas, want_lse=True)
+    _assert_parity(out, ex, gg)
+    assert np.all(out[3] == 0) and np.all(out[17] == 0)
+    live = np.asarray(lens) > 0
+    assert np.all(np.isneginf(lse_gpu[~live]))
+    assert np.allclose(lse_gpu[live], lse[live], atol=1e-3, rtol=1e-4)
+
+
 def test_page_permutation_is_bit_invariant():
     # Same K/V content placed in differently permuted pages -> identical output bits.
     rng = np.random.default_rng(5)

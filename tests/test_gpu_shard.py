@@ -238,6 +238,7 @@ def test_kv_split_nccl_two_ranks(tmp_path):
                 os.environ[k] = v
     for r in range(2):
         res = json.load(open(os.path.join(tmp_path, f"rank{r}.json")))
-        for key in ("split_fused", "split_fused_graph", "split_p2p", "split_collective", "split_p2p_graph"):
+        for key in ("split_fused", "split_fused_graph", "split_p2p", "split_collective", "split_p2p_graph",
+                    "peer_barrier"):
             ok, err = res[key]
             assert ok, (r, key, err)
