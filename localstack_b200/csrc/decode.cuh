@@ -905,9 +905,7 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         if (tid < nd) p.out[row * kD + d0 + tid] = o;
         if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = lse;
     } else {
-        constexpr int kMaxRanks = kCombineThreads;
-        __shared__ float o_s[kD + 1];       // the local share, then its lse
-        __shared__ float lse_s[kMaxRanks];  // every rank's lse of the row
+        __shared__ float o_s[kD + 1];  // the local share, then its lse
         __shared__ int timed_out;
         const int R = p.n_ranks;
         const int64_t n_rows = (int64_t) p.n_seqs * p.n_head;
@@ -921,6 +919,7 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         if (tid == 0) o_s[nd] = lse, timed_out = 0;
         __syncthreads();
         const uint64_t tag = (uint64_t) epoch << 32;
+        const uint64_t t_start = global_timer_ns();  // the waits below are bounded from here
         const int per = nd + (first ? 1 : 0);  // words this CTA sends to each rank
         for (int i = tid; i < R * per; i += blockDim.x) {
             const int r = i / per, e = i - r * per;
@@ -929,43 +928,72 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
                           row * (kD + 1) + d;
             exchange::st_relaxed_sys_u64(w, tag | __float_as_uint(o_s[e]));
         }
-        // Poll the own mailbox: thread r < R the lse word of source r, thread t < nd the value
-        // words of dim d0 + t from every source (the lse values come through shared memory).
+        // Poll the own mailbox for every word of the share from every source at once: item i of a
+        // pass is source r0 + i / (nd + 1), dim d0 + i % (nd + 1) (the last word of a source is
+        // its lse), up to 4 items per thread, all loads issued before any is checked, so a share
+        // costs one memory round trip once the peers' words have landed. The values go through
+        // shared memory to thread t < nd, which merges dim d0 + t over the sources (passes of up
+        // to 1024 words, merged online, for many ranks).
         const uint64_t *base = reinterpret_cast<const uint64_t *>(own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
         volatile int *const abort = &timed_out;
-        auto await = [&](const uint64_t *w, float &v, int src) {
-            uint64_t x = exchange::ld_relaxed_sys_u64(w);
-            if ((uint32_t) (x >> 32) != epoch) {
-                const uint64_t t0 = global_timer_ns();
-                for (uint32_t i = 1;; i++) {
-                    x = exchange::ld_relaxed_sys_u64(w);
-                    if ((uint32_t) (x >> 32) == epoch) break;
-                    if ((i & 63u) == 0 && (global_timer_ns() - t0 > p.wait_ns || *abort)) {
-                        *abort = 1;
-                        report(p.status, kStatusTimeout, kSiteExchangeWait, src);
-                        v = 0.f;
-                        return;
-                    }
+        auto await = [&](const uint64_t *w, int src) -> float {
+            for (uint32_t i = 1;; i++) {
+                const uint64_t x = exchange::ld_relaxed_sys_u64(w);
+                if ((uint32_t) (x >> 32) == epoch) return __uint_as_float((uint32_t) x);
+                if ((i & 63u) == 0 && (global_timer_ns() - t_start > p.wait_ns || *abort)) {
+                    *abort = 1;
+                    report(p.status, kStatusTimeout, kSiteExchangeWait, src);
+                    return 0.f;
                 }
             }
-            v = __uint_as_float((uint32_t) x);
         };
-        if (tid < R) await(base + (int64_t) tid * slot + kD, lse_s[tid], tid);
-        __syncthreads();
+        constexpr int kWords = 1024;  // words per pass = 4 per thread
+        constexpr int kPer = kWords / kCombineThreads;
+        __shared__ float w_s[kWords];
+        const int wpr = nd + 1;     // words per source
+        const int rc = kWords / wpr;  // sources per pass: 7 (nd 128) to 31 (nd 32)
+        float M = -INFINITY, den = 0.f, acc = 0.f;  // thread t < nd: the running merge of its dim
+        for (int r0 = 0; r0 < R; r0 += rc) {
+            const int nr = min(rc, R - r0), items = nr * wpr;
+            uint64_t x[kPer];
+#pragma unroll
+            for (int k = 0; k < kPer; k++) {
+                const int i = tid + k * kCombineThreads;
+                if (i < items) {
+                    const int r = r0 + i / wpr, e = i % wpr;
+                    x[k] = exchange::ld_relaxed_sys_u64(base + (int64_t) r * slot + (e < nd ? d0 + e : kD));
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kPer; k++) {
+                const int i = tid + k * kCombineThreads;
+                if (i < items) {
+                    const int r = r0 + i / wpr, e = i % wpr;
+                    w_s[i] = (uint32_t) (x[k] >> 32) == epoch
+                                 ? __uint_as_float((uint32_t) x[k])
+                                 : await(base + (int64_t) r * slot + (e < nd ? d0 + e : kD), r);
+                }
+            }
+            __syncthreads();
+            if (tid < nd) {
+                float cm = M;
+                for (int j = 0; j < nr; j++) cm = fmaxf(cm, w_s[j * wpr + nd]);
+                if (cm != -INFINITY) {
+                    const float f = __expf(M - cm);
+                    den *= f;
+                    acc *= f;
+                    for (int j = 0; j < nr; j++) {
+                        const float wt = __expf(w_s[j * wpr + nd] - cm);
+                        den += wt;
+                        acc += wt * w_s[j * wpr + tid];
+                    }
+                    M = cm;
+                }
+            }
+            __syncthreads();  // w_s is refilled by the next pass
+        }
         if (tid < nd) {
             float v = 0.f, l = -INFINITY;
-            float M = -INFINITY;
-            for (int r = 0; r < R; r++) M = fmaxf(M, lse_s[r]);
-            float den = 0.f, acc = 0.f;
-            for (int r = 0; r < R; r++) {
-                float x;
-                await(base + (int64_t) r * slot + d0 + tid, x, r);
-                if (M != -INFINITY) {
-                    const float wt = __expf(lse_s[r] - M);
-                    den += wt;
-                    acc += wt * x;
-                }
-            }
             if (M != -INFINITY && !timed_out) {
                 v = acc / den;
                 l = M + __logf(den);
