@@ -897,126 +897,112 @@ __host__ __device__ inline bool combine_by_rows(int n_seqs, int n_hg, int grid) 
 // call by every CTA of the grid (see advance_epoch), so calls replay from a CUDA graph and the
 // CTAs of one row always agree on it; words alternate between two banks by epoch parity (a rank
 // is at most one call ahead of a peer: it needs the peer's row of the current call to finish it).
+// A combine CTA's exchange state, read at the kernel's start (off the critical path): its own
+// mailbox, its epoch for this call, and (in shared memory) every rank's mailbox address.
+struct ExchangeState {
+    uint8_t *own;
+    uint32_t epoch;
+    uint8_t *const *mb;  // shared memory [n_ranks]
+};
+
 template <bool kExchange>
-__device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, int d0, int nd, float o, float lse) {
+__device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, int d0, int nd, float o, float lse,
+                                           const ExchangeState &xs) {
     const int tid = threadIdx.x;
     const bool first = d0 == 0;
     if constexpr (!kExchange) {
         if (tid < nd) p.out[row * kD + d0 + tid] = o;
         if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = lse;
     } else {
-        __shared__ float o_s[kD + 1];  // the local share, then its lse
-        __shared__ int timed_out;
+        // Thread t < nd sends its dim's word to every peer and polls the same dim's word of every
+        // peer in its own mailbox (thread 0 also the lse words), then merges the R sources in rank
+        // order - the same order on every rank - online in chunks of 8 with all of a chunk's loads
+        // issued before any is checked: no shared memory and no block barrier, so a share costs
+        // one memory round trip once the peers' words have landed. On a timeout (a word still
+        // without this call's epoch after wait_ns) the thread reports it and writes zero.
+        if (tid >= nd) return;
         const int R = p.n_ranks;
         const int64_t n_rows = (int64_t) p.n_seqs * p.n_head;
-        uint8_t *own = p.mailboxes[p.rank];
-        const int cta = (blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z;
-        const uint32_t epoch = reinterpret_cast<const uint32_t *>(own)[cta] + 1u;
+        const uint32_t epoch = xs.epoch;
         const int bank = (int) (epoch & 1u);
         const size_t w_off = exchange::words_offset(R, n_rows);
         const int64_t slot = n_rows * (kD + 1);  // words per (bank, source)
-        if (tid < nd) o_s[tid] = o;
-        if (tid == 0) o_s[nd] = lse, timed_out = 0;
-        __syncthreads();
         const uint64_t tag = (uint64_t) epoch << 32;
         const uint64_t t_start = global_timer_ns();  // the waits below are bounded from here
-        const int per = nd + (first ? 1 : 0);  // words this CTA sends to each rank
-        for (int i = tid; i < R * per; i += blockDim.x) {
-            const int r = i / per, e = i - r * per;
-            const int d = e < nd ? d0 + e : kD;
-            uint64_t *w = reinterpret_cast<uint64_t *>(p.mailboxes[r] + w_off) + ((int64_t) bank * R + p.rank) * slot +
-                          row * (kD + 1) + d;
-            exchange::st_relaxed_sys_u64(w, tag | __float_as_uint(o_s[e]));
+        const int64_t w_row = ((int64_t) bank * R + p.rank) * slot + row * (kD + 1);
+        for (int r = 0; r < R; r++) {
+            if (r == p.rank) continue;
+            uint64_t *w = reinterpret_cast<uint64_t *>(xs.mb[r] + w_off) + w_row;
+            exchange::st_relaxed_sys_u64(w + d0 + tid, tag | __float_as_uint(o));
+            if (tid == 0 && first) exchange::st_relaxed_sys_u64(w + kD, tag | __float_as_uint(lse));
         }
-        // Poll the own mailbox for every word of the share from every source at once: item i of a
-        // pass is source r0 + i / (nd + 1), dim d0 + i % (nd + 1) (the last word of a source is
-        // its lse), up to 4 items per thread, all loads issued before any is checked, so a share
-        // costs one memory round trip once the peers' words have landed. The values go through
-        // shared memory to thread t < nd, which merges dim d0 + t over the sources (passes of up
-        // to 1024 words, merged online, for many ranks).
-        const uint64_t *base = reinterpret_cast<const uint64_t *>(own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
-        volatile int *const abort = &timed_out;
-        auto await = [&](const uint64_t *w, int src) -> float {
-            for (uint32_t i = 1;; i++) {
-                const uint64_t x = exchange::ld_relaxed_sys_u64(w);
-                if ((uint32_t) (x >> 32) == epoch) return __uint_as_float((uint32_t) x);
-                if ((i & 63u) == 0 && (global_timer_ns() - t_start > p.wait_ns || *abort)) {
-                    *abort = 1;
-                    report(p.status, kStatusTimeout, kSiteExchangeWait, src);
+        const uint64_t *base = reinterpret_cast<const uint64_t *>(xs.own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
+        bool timed_out = false;
+        auto value = [&](uint64_t x, const uint64_t *w, int src) -> float {
+            for (uint32_t i = 1; (uint32_t) (x >> 32) != epoch; i++) {
+                if ((i & 63u) == 0 && global_timer_ns() - t_start > p.wait_ns) {
+                    if (!timed_out) report(p.status, kStatusTimeout, kSiteExchangeWait, src);
+                    timed_out = true;
                     return 0.f;
                 }
+                x = exchange::ld_relaxed_sys_u64(w);
             }
+            return __uint_as_float((uint32_t) x);
         };
-        constexpr int kWords = 1024;  // words per pass = 4 per thread
-        constexpr int kPer = kWords / kCombineThreads;
-        __shared__ float w_s[kWords];
-        const int wpr = nd + 1;     // words per source
-        const int rc = kWords / wpr;  // sources per pass: 7 (nd 128) to 31 (nd 32)
-        float M = -INFINITY, den = 0.f, acc = 0.f;  // thread t < nd: the running merge of its dim
-        for (int r0 = 0; r0 < R; r0 += rc) {
-            const int nr = min(rc, R - r0), items = nr * wpr;
-            uint64_t x[kPer];
+        constexpr int kChunk = 8;
+        float M = -INFINITY, den = 0.f, acc = 0.f;
+        for (int r0 = 0; r0 < R; r0 += kChunk) {
+            uint64_t lw[kChunk], xw[kChunk];
 #pragma unroll
-            for (int k = 0; k < kPer; k++) {
-                const int i = tid + k * kCombineThreads;
-                if (i < items) {
-                    const int r = r0 + i / wpr, e = i % wpr;
-                    x[k] = exchange::ld_relaxed_sys_u64(base + (int64_t) r * slot + (e < nd ? d0 + e : kD));
+            for (int k = 0; k < kChunk; k++) {
+                const int r = r0 + k;
+                if (r < R && r != p.rank) {
+                    lw[k] = exchange::ld_relaxed_sys_u64(base + (int64_t) r * slot + kD);
+                    xw[k] = exchange::ld_relaxed_sys_u64(base + (int64_t) r * slot + d0 + tid);
                 }
             }
+            float lv[kChunk], xv[kChunk];
 #pragma unroll
-            for (int k = 0; k < kPer; k++) {
-                const int i = tid + k * kCombineThreads;
-                if (i < items) {
-                    const int r = r0 + i / wpr, e = i % wpr;
-                    w_s[i] = (uint32_t) (x[k] >> 32) == epoch
-                                 ? __uint_as_float((uint32_t) x[k])
-                                 : await(base + (int64_t) r * slot + (e < nd ? d0 + e : kD), r);
+            for (int k = 0; k < kChunk; k++) {
+                const int r = r0 + k;
+                lv[k] = -INFINITY, xv[k] = 0.f;
+                if (r == p.rank) {
+                    lv[k] = lse, xv[k] = o;
+                } else if (r < R) {
+                    lv[k] = value(lw[k], base + (int64_t) r * slot + kD, r);
+                    xv[k] = value(xw[k], base + (int64_t) r * slot + d0 + tid, r);
                 }
             }
-            __syncthreads();
-            if (tid < nd) {
-                float cm = M;
-                for (int j = 0; j < nr; j++) cm = fmaxf(cm, w_s[j * wpr + nd]);
-                if (cm != -INFINITY) {
-                    const float f = __expf(M - cm);
-                    den *= f;
-                    acc *= f;
-                    for (int j = 0; j < nr; j++) {
-                        const float wt = __expf(w_s[j * wpr + nd] - cm);
-                        den += wt;
-                        acc += wt * w_s[j * wpr + tid];
-                    }
-                    M = cm;
+            float cm = M;
+#pragma unroll
+            for (int k = 0; k < kChunk; k++) cm = fmaxf(cm, lv[k]);
+            if (cm != -INFINITY) {
+                const float f = __expf(M - cm);
+                den *= f;
+                acc *= f;
+#pragma unroll
+                for (int k = 0; k < kChunk; k++) {
+                    const float wt = __expf(lv[k] - cm);
+                    den += wt;
+                    acc += wt * xv[k];
                 }
+                M = cm;
             }
-            __syncthreads();  // w_s is refilled by the next pass
         }
-        if (tid < nd) {
-            float v = 0.f, l = -INFINITY;
-            if (M != -INFINITY && !timed_out) {
-                v = acc / den;
-                l = M + __logf(den);
-            }
-            p.out[row * kD + d0 + tid] = v;
-            if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = l;
-        }
-        __syncthreads();
-        if (timed_out && tid < nd) p.out[row * kD + d0 + tid] = 0.f;  // every thread's result is void
-        if (timed_out && tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = -INFINITY;
+        const bool ok = M != -INFINITY && !timed_out;
+        p.out[row * kD + d0 + tid] = ok ? acc / den : 0.f;
+        if (tid == 0 && first && p.lse_out != nullptr) p.lse_out[row] = ok ? M + __logf(den) : -INFINITY;
     }
 }
 
 // Every CTA of an exchanging combine grid, whatever it does, advances its epoch counter once per
 // call (after its last read of it), so CTAs that share a row in one call have the same history.
 template <bool kExchange>
-__device__ __forceinline__ void advance_epoch(const CombineParams &p) {
+__device__ __forceinline__ void advance_epoch(const CombineParams &p, const ExchangeState &xs) {
     if constexpr (kExchange) {
-        if (threadIdx.x == 0) {
-            uint32_t *ctr = reinterpret_cast<uint32_t *>(p.mailboxes[p.rank]) +
-                            (blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z;
-            *ctr = *ctr + 1u;
-        }
+        if (threadIdx.x == 0)
+            reinterpret_cast<uint32_t *>(xs.own)[(blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z] =
+                xs.epoch;
     }
 }
 
@@ -1043,7 +1029,7 @@ __device__ __forceinline__ void merge_state(float &m, float &den, float4 &acc, f
 // memory. Piece i is split CTA c0 + i; its record is slot 0 of that CTA's pair, except for the
 // first piece when the CTA's range began in an earlier segment (slot 1).
 template <bool kExchange>
-__global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_kernel(const CombineParams p) {
+__global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(const CombineParams p) {
     pdl_wait();  // the split grid's partials and prefix are complete and visible
     const int S = p.dsplit;
     const int b = blockIdx.x, hg = blockIdx.y;
@@ -1051,11 +1037,20 @@ __global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_kernel(cons
     const int w = zr / kMaxGroup, n = zr % kMaxGroup;
     const int kvh = hg * kHeadsPerGroup + w;
     const int nd = kD / S, d0 = q * nd;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ uint8_t *mb_s[kExchange ? kCombineThreads : 1];
+    ExchangeState xs{nullptr, 0u, mb_s};
+    if constexpr (kExchange) {
+        xs.own = p.mailboxes[p.rank];
+        xs.epoch = reinterpret_cast<const uint32_t *>(xs.own)[(blockIdx.x * gridDim.y + blockIdx.y) * gridDim.z +
+                                                              blockIdx.z] + 1u;
+        if (tid < p.n_ranks) mb_s[tid] = p.mailboxes[tid];  // published by the plan's barrier below
+    }
     if (kvh >= p.n_head_kv || n >= p.group) {
-        advance_epoch<kExchange>(p);
+        __syncthreads();  // every thread has read the epoch counter before it is advanced
+        advance_epoch<kExchange>(p, xs);
         return;
     }
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t out_row = (int64_t) b * p.n_head + (int64_t) kvh * p.group + n;
     const int part_row = w * kMaxGroup + n;
     const int lp = nd / 4;  // lanes per piece
@@ -1138,19 +1133,11 @@ __global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_kernel(cons
         plan_P = P;
     }
     __syncthreads();
+    // Every path below ends in the one call of finish_row (one copy of its code: after a cold
+    // start each new stretch of code is fetched from memory).
     const int mode = plan_s[0];
-    if (mode == 0) {
-        accumulate();
-    } else if (mode == 1) {
-        finish_row<kExchange>(p, out_row, d0, nd, 0.f, -INFINITY);
-        advance_epoch<kExchange>(p);
-        return;
-    } else if (mode == 2) {  // the split kernel wrote this row directly (with an exchange, its local row)
-        if constexpr (kExchange)
-            finish_row<true>(p, out_row, d0, nd, tid < nd ? p.out[out_row * kD + d0 + tid] : 0.f, p.lse_out[out_row]);
-        advance_epoch<kExchange>(p);
-        return;
-    } else {
+    if (mode == 2 && !kExchange) return;  // the split kernel wrote this row directly
+    if (mode == 3) {
         const int c0 = plan_s[1], n_pc = plan_s[2], first_slot = plan_s[3];
         const int64_t P = plan_P;
         const bool may_be_empty = P < p.grid;  // only then can a split CTA's range be empty
@@ -1158,36 +1145,45 @@ __global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_kernel(cons
             load(i0, c0, n_pc, first_slot, may_be_empty, P);
             accumulate();
         }
+    } else if (mode == 0) {
+        accumulate();
     }
-    // Lane groups of a warp hold the same dims: merge them (offsets lp, 2 lp, ...).
-    for (int off = lp; off < 32; off <<= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-        const float den2 = __shfl_xor_sync(0xffffffffu, den, off);
-        float4 a2;
-        a2.x = __shfl_xor_sync(0xffffffffu, acc.x, off);
-        a2.y = __shfl_xor_sync(0xffffffffu, acc.y, off);
-        a2.z = __shfl_xor_sync(0xffffffffu, acc.z, off);
-        a2.w = __shfl_xor_sync(0xffffffffu, acc.w, off);
-        merge_state(m, den, acc, m2, den2, a2);
-    }
-    __shared__ float m_s[kCombineWarps], den_s[kCombineWarps];
-    __shared__ __align__(16) float acc_s[kCombineWarps][kD];  // written as float4
-    if (lane < lp) reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
-    if (lane == 0) m_s[warp] = m, den_s[warp] = den;
-    __syncthreads();
-    float M = -INFINITY;
-    for (int k = 0; k < kCombineWarps; k++) M = fmaxf(M, m_s[k]);
-    float o = 0.f, total = 0.f;
-    if (M != -INFINITY && tid < nd) {
-        for (int k = 0; k < kCombineWarps; k++) {
-            const float f = exp2f(m_s[k] - M);
-            total += den_s[k] * f;
-            o += acc_s[k][tid] * f;
+    float o = 0.f, row_lse = -INFINITY;
+    if (mode == 2) {  // with an exchange: the local row the split kernel wrote
+        if (tid < nd) o = p.out[out_row * kD + d0 + tid];
+        row_lse = p.lse_out[out_row];
+    } else if (mode != 1) {
+        // Lane groups of a warp hold the same dims: merge them (offsets lp, 2 lp, ...).
+        for (int off = lp; off < 32; off <<= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+            const float den2 = __shfl_xor_sync(0xffffffffu, den, off);
+            float4 a2;
+            a2.x = __shfl_xor_sync(0xffffffffu, acc.x, off);
+            a2.y = __shfl_xor_sync(0xffffffffu, acc.y, off);
+            a2.z = __shfl_xor_sync(0xffffffffu, acc.z, off);
+            a2.w = __shfl_xor_sync(0xffffffffu, acc.w, off);
+            merge_state(m, den, acc, m2, den2, a2);
         }
+        __shared__ float m_s[kCombineWarps], den_s[kCombineWarps];
+        __shared__ __align__(16) float acc_s[kCombineWarps][kD];  // written as float4
+        if (lane < lp) reinterpret_cast<float4 *>(acc_s[warp])[lane] = acc;
+        if (lane == 0) m_s[warp] = m, den_s[warp] = den;
+        __syncthreads();
+        float M = -INFINITY;
+        for (int k = 0; k < kCombineWarps; k++) M = fmaxf(M, m_s[k]);
+        float total = 0.f;  // on every thread: the exchange needs the row's lse in all of them
+        if (M != -INFINITY) {
+            for (int k = 0; k < kCombineWarps; k++) {
+                const float f = exp2f(m_s[k] - M);
+                total += den_s[k] * f;
+                if (tid < nd) o += acc_s[k][tid] * f;
+            }
+        }
+        o = total > 0.f ? o / total : 0.f;
+        row_lse = total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY;
     }
-    finish_row<kExchange>(p, out_row, d0, nd, total > 0.f ? o / total : 0.f,
-                          total > 0.f ? (M + __log2f(total)) * 0.69314718055994531f : -INFINITY);
-    advance_epoch<kExchange>(p);
+    finish_row<kExchange>(p, out_row, d0, nd, o, row_lse, xs);
+    advance_epoch<kExchange>(p, xs);
 }
 
 // The combine for a batch of short rows (no exchange): grid (sequence b, head group hg, KV head
