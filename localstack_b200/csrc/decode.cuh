@@ -865,23 +865,27 @@ struct CombineParams {
     DeviceStatus *status;
 };
 
-// CTAs per output row of the combine: enough that a row split over many pieces (one long
-// sequence over the whole grid: up to 148 pieces of 512 bytes) is read by several SMs, while a
-// batch of short rows keeps one CTA per row. Fused exchange: every combine CTA owns an epoch
-// counter in the mailbox header, so the grid must fit it.
-__host__ __device__ inline int combine_dsplit(int n_seqs, int n_hg, int grid, bool exchange, int max_ctas) {
+// CTAs per output row of decode_combine_kernel (1, 2 or 4): rows over many pieces (8 or more per
+// segment) are split while the grid stays within one CTA per SM - one long sequence (32 rows)
+// goes over 128 CTAs, each reading a quarter of every piece - and no further, since a CTA's fixed
+// cost (launch, plan, barriers) is paid once per CTA. Fused exchange: every combine CTA owns an
+// epoch counter in the mailbox header, so the grid must fit it.
+__host__ __device__ inline int combine_dsplit(int n_seqs, int n_hg, int grid, bool exchange, int max_ctas, int n_sms) {
     const int64_t segs = (int64_t) n_seqs * n_hg;
     const int64_t per = segs > 0 ? grid / segs : 0;  // pieces per segment, about
-    int d = per >= 32 ? 4 : per >= 8 ? 2 : 1;
+    int d = 1;
+    if (per >= 8)
+        while (d < 4 && segs * kPartRows * d * 2 <= n_sms) d *= 2;
     while (exchange && d > 1 && segs * kPartRows * d > max_ctas) d >>= 1;
     return d;
 }
 
-// Batches whose segments average fewer than 8 pieces (more sequences than a few per grid) merge
-// a row per warp (decode_combine_rows_kernel); longer rows spread over CTAs.
+// Batches whose segments average fewer than 16 pieces (more than a few sequences per grid) merge
+// a row per warp (decode_combine_rows_kernel: one round trip for up to 16 pieces); longer rows
+// spread over CTAs.
 __host__ __device__ inline bool combine_by_rows(int n_seqs, int n_hg, int grid) {
     const int64_t segs = (int64_t) n_seqs * n_hg;
-    return segs > 0 && grid / segs < 8;
+    return segs > 0 && grid / segs < 16;
 }
 
 // The end of a combine CTA's share of a row: dims [d0, d0 + nd), thread t < nd holding dim
@@ -1188,11 +1192,11 @@ __global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_kernel(cons
 
 // The combine for a batch of short rows (no exchange): grid (sequence b, head group hg, KV head
 // w of the group), warp n merging query row n's pieces on its own - lane l the float4 of dims
-// 4l .. 4l + 3 of each piece, kBatch pieces in flight, an online (max, sum, accumulator) state -
+// 4l .. 4l + 3 of each piece, 16 pieces in flight, an online (max, sum, accumulator) state -
 // and writing the row, so nothing crosses warps after the segment's plan, which thread 0 works
 // out once for the CTA's eight rows. Chosen where segments have few pieces (many sequences per
 // grid); a long row over many pieces takes decode_combine_kernel, which spreads it over CTAs.
-__global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_rows_kernel(const CombineParams p) {
+__global__ void __launch_bounds__(kCombineThreads, 2) decode_combine_rows_kernel(const CombineParams p) {
     pdl_wait();  // the split grid's partials and prefix are complete and visible
     const int b = blockIdx.x, hg = blockIdx.y, w = blockIdx.z;
     const int kvh = hg * kHeadsPerGroup + w;
@@ -1230,7 +1234,7 @@ __global__ void __launch_bounds__(kCombineThreads, 3) decode_combine_rows_kernel
     const int64_t P = plan_P;
     const bool may_be_empty = P < p.grid;
     const int part_row = w * kMaxGroup + n;
-    constexpr int kBatch = 8;
+    constexpr int kBatch = 16;
     float m = -INFINITY, den = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = 0; i0 < n_pc; i0 += kBatch) {

@@ -443,7 +443,7 @@ struct ExchangeSpec {
 // kdmap / vdmap: the scale-plane maps of a q8_0 cache (q8 true), else ignored.
 static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &kdmap,
                          const CUtensorMap &vdmap, bool q8, const decode::Params &p, int grid, size_t smem,
-                         cudaStream_t s, const ExchangeSpec *ex = nullptr) {
+                         int n_sms, cudaStream_t s, const ExchangeSpec *ex = nullptr) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -478,7 +478,7 @@ static int launch_decode(const CUtensorMap &kmap, const CUtensorMap &vmap, const
     c.n_ranks = ex ? ex->n_ranks : 1;
     c.wait_ns = ex ? ex->wait_ns : 0;
     c.status = p.status;
-    c.dsplit = decode::combine_dsplit(p.n_seqs, p.n_hg, grid, ex != nullptr, exchange::kMaxCtas);
+    c.dsplit = decode::combine_dsplit(p.n_seqs, p.n_hg, grid, ex != nullptr, exchange::kMaxCtas, n_sms);
     cfg.blockDim = dim3(decode::kCombineThreads);
     cfg.dynamicSmemBytes = 0;
     if (!ex && decode::combine_by_rows(p.n_seqs, p.n_hg, grid)) {
@@ -599,7 +599,7 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
                                  "cudaFuncSetAttribute(decode)"))) {
         return rc;
     }
-    return launch_decode(kmap, vmap, kdmap, vdmap, q8 != nullptr, p, (int) grid, smem,
+    return launch_decode(kmap, vmap, kdmap, vdmap, q8 != nullptr, p, (int) grid, smem, dev->n_sms,
                          static_cast<cudaStream_t>(stream), ex);
 }
 
@@ -1284,7 +1284,8 @@ int lstk_cuda_attn_decode_static(const lstk_kv_layout *layout, const void *k_cac
     const size_t smem = decode::split_smem_bytes<false>(n_seqs);
     if ((rc = ensure_smem(&dev->decode_smem, decode::decode_split_kernel<false>, smem, "cudaFuncSetAttribute(decode)")))
         return rc;
-    return launch_decode(kmap, vmap, kmap, vmap, false, p, (int) grid, smem, static_cast<cudaStream_t>(stream));
+    return launch_decode(kmap, vmap, kmap, vmap, false, p, (int) grid, smem, dev->n_sms,
+                         static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
