@@ -901,6 +901,22 @@ __host__ __device__ inline bool combine_by_rows(int n_seqs, int n_hg, int grid) 
 // call by every CTA of the grid (see advance_epoch), so calls replay from a CUDA graph and the
 // CTAs of one row always agree on it; words alternate between two banks by epoch parity (a rank
 // is at most one call ahead of a peer: it needs the peer's row of the current call to finish it).
+// The slow path of a poll: spins on word w until it carries `epoch` (bounded: after wait_ns from
+// t_start it reports the timeout once and returns 0). Out of line, so the inlined fast path (the
+// word had already landed) stays small: after a launch every stretch of code is fetched anew.
+__device__ __noinline__ float exchange_spin(const uint64_t *w, uint32_t epoch, uint64_t t_start, uint64_t wait_ns,
+                                            DeviceStatus *status, int src, bool &timed_out) {
+    for (uint32_t i = 1;; i++) {
+        const uint64_t x = exchange::ld_relaxed_sys_u64(w);
+        if ((uint32_t) (x >> 32) == epoch) return __uint_as_float((uint32_t) x);
+        if ((i & 63u) == 0 && global_timer_ns() - t_start > wait_ns) {
+            if (!timed_out) report(status, kStatusTimeout, kSiteExchangeWait, src);
+            timed_out = true;
+            return 0.f;
+        }
+    }
+}
+
 // A combine CTA's exchange state, read at the kernel's start (off the critical path): its own
 // mailbox, its epoch for this call, and (in shared memory) every rank's mailbox address.
 struct ExchangeState {
@@ -943,15 +959,8 @@ __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, 
         const uint64_t *base = reinterpret_cast<const uint64_t *>(xs.own + w_off) + (int64_t) bank * R * slot + row * (kD + 1);
         bool timed_out = false;
         auto value = [&](uint64_t x, const uint64_t *w, int src) -> float {
-            for (uint32_t i = 1; (uint32_t) (x >> 32) != epoch; i++) {
-                if ((i & 63u) == 0 && global_timer_ns() - t_start > p.wait_ns) {
-                    if (!timed_out) report(p.status, kStatusTimeout, kSiteExchangeWait, src);
-                    timed_out = true;
-                    return 0.f;
-                }
-                x = exchange::ld_relaxed_sys_u64(w);
-            }
-            return __uint_as_float((uint32_t) x);
+            if ((uint32_t) (x >> 32) == epoch) return __uint_as_float((uint32_t) x);
+            return exchange_spin(w, epoch, t_start, p.wait_ns, p.status, src, timed_out);
         };
         constexpr int kChunk = 8;
         float M = -INFINITY, den = 0.f, acc = 0.f;
