@@ -536,7 +536,11 @@ def run_b200(args):
                            float(loads.max() / loads.mean()), 4),
                        "l2": "KV inputs 2.2 GB in total > 126 MB L2, no flush"},
             "tokens_per_s": round(len(ctx_all) / (ms_max / 1e3), 1),
-            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel + decode_combine_kernel",
+            # the merge kernel the library picks for this rank's batch: a row per warp while the
+            # sequences average fewer than 16 pieces of the 148-CTA grid, else rows over CTAs
+            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel + " + (
+                             "decode_combine_rows_kernel" if torch.cuda.get_device_properties(dev).multi_processor_count
+                             // max(1, len(w["ctx"]) * ((HKV + 3) // 4)) < 16 else "decode_combine_kernel"),
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} hbm_gbs",
                          "algorithmic_bytes_per_launch": read_bytes, "launch_ms": round(dec_ms, 4),
