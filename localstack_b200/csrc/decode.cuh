@@ -888,19 +888,6 @@ __host__ __device__ inline bool combine_by_rows(int n_seqs, int n_hg, int grid) 
     return segs > 0 && grid / segs < 16;
 }
 
-// The end of a combine CTA's share of a row: dims [d0, d0 + nd), thread t < nd holding dim
-// d0 + t in o, and the row's lse (natural log; every CTA of the row has the same). Without an
-// exchange, out (and, from the row's first CTA, lse_out) get the local values. With one, the
-// share goes to every rank (exchange.cuh's mailboxes) and out / lse_out get the log-sum-exp merge
-// of the R ranks' rows. A row travels as 129 words of 8 bytes - a value's f32 bits and the call's
-// epoch - stored straight into slot `rank` of every rank's mailbox (plain peer stores; the lse
-// word by the row's first CTA); a reader polls the words of its own mailbox until each carries
-// the epoch, and an 8-byte word is written and read whole, so no flag and no system-scope fence
-// is needed. Waits are bounded by wait_ns (on timeout the status records it and the share is
-// zeros). The epoch is the mailbox header counter of the CTA's linear index, advanced once per
-// call by every CTA of the grid (see advance_epoch), so calls replay from a CUDA graph and the
-// CTAs of one row always agree on it; words alternate between two banks by epoch parity (a rank
-// is at most one call ahead of a peer: it needs the peer's row of the current call to finish it).
 // The slow path of a poll: spins on word w until it carries `epoch` (bounded: after wait_ns from
 // t_start it reports the timeout once and returns 0). Out of line, so the inlined fast path (the
 // word had already landed) stays small: after a launch every stretch of code is fetched anew.
@@ -925,6 +912,19 @@ struct ExchangeState {
     uint8_t *const *mb;  // shared memory [n_ranks]
 };
 
+// The end of a combine CTA's share of a row: dims [d0, d0 + nd), thread t < nd holding dim
+// d0 + t in o, and the row's lse (natural log; every CTA of the row has the same). Without an
+// exchange, out (and, from the row's first CTA, lse_out) get the local values. With one, the
+// share goes to every peer (exchange.cuh's mailboxes) and out / lse_out get the log-sum-exp merge
+// of the R ranks' rows. A share travels as words of 8 bytes - a value's f32 bits and the call's
+// epoch - stored straight into slot `rank` of every peer's mailbox (plain peer stores; the lse
+// word by the row's first CTA); a reader polls the words of its own mailbox until each carries
+// the epoch, and an 8-byte word is written and read whole, so no flag and no system-scope fence
+// is needed. Waits are bounded by wait_ns (on timeout the status records it and the share is
+// zeros). The epoch is the mailbox header counter of the CTA's linear index, advanced once per
+// call by every CTA of the grid (see advance_epoch), so calls replay from a CUDA graph and the
+// CTAs of one row always agree on it; words alternate between two banks by epoch parity (a rank
+// is at most one call ahead of a peer: it needs the peer's row of the current call to finish it).
 template <bool kExchange>
 __device__ __forceinline__ void finish_row(const CombineParams &p, int64_t row, int d0, int nd, float o, float lse,
                                            const ExchangeState &xs) {
