@@ -900,13 +900,17 @@ def config4_split(L, dev, world):
     for the peers' words and merges; the headline), "p2p" (the same exchange in a kernel of its
     own after the decode) and "collective" (NCCL all-gather of [O | lse] records + merge kernel),
     and the rank's decode alone. One step is captured in a CUDA graph and timed with CUDA events,
-    max over ranks of the mean per-step time, every step started on all ranks together (a
-    device-side barrier of the ranks' streams over peer memory). Two cache conditions:
-      * "ms" (warm code, cold KV - a serving loop, where the layer's KV was evicted by the other
-        layers' since its last decode but the kernels' code and the small control data stay in
-        L2): the chunk's K/V is held in enough copies (same content) that the copies together
-        exceed twice the 126 MB L2, and step i reads copy i mod n;
-      * "ms_cold": L2 flushed by reading 256 MB before each step (code, tables and KV all cold).
+    max over ranks of the mean per-step time, every timed replay started on all ranks together
+    (a device-side barrier of the ranks' streams over peer memory). The chunk's K/V is held in
+    enough copies (same content) that the copies together exceed twice the 126 MB L2, and step i
+    reads copy i mod n, so the KV is cold while the kernels' code and the small control data stay
+    warm, as in a serving loop whose other layers evict this layer's KV between its decodes:
+      * "ms": a CUDA graph of 10 consecutive steps (the way config 4 is timed on one GPU:
+        back-to-back decodes in one graph), event time / 10 - the steps pace each other through
+        the exchange itself;
+      * "ms_single": one step per graph replay, CUDA events around it (adds the replay's
+        launch-to-event floor, a few us);
+      * "ms_cold": one step per replay after reading 256 MB (code, tables and KV all cold).
     After the timed replays every rank's merged output is checked against a one-GPU decode of the
     whole context (rank 0 rebuilds every chunk from its seed)."""
     import torch
@@ -946,9 +950,10 @@ def config4_split(L, dev, world):
     flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
     pbar = PeerBarrier(dev)
     res = {"n_gpus": world, "pages_per_rank": n_local, "kv_copies": n_copies,
-           "l2": f"ms: warm code, cold KV ({n_copies} copies of the chunk read in turn, > 2x L2); "
+           "l2": f"ms, ms_single: warm code, cold KV ({n_copies} copies of the chunk read in turn, > 2x L2); "
                  "ms_cold: 256 MB read before each step",
-           "timing": "CUDA graph of one step, CUDA events, max over ranks of the mean",
+           "timing": "ms: CUDA graph of 10 consecutive steps / 10 (as config 4 on one GPU); ms_single, ms_cold: "
+                     "one step per graph replay; CUDA events, max over ranks of the mean",
            "start": "device barrier of the ranks' streams (one exchange over peer memory) before each step",
            "check": "every rank's merged output after the timed replays vs a one-GPU decode of the whole context "
                     "(|d| <= 2e-3 + 1e-2 |ref|), max over ranks"}
@@ -973,9 +978,14 @@ def config4_split(L, dev, world):
             with torch.cuda.graph(g):
                 step(kc_i, vc_i)
             graphs.append(g)
+        per_graph = 10
+        g10 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g10):
+            for i in range(per_graph):
+                step(*copies[i % len(copies)])
         entry = {}
-        for cond in ("warm", "cold"):
-            reps = 30
+        for cond in ("b2b", "single", "cold"):
+            reps = 10 if cond == "b2b" else 30
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
             dist.barrier()
             torch.cuda.synchronize()
@@ -986,14 +996,14 @@ def config4_split(L, dev, world):
                     torch.cuda._sleep(40000)  # the GPU waits while every host queues the step behind it
                 pbar()
                 a.record()
-                graphs[i % len(graphs)].replay()
+                (g10 if cond == "b2b" else graphs[i % len(graphs)]).replay()
                 b.record()
             torch.cuda.synchronize()
-            ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+            ms = sum(a.elapsed_time(b) for a, b in evs) / reps / (per_graph if cond == "b2b" else 1)
             t = torch.tensor([ms], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            entry["ms" if cond == "warm" else "ms_cold"] = round(float(t[0]), 4)
-        del graphs
+            entry[{"b2b": "ms", "single": "ms_single", "cold": "ms_cold"}[cond]] = round(float(t[0]), 4)
+        del graphs, g10
         L.check_status()
         entry["gbs"] = round(ctx * HKV * D * 4 / (entry["ms"] / 1e3) / 1e9, 1)
         if exchange != "decode_only":
@@ -1007,7 +1017,8 @@ def config4_split(L, dev, world):
         dec.close()
         res[exchange] = entry
     pbar.close()
-    res["ms"], res["ms_cold"], res["gbs"] = res["fused"]["ms"], res["fused"]["ms_cold"], res["fused"]["gbs"]
+    res["ms"], res["ms_single"], res["ms_cold"] = res["fused"]["ms"], res["fused"]["ms_single"], res["fused"]["ms_cold"]
+    res["gbs"] = res["fused"]["gbs"]
     res["outputs_match"] = ok_all
     if not ok_all and rank == 0:
         print("config4_split: merged output outside the tolerance of the one-GPU decode", file=sys.stderr)
