@@ -271,14 +271,16 @@ constexpr int kQ8VdOff = kQ8KdOff + kPage * 32;          // scale rows of up to 
 
 // Split-kernel shapes. f16: 4 consumer warps (one per KV head of the group, both 16-token slabs of
 // a page), 3 stages of 64 KiB. q8_0: a page costs half the bytes and more instructions per byte,
-// so 8 consumer warps - warp w takes KV head w % 4 and slab w / 4 of every page - and 4 stages of
-// 35 KiB; the two warps of a head merge their softmax states through shared memory at the end of
-// each piece (kMergeBytes: per head, 32 lanes x (2 maxima, 2 sums, 32 accumulators)).
+// so 8 consumer warps - warp w takes KV head w % 4 and slab w / 4 of every page - and 2 stages of
+// 35 KiB, with two CTAs per SM (the launch doubles the grid) so that 16 consumer warps per SM hide
+// a slab's chain of dependent steps (one CTA of four stages streamed at ~0.73 of HBM, two CTAs of
+// two stages at ~0.88); the two warps of a head merge their softmax states through shared memory
+// at the end of each piece (kMergeBytes: per head, 32 lanes x (2 maxima, 2 sums, 32 accumulators)).
 template <bool kQ8>
 struct SplitCfg {
     static constexpr int kConsumers = kQ8 ? 8 : kConsumerWarps;
     static constexpr int kThreads = (kConsumers + 1) * 32;
-    static constexpr int kStages = kQ8 ? 4 : decode::kStages;
+    static constexpr int kStages = kQ8 ? 2 : decode::kStages;
     static constexpr int kStageBytes = kQ8 ? 35 * 1024 : decode::kStageBytes;
     static constexpr int kMergeBytes = kQ8 ? kHeadsPerGroup * 32 * 36 * 4 : 0;
     static constexpr int kBarriers = 2 * kStages + (kQ8 ? 2 * kHeadsPerGroup : 0);
@@ -493,7 +495,7 @@ extern __shared__ __align__(1024) uint8_t dyn_smem[];
 // kQ8: the cache is q8_0 planes (kmap / vmap over the qs planes, kdmap / vdmap over the scale
 // planes); else f16 rows (kmap / vmap; the scale maps are unused).
 template <bool kQ8>
-__global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(SplitCfg<kQ8>::kThreads, kQ8 ? 2 : 1) decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
                                                                     const __grid_constant__ CUtensorMap kdmap,
                                                                     const __grid_constant__ CUtensorMap vdmap,

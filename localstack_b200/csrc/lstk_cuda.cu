@@ -561,7 +561,9 @@ static int decode_range(const lstk_kv_layout *layout, const void *k_cache, const
 
     const int n_hg = (hkv + decode::kHeadsPerGroup - 1) / decode::kHeadsPerGroup;
     const int64_t max_groups = (int64_t) n_seqs * n_hg * ((max_seq_len + decode::kPage - 1) / decode::kPage);
-    int64_t grid = n_ctas > 0 ? n_ctas : dev->n_sms;
+    // q8_0: two CTAs per SM (a slab's dependent chain of int8 MMAs, scales and conversions needs
+    // more warps per SM than the f16 kernel to keep HBM busy)
+    int64_t grid = n_ctas > 0 ? n_ctas : (q8 ? 2 : 1) * dev->n_sms;
     grid = std::max<int64_t>(1, std::min<int64_t>({grid, max_groups, (int64_t) decode::kMaxCtas}));
 
     uint8_t *ws = static_cast<uint8_t *>(workspace);
