@@ -10,8 +10,9 @@ attention node shards in two ways, both built here on the single-GPU C ABI:
   rank r. Each rank decodes its chunk with lse_out, then the partials are exchanged and merged
   by log-sum-exp, so the merged output is replicated on every rank. Three exchanges:
   - "fused": lstk_cuda_attn_decode_exchange - the decode's own combine kernel stores each row it
-    finishes straight into every rank's mailbox over NVLink (CUDA IPC mappings set up once
-    through the process group), waits on the row's flags and merges: no launch after the decode;
+    finishes straight into every peer's mailbox over NVLink (CUDA IPC mappings set up once
+    through the process group) as value+epoch words, waits until the peers' words of the row
+    carry the call's epoch and merges: no launch after the decode;
   - "p2p": the same protocol in a kernel of its own (lstk_cuda_attn_exchange_merge) after the
     decode;
   - "collective": one record [O (rows x D) | lse (rows)] per rank, all-gathered through the
